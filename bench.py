@@ -1,0 +1,458 @@
+"""Benchmark: TurboQuant decode attention + append on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one "step"): one decode step of Mixtral-8x7B attention over a
+packed TurboQuant KV cache — for each of 32 layers, append the new token's
+K/V (B x Hkv vectors: norm, rotate, quantise, pack, QJL sketch) and run GQA
+decode attention (Hq 32, Hkv 8, D 128) over 8192 cached tokens + the new one,
+K 4-bit + 1-bit QJL residual, V 2-bit, bf16 in/out.  Synthetic seeded data:
+K/V ~ N(0,1) with 1% of channels (2 of 128, fixed per head) scaled x8.
+
+Multi-GPU (torchrun, one rank per GPU): KV heads are sharded over N ranks
+(8/N heads per rank) and the global batch is 16*N sequences, so every rank
+holds the same 128 (sequence, kv-head) streams as the 1-GPU run (weak
+scaling); each layer ends with an NCCL all-gather of the attention outputs.
+
+The JSON line's `value` is decode tokens/s over all ranks (global batch /
+step time, max over ranks), timed on the device with CUDA events around K
+CUDA-graph replays of the step.  Packed KV per step is 3.96 GB per rank,
+far above L2 (126 MB), so no L2 flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS, HQ, HKV, D, T_CTX, B_PER_GPU = 32, 32, 8, 128, 8192, 16
+KEY_BITS, VALUE_BITS, QJL = 4, 2, True
+APPEND_CFG = dict(layers=48, B=8, H=8, T=4096, D=128, bits=4)
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _traffic_per_launch():
+    """dram bytes per decode launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "decode_kernel_mixtral_b16_t8192.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(float(line.split(":")[1]))
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        loaded = [s for s in sm if s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path on the host cores (rank 0)."""
+    if rank != 0:
+        return
+    import torch
+    from oracle import cpu_baseline as C
+    B = B_PER_GPU * world
+    kc, kb = C.codebook(D, KEY_BITS)
+    vc, vb = C.codebook(D, VALUE_BITS)
+    layer = C.RefLayer(B, HKV, D, T_CTX, KEY_BITS, VALUE_BITS, kc, kb, vc, vb)
+    g = torch.Generator(device="cpu")
+    g.manual_seed(0)
+    q = torch.randn(B, HQ, 1, D, generator=g).to(torch.bfloat16)
+    kv = [(torch.randn(B, HKV, 1, D, generator=g).to(torch.bfloat16),
+           torch.randn(B, HKV, 1, D, generator=g).to(torch.bfloat16)) for _ in range(4)]
+    for i in range(args.warmup):
+        layer.decode_step(*kv[i % 4], q)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        layer.decode_step(*kv[i % 4], q)
+    per_layer = (time.perf_counter() - t0) / args.steps
+    step_s = per_layer * LAYERS
+    value = B / step_s
+    line = {
+        "impl": "reference", "metric": "decode-attn tokens/s", "value": value,
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": _config(world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": C.host_threads(),
+                         "kind": "port",
+                         "sample": f"1 of {LAYERS} layers per step timed, x{LAYERS}; "
+                                   f"reference update()+SDPA, B{B} Hkv{HKV} T{T_CTX}, "
+                                   "no QJL (the reference has none)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _config(world):
+    return {"workload": f"Mixtral-8x7B attention decode step: {LAYERS} layers x (append 1 "
+                        f"token + GQA decode), Hq{HQ}/Hkv{HKV}, D{D}, context {T_CTX}, "
+                        f"K{KEY_BITS}+QJL/V{VALUE_BITS}",
+            "global_batch": B_PER_GPU * world, "seq_len": T_CTX, "layers": LAYERS,
+            "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "key_bits": KEY_BITS,
+            "value_bits": VALUE_BITS, "qjl": QJL,
+            "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+            "l2": "no flush: 3.96 GB packed KV per step per GPU > 126 MB L2"}
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from bhaskera_col_b200 import _lib
+    from bhaskera_col_b200.inference import TurboQuantKVCache, ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    hkv = HKV // world
+    hq = HQ // world
+    B = B_PER_GPU * world
+    S = B * hkv
+    bpt = ops.page_bytes(D, KEY_BITS, VALUE_BITS, QJL) // 64
+
+    # ---- cache: 32 layers, filled with T_CTX synthetic tokens -------------
+    cache = TurboQuantKVCache(num_layers=LAYERS, batch_size=B, num_heads=hkv, head_dim=D,
+                              key_bits=KEY_BITS, value_bits=VALUE_BITS, residual_window=0,
+                              protected_layers=0, dtype=torch.bfloat16, device=dev,
+                              max_seq_len=T_CTX + 64 + args.steps + args.warmup, qjl=QJL)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    out_ch = torch.randperm(D, generator=torch.Generator().manual_seed(7))[:2].to(dev)
+    scale = torch.ones(D, device=dev)
+    scale[out_ch] = 8.0
+
+    def synth(shape):
+        return (torch.randn(shape, device=dev, generator=gen) * scale).to(torch.bfloat16)
+
+    CH = 2048
+    for layer in range(LAYERS):
+        for c0 in range(0, T_CTX, CH):
+            cache.append(synth((B, hkv, CH, D)), synth((B, hkv, CH, D)), layer)
+    torch.cuda.synchronize()
+
+    stores = cache._stores
+    q_dev = [synth((B, hq, 1, D)) for _ in range(LAYERS)]
+    k_new = [synth((B, hkv, 1, D)) for _ in range(LAYERS)]
+    v_new = [synth((B, hkv, 1, D)) for _ in range(LAYERS)]
+    o_loc = [torch.empty((B, hq, 1, D), dtype=torch.bfloat16, device=dev) for _ in range(LAYERS)]
+    o_all = [torch.empty((world, B, hq, 1, D), dtype=torch.bfloat16, device=dev)
+             for _ in range(LAYERS)]
+    ws = ops.DecodeWorkspace()
+    n_tok = T_CTX + 1
+
+    def step(phased_events=None):
+        for layer in range(LAYERS):
+            st = stores[layer]
+            ops.append(st.tables, st._pages, k_new[layer], v_new[layer], T_CTX)
+            if phased_events is None:
+                ops.decode_attention(st.tables, st._pages, q_dev[layer], n_tok,
+                                     out=o_loc[layer], workspace=ws)
+            else:
+                ops.decode_attention(st.tables, st._pages, q_dev[layer], n_tok,
+                                     out=o_loc[layer], workspace=ws,
+                                     phases=_lib.PHASE_QPREP)
+                e0, e1 = phased_events[layer]
+                e0.record()
+                ops.decode_attention(st.tables, st._pages, q_dev[layer], n_tok,
+                                     out=o_loc[layer], workspace=ws,
+                                     phases=_lib.PHASE_DECODE)
+                e1.record()
+                ops.decode_attention(st.tables, st._pages, q_dev[layer], n_tok,
+                                     out=o_loc[layer], workspace=ws,
+                                     phases=_lib.PHASE_MERGE)
+            if world > 1:
+                dist.all_gather_into_tensor(o_all[layer], o_loc[layer])
+
+    # eager warm-up (sets kernel attributes, sizes the workspace)
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if ws.status() != 0:
+        raise RuntimeError("device status error after warm-up")
+
+    # ---- CUDA graph of one step -------------------------------------------
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    phys = local_rank
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if cvd:
+        try:
+            phys = int(cvd.split(",")[local_rank])
+        except ValueError:
+            pass
+    sampler = ClockSampler(phys)
+
+    # ---- timed region: K graph replays --------------------------------------
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = B / (ms_step / 1e3)
+
+    # ---- roofline pass: decode kernel timed alone with events ---------------
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(LAYERS)] for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(2e8))          # let the host queue the whole pass first
+    for k in range(args.steps):
+        step(phased_events=evs[k])
+    torch.cuda.synchronize()
+    dec_ms = [e0.elapsed_time(e1) for row in evs for (e0, e1) in row]
+    dec_avg = sum(dec_ms) / len(dec_ms)
+    alg_bytes = S * n_tok * bpt
+    hbm_peak, peak_kind = _peaks()
+    achieved = alg_bytes / (dec_avg / 1e3) / 1e9
+
+    # ---- e2e through the public API with host buffers -----------------------
+    q_h = [q.cpu().pin_memory() for q in q_dev[:4]]
+    k_h = [k.cpu().pin_memory() for k in k_new[:4]]
+    v_h = [v.cpu().pin_memory() for v in v_new[:4]]
+    o_h = torch.empty((world if world > 1 else 1, B, hq, 1, D), dtype=torch.bfloat16).pin_memory()
+    h2d = (q_h[0].numel() + k_h[0].numel() + v_h[0].numel()) * 2 * LAYERS
+    d2h = o_h.numel() * 2 * LAYERS
+
+    def e2e_step():
+        for layer in range(LAYERS):
+            qd = q_h[layer % 4].to(dev, non_blocking=True)
+            kd = k_h[layer % 4].to(dev, non_blocking=True)
+            vd = v_h[layer % 4].to(dev, non_blocking=True)
+            cache.append(kd, vd, layer)
+            o = cache.attend(qd, layer)
+            if world > 1:
+                dist.all_gather_into_tensor(o_all[layer], o)
+                o_h.copy_(o_all[layer], non_blocking=True)
+            else:
+                o_h[0].copy_(o, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
+    for st in stores:      # the e2e leg appends for real: start from T_CTX tokens
+        st._comp_ptr = T_CTX
+    for _ in range(args.warmup):
+        e2e_step()
+    for st in stores:
+        st._comp_ptr = T_CTX
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = B / (e2e_ms / args.steps / 1e3)
+    status = cache.device_status() | ws.status()
+    del graph
+
+    # ---- prefill append throughput (48 layers x B8 x Hkv8 x 4096, 4-bit) ----
+    append_line = None
+    if rank == 0 and not args.skip_append:
+        append_line = bench_append(dev, args)
+
+    cpu_line = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        from oracle import cpu_baseline as C
+        t_layer = C.time_decode(B, HQ, HKV, D, T_CTX, KEY_BITS, VALUE_BITS, steps=2)
+        cpu_line = {"value": B / (t_layer * LAYERS), "unit": "tokens/s",
+                    "cores": C.host_threads(), "kind": "port",
+                    "sample": f"reference update()+SDPA, 1 of {LAYERS} layers x 2 steps "
+                              f"timed and scaled x{LAYERS}; B{B} Hkv{HKV} T{T_CTX}, no QJL"}
+
+    if rank == 0:
+        line = {
+            "metric": "decode-attn tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": _config(world),
+            "packed_kv_gbs_per_gpu": LAYERS * alg_bytes / (ms_step / 1e3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "traffic": _traffic_per_launch(),
+                         "kernel": "decode_kernel<128,4,2,qjl>",
+                         "algorithmic_bytes_per_launch": alg_bytes,
+                         "avg_launch_ms": dec_avg, "peak_kind": peak_kind},
+            "cpu_baseline": cpu_line,
+            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "path": "TurboQuantKVCache.append + .attend per layer, pinned host "
+                            "q/k/v in, output out"},
+            "gpu_launches": args.steps * LAYERS * 4,
+            "clocks": clocks,
+            "append": append_line,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def bench_append(dev, args):
+    """Prefill append GB/s: 48 layers x (B8 x Hkv8 x 4096 tokens x D128) bf16,
+    K and V at 4 bits: 512 B read + 132 B written per token-head."""
+    import torch
+    from bhaskera_col_b200.inference import ops
+    from bhaskera_col_b200.inference.kv_cache import (FastLloydMaxCodebook,
+                                                      _generate_rotation_matrix)
+    c = APPEND_CFG
+    L, B, H, T, Dd, bits = c["layers"], c["B"], c["H"], c["T"], c["D"], c["bits"]
+    cb = FastLloydMaxCodebook.get(Dd, bits, dev)
+    tables = [ops.LayerTables(Dd, bits, bits, False, cb.centroids, cb.boundaries,
+                              cb.centroids, cb.boundaries,
+                              _generate_rotation_matrix(Dd, 42 + 13 * i, dev).contiguous())
+              for i in range(L)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    sc = torch.exp(torch.empty(Dd, device=dev).uniform_(math.log(0.1), math.log(10.0),
+                                                        generator=gen))
+    xs = [((torch.randn((B, H, T, Dd), device=dev, generator=gen) * sc).to(torch.bfloat16),
+           (torch.randn((B, H, T, Dd), device=dev, generator=gen) * sc).to(torch.bfloat16))
+          for _ in range(4)]
+    pb = ops.page_bytes(Dd, bits, bits, False)
+    pages = [torch.zeros((B * H, T // 64, pb), dtype=torch.uint8, device=dev) for _ in range(L)]
+
+    def run():
+        for i in range(L):
+            k, v = xs[i % 4]
+            ops.append(tables[i], pages[i], k, v, 0)
+
+    run()
+    torch.cuda.synchronize()
+    reps = max(1, min(args.steps, 3))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    th = L * B * H * T
+    alg = th * (2 * Dd * 2 + 2 * (Dd * bits // 8 + 2))
+    return {"workload": f"prefill append {L} layers x B{B} x Hkv{H} x {T} tokens, D{Dd}, "
+                        f"K{bits}/V{bits}, bf16 in", "ms": ms, "gbs": alg / (ms / 1e3) / 1e9,
+            "token_heads_per_s": th / (ms / 1e3), "algorithmic_bytes": alg}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-append", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if world != args.gpus and "WORLD_SIZE" in os.environ:
+        args.gpus = world
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch.distributed as dist
+    if world > 1:
+        import torch
+        torch.cuda.set_device(local_rank)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,280 @@
+// tq_capi.cu — extern "C" boundary: argument validation, error reporting and
+// dispatch to the kernels.  See include/tq_b200.h for the contract.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <utility>
+
+#include "tq_common.cuh"
+#include "tq_internal.h"
+
+namespace tq {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s: launch failed: %s", what, cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return TQ_OK;
+}
+
+// Kernel attributes and device properties are queried once per (device,
+// kernel) and cached, so that launches made while a stream is being captured
+// into a CUDA graph issue nothing but the kernels themselves.
+static std::mutex g_attr_mu;
+static std::map<std::pair<int, const void*>, size_t> g_smem_set;
+static std::map<std::tuple<int, const void*, size_t, int>, int> g_occ;
+static std::map<int, int> g_sms;
+
+static int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int set_smem_attr(const void* kernel, size_t bytes) {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  auto key = std::make_pair(dev, kernel);
+  auto it = g_smem_set.find(key);
+  if (it != g_smem_set.end() && it->second >= bytes) return TQ_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)bytes);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute(%zu bytes of shared memory): %s", bytes, cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  g_smem_set[key] = bytes;
+  return TQ_OK;
+}
+
+int occupancy(const void* kernel, int threads, size_t smem) {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  auto key = std::make_tuple(dev, kernel, smem, threads);
+  auto it = g_occ.find(key);
+  if (it != g_occ.end()) return it->second;
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem) != cudaSuccess)
+    occ = 1;
+  g_occ[key] = occ;
+  return occ;
+}
+
+int device_sm_count() {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  auto it = g_sms.find(dev);
+  if (it != g_sms.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
+  g_sms[dev] = n;
+  return n;
+}
+
+static bool valid_dtype(int d) { return d == TQ_F32 || d == TQ_F16 || d == TQ_BF16; }
+
+static int check_geom(const tq_geom* g, const char* fn) {
+  if (!g) { set_error("%s: geometry is NULL", fn); return TQ_ERR_INVALID; }
+  if (g->head_dim < 32 || g->head_dim > 256 || g->head_dim % 32) {
+    set_error("%s: head_dim must be a multiple of 32 in [32, 256], got %d", fn, g->head_dim);
+    return TQ_ERR_INVALID;
+  }
+  if (g->key_bits < 1 || g->key_bits > 8 || g->value_bits < 1 || g->value_bits > 8) {
+    set_error("%s: bit widths must be in [1, 8], got key_bits=%d value_bits=%d", fn,
+              g->key_bits, g->value_bits);
+    return TQ_ERR_INVALID;
+  }
+  return TQ_OK;
+}
+
+static int check_tables(const tq_geom* g, const tq_tables* t, const char* fn) {
+  if (!t || !t->k_centroids || !t->k_boundaries || !t->v_centroids || !t->v_boundaries || !t->rot) {
+    set_error("%s: a codebook or rotation table pointer is NULL", fn);
+    return TQ_ERR_INVALID;
+  }
+  if (g->qjl && !t->qjl) { set_error("%s: qjl enabled but the QJL matrix is NULL", fn); return TQ_ERR_INVALID; }
+  return TQ_OK;
+}
+
+static int check_cache(const tq_cache* c, const char* fn) {
+  if (!c || !c->pages || c->streams <= 0 || c->pages_per_stream <= 0) {
+    set_error("%s: invalid cache descriptor", fn);
+    return TQ_ERR_INVALID;
+  }
+  if (reinterpret_cast<uintptr_t>(c->pages) % 16) {
+    set_error("%s: page storage must be 16-byte aligned", fn);
+    return TQ_ERR_INVALID;
+  }
+  return TQ_OK;
+}
+
+static int check_t4(const tq_tensor4* x, const char* what, const char* fn) {
+  if (!x || !x->data) { set_error("%s: %s is NULL", fn, what); return TQ_ERR_INVALID; }
+  if (!valid_dtype(x->dtype)) { set_error("%s: %s has unsupported dtype %d", fn, what, x->dtype); return TQ_ERR_INVALID; }
+  for (int i = 0; i < 4; ++i)
+    if (x->shape[i] < 0) { set_error("%s: %s has a negative extent", fn, what); return TQ_ERR_INVALID; }
+  return TQ_OK;
+}
+
+}  // namespace tq
+
+using namespace tq;
+
+extern "C" {
+
+const char* tq_last_error(void) { return g_err; }
+
+int32_t tq_version(void) { return 1; }
+
+int64_t tq_page_bytes(const tq_geom* g) {
+  if (check_geom(g, "tq_page_bytes") != TQ_OK) return -1;
+  return make_geom(g->head_dim, g->key_bits, g->value_bits, g->qjl).page_bytes;
+}
+
+int32_t tq_quantize_rotated(const float* y, int64_t n, const float* boundaries,
+                            int32_t n_boundaries, int16_t* codes, void* stream) {
+  if (n < 0 || (n > 0 && (!y || !codes || !boundaries)) || n_boundaries < 1 || n_boundaries > 255) {
+    set_error("tq_quantize_rotated: invalid arguments (n=%lld, n_boundaries=%d)", (long long)n,
+              n_boundaries);
+    return TQ_ERR_INVALID;
+  }
+  return launch_quantize_rotated(y, n, boundaries, n_boundaries, codes, (cudaStream_t)stream);
+}
+
+int32_t tq_append(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                  const tq_tensor4* k, const tq_tensor4* v, int64_t pos, void* stream) {
+  const char* fn = "tq_append";
+  int rc;
+  if ((rc = check_geom(g, fn)) || (rc = check_tables(g, t, fn)) || (rc = check_cache(c, fn)) ||
+      (rc = check_t4(k, "k", fn)) || (rc = check_t4(v, "v", fn)))
+    return rc;
+  if (g->head_dim > 128) {
+    set_error("%s: head_dim %d > 128 is not supported by the append kernel", fn, g->head_dim);
+    return TQ_ERR_INVALID;
+  }
+  for (int i = 0; i < 4; ++i)
+    if (k->shape[i] != v->shape[i]) { set_error("%s: k and v shapes differ", fn); return TQ_ERR_INVALID; }
+  if (k->shape[3] != g->head_dim) {
+    set_error("%s: last dim %lld != head_dim %d", fn, (long long)k->shape[3], g->head_dim);
+    return TQ_ERR_INVALID;
+  }
+  if (k->shape[0] * k->shape[1] != c->streams) {
+    set_error("%s: B*H = %lld does not match the cache's %lld streams", fn,
+              (long long)(k->shape[0] * k->shape[1]), (long long)c->streams);
+    return TQ_ERR_INVALID;
+  }
+  if (pos < 0 || pos + k->shape[2] > c->pages_per_stream * TQ_PAGE_TOKENS) {
+    set_error("%s: tokens [%lld, %lld) exceed the capacity of %lld tokens", fn, (long long)pos,
+              (long long)(pos + k->shape[2]), (long long)(c->pages_per_stream * TQ_PAGE_TOKENS));
+    return TQ_ERR_INVALID;
+  }
+  return launch_append(g, t, c, k, v, pos, (cudaStream_t)stream);
+}
+
+int32_t tq_dequantize(const tq_geom* g, const tq_tables* t, const tq_cache* c, int64_t t0,
+                      int64_t t1, const tq_tensor4* k_out, const tq_tensor4* v_out, void* stream) {
+  const char* fn = "tq_dequantize";
+  int rc;
+  if ((rc = check_geom(g, fn)) || (rc = check_tables(g, t, fn)) || (rc = check_cache(c, fn)))
+    return rc;
+  if (k_out && (rc = check_t4(k_out, "k_out", fn))) return rc;
+  if (v_out && (rc = check_t4(v_out, "v_out", fn))) return rc;
+  if (t0 < 0 || t1 < t0 || t1 > c->pages_per_stream * TQ_PAGE_TOKENS) {
+    set_error("%s: token range [%lld, %lld) out of bounds", fn, (long long)t0, (long long)t1);
+    return TQ_ERR_INVALID;
+  }
+  const tq_tensor4* o[2] = {k_out, v_out};
+  for (int w = 0; w < 2; ++w) {
+    if (!o[w]) continue;
+    if (o[w]->shape[0] * o[w]->shape[1] != c->streams || o[w]->shape[2] != t1 - t0 ||
+        o[w]->shape[3] != g->head_dim) {
+      set_error("%s: output view shape does not match (streams, t1-t0, head_dim)", fn);
+      return TQ_ERR_INVALID;
+    }
+  }
+  return launch_dequant(g, t, c, t0, t1, k_out, v_out, (cudaStream_t)stream);
+}
+
+static int check_decode(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                        const tq_decode_args* a, const char* fn) {
+  int rc;
+  if ((rc = check_geom(g, fn)) || (rc = check_tables(g, t, fn)) || (rc = check_cache(c, fn)))
+    return rc;
+  if (!a) { set_error("%s: args is NULL", fn); return TQ_ERR_INVALID; }
+  if ((rc = check_t4(a->q, "q", fn)) || (rc = check_t4(a->out, "out", fn))) return rc;
+  const int64_t B = a->q->shape[0];
+  if (B <= 0 || c->streams % B) { set_error("%s: batch does not divide the stream count", fn); return TQ_ERR_INVALID; }
+  const int64_t Hkv = c->streams / B;
+  if (a->num_q_heads <= 0 || a->num_q_heads % Hkv || a->q->shape[1] != a->num_q_heads ||
+      a->q->shape[2] != 1 || a->q->shape[3] != g->head_dim) {
+    set_error("%s: q must be (B, Hq, 1, D) with Hq a multiple of Hkv=%lld", fn, (long long)Hkv);
+    return TQ_ERR_INVALID;
+  }
+  for (int i = 0; i < 4; ++i)
+    if (a->out->shape[i] != a->q->shape[i]) { set_error("%s: out shape != q shape", fn); return TQ_ERR_INVALID; }
+  if (a->n_tokens < 0 || a->n_tokens > c->pages_per_stream * TQ_PAGE_TOKENS) {
+    set_error("%s: n_tokens=%lld exceeds the cache capacity", fn, (long long)a->n_tokens);
+    return TQ_ERR_INVALID;
+  }
+  if ((a->window_k == nullptr) != (a->window_v == nullptr)) {
+    set_error("%s: window_k and window_v must both be given or both be NULL", fn);
+    return TQ_ERR_INVALID;
+  }
+  if (a->window_k) {
+    if ((rc = check_t4(a->window_k, "window_k", fn)) || (rc = check_t4(a->window_v, "window_v", fn))) return rc;
+    for (int i = 0; i < 4; ++i)
+      if (a->window_k->shape[i] != a->window_v->shape[i]) { set_error("%s: window shapes differ", fn); return TQ_ERR_INVALID; }
+    if (a->window_k->dtype != a->window_v->dtype) { set_error("%s: window dtypes differ", fn); return TQ_ERR_INVALID; }
+    if (a->window_k->shape[0] != B || a->window_k->shape[1] != Hkv || a->window_k->shape[3] != g->head_dim) {
+      set_error("%s: window must be (B, Hkv, W, D)", fn);
+      return TQ_ERR_INVALID;
+    }
+    if (a->window_k->shape[2] > 4096) { set_error("%s: window longer than 4096 tokens", fn); return TQ_ERR_INVALID; }
+  }
+  return TQ_OK;
+}
+
+size_t tq_decode_workspace_bytes(const tq_geom* g, const tq_cache* c, const tq_decode_args* a) {
+  const char* fn = "tq_decode_workspace_bytes";
+  if (check_geom(g, fn) || check_cache(c, fn) || !a || check_t4(a->q, "q", fn)) return 0;
+  if (a->q->shape[0] <= 0 || c->streams % a->q->shape[0]) return 0;
+  return decode_workspace_bytes(g, c, a);
+}
+
+int32_t tq_decode_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                       const tq_decode_args* a, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  const char* fn = "tq_decode_attn";
+  int rc = check_decode(g, t, c, a, fn);
+  if (rc) return rc;
+  return launch_decode(g, t, c, a, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream) {
+  if (!workspace || !status) { set_error("tq_workspace_status: NULL argument"); return TQ_ERR_INVALID; }
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(status, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(workspace, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) {
+    set_error("tq_workspace_status: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return *status ? TQ_ERR_DEVICE : TQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,33 @@
+// tq_internal.h — host-side glue shared by the .cu translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "tq_b200.h"
+
+namespace tq {
+
+// Thread-local error message (tq_last_error).
+void set_error(const char* fmt, ...);
+// Returns TQ_OK, or TQ_ERR_CUDA with the launch error recorded.
+int check_launch(const char* what);
+int set_smem_attr(const void* kernel, size_t bytes);
+int device_sm_count();
+// Resident CTAs per SM for a kernel (cached per device).
+int occupancy(const void* kernel, int threads, size_t smem);
+
+int launch_quantize_rotated(const float* y, int64_t n, const float* b, int nb,
+                            int16_t* codes, cudaStream_t st);
+int launch_append(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                  const tq_tensor4* k, const tq_tensor4* v, int64_t pos,
+                  cudaStream_t st);
+int launch_dequant(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                   int64_t t0, int64_t t1, const tq_tensor4* ko, const tq_tensor4* vo,
+                   cudaStream_t st);
+size_t decode_workspace_bytes(const tq_geom* g, const tq_cache* c,
+                              const tq_decode_args* a);
+int launch_decode(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                  const tq_decode_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
+
+}  // namespace tq

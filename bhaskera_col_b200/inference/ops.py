@@ -1,0 +1,188 @@
+"""torch-facing wrappers of the libtq_b200 C ABI.
+
+Tensors are owned by PyTorch; the kernels borrow raw device pointers and run
+on the current CUDA stream.  Every wrapper raises (never falls back to a CPU
+or PyTorch implementation) when the library or the device is unavailable.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from .. import _lib
+
+_DT = {torch.float32: _lib.TQ_F32, torch.float16: _lib.TQ_F16, torch.bfloat16: _lib.TQ_BF16}
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("TurboQuant kernels need CUDA tensors (there is no CPU path)")
+
+
+def tensor4(x: torch.Tensor) -> _lib.Tensor4:
+    if x.dim() != 4:
+        raise ValueError(f"expected a 4-d tensor, got shape {tuple(x.shape)}")
+    if x.dtype not in _DT:
+        raise ValueError(f"unsupported dtype {x.dtype}")
+    t = _lib.Tensor4()
+    t.data = x.data_ptr()
+    t.dtype = _DT[x.dtype]
+    for i in range(4):
+        t.shape[i] = x.shape[i]
+        t.stride[i] = x.stride(i)
+    return t
+
+
+@dataclass
+class LayerTables:
+    """Per-layer constant device tables (codebooks, rotation, QJL matrix)."""
+    head_dim: int
+    key_bits: int
+    value_bits: int
+    qjl: bool
+    k_centroids: torch.Tensor
+    k_boundaries: torch.Tensor
+    v_centroids: torch.Tensor
+    v_boundaries: torch.Tensor
+    rot: torch.Tensor
+    qjl_mat: Optional[torch.Tensor] = None
+
+    def geom(self) -> _lib.Geom:
+        return _lib.Geom(self.head_dim, self.key_bits, self.value_bits, 1 if self.qjl else 0)
+
+    def ctables(self) -> _lib.Tables:
+        t = _lib.Tables()
+        t.k_centroids = self.k_centroids.data_ptr()
+        t.k_boundaries = self.k_boundaries.data_ptr()
+        t.v_centroids = self.v_centroids.data_ptr()
+        t.v_boundaries = self.v_boundaries.data_ptr()
+        t.rot = self.rot.data_ptr()
+        t.qjl = self.qjl_mat.data_ptr() if self.qjl_mat is not None else None
+        return t
+
+
+def page_bytes(head_dim: int, key_bits: int, value_bits: int, qjl: bool) -> int:
+    """Bytes of one 64-token page (same formula as tq_page_bytes)."""
+    krow, vrow = head_dim * key_bits // 8, head_dim * value_bits // 8
+    qrow = head_dim // 8 if qjl else 0
+    return _lib.PAGE_TOKENS * (krow + vrow + qrow + 4 + (2 if qjl else 0))
+
+
+def _cache_desc(pages: torch.Tensor) -> _lib.Cache:
+    c = _lib.Cache()
+    c.pages = pages.data_ptr()
+    c.streams = pages.shape[0]
+    c.pages_per_stream = pages.shape[1]
+    return c
+
+
+# ---------------------------------------------------------------------------
+def quantize_rotated(y: torch.Tensor, boundaries: torch.Tensor) -> torch.Tensor:
+    """Bit-exact torch.bucketize(y, boundaries) -> int16, on the GPU."""
+    _require_cuda(y, boundaries)
+    y = y.contiguous().float()
+    b = boundaries.contiguous().float()
+    codes = torch.empty(y.shape, dtype=torch.int16, device=y.device)
+    lib = _lib.load()
+    _lib.check("tq_quantize_rotated",
+               lib.tq_quantize_rotated(y.data_ptr(), y.numel(), b.data_ptr(), b.numel(),
+                                       codes.data_ptr(), _stream(y.device)))
+    return codes
+
+
+def append(tables: LayerTables, pages: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+           pos: int) -> None:
+    """Quantise and store tokens [pos, pos+T) of (B, H, T, D) k/v into pages."""
+    _require_cuda(pages, k, v)
+    lib = _lib.load()
+    g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
+    kt, vt = tensor4(k), tensor4(v)
+    _lib.check("tq_append", lib.tq_append(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c),
+                                          ctypes.byref(kt), ctypes.byref(vt), int(pos),
+                                          _stream(k.device)))
+
+
+def dequantize(tables: LayerTables, pages: torch.Tensor, t0: int, t1: int,
+               k_out: Optional[torch.Tensor], v_out: Optional[torch.Tensor]) -> None:
+    """Write dequantised tokens [t0, t1) into (B, H, t1-t0, D) views."""
+    _require_cuda(pages, k_out, v_out)
+    lib = _lib.load()
+    g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
+    ko = tensor4(k_out) if k_out is not None else None
+    vo = tensor4(v_out) if v_out is not None else None
+    _lib.check("tq_dequantize", lib.tq_dequantize(
+        ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), int(t0), int(t1),
+        ctypes.byref(ko) if ko is not None else None,
+        ctypes.byref(vo) if vo is not None else None, _stream(pages.device)))
+
+
+class DecodeWorkspace:
+    """Grow-only device scratch for tq_decode_attn (first 4 bytes: status word)."""
+
+    def __init__(self):
+        self.buf: Optional[torch.Tensor] = None
+
+    def get(self, nbytes: int, device: torch.device) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+            self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        return self.buf
+
+    def status(self) -> int:
+        """Read and clear the device status word (synchronises the stream)."""
+        if self.buf is None:
+            return 0
+        lib = _lib.load()
+        st = ctypes.c_uint32(0)
+        lib.tq_workspace_status(self.buf.data_ptr(), ctypes.byref(st), _stream(self.buf.device))
+        return int(st.value)
+
+
+def decode_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
+                     n_tokens: int, window_k: Optional[torch.Tensor] = None,
+                     window_v: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                     out: Optional[torch.Tensor] = None,
+                     workspace: Optional[DecodeWorkspace] = None,
+                     num_ctas: int = 0, phases: int = 0) -> torch.Tensor:
+    """softmax(q K^T * scale) V over the packed tokens [0, n_tokens) of every
+    stream plus an optional full-precision window.  q: (B, Hq, 1, D).
+
+    ``phases`` (OR of _lib.PHASE_*) runs a subset of the three kernels; the
+    later phases read what the earlier ones left in the same ``workspace``."""
+    _require_cuda(pages, q)
+    lib = _lib.load()
+    if out is None:
+        out = torch.empty_like(q)
+    D = q.shape[-1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
+    qt, ot = tensor4(q), tensor4(out)
+    wk = tensor4(window_k) if window_k is not None and window_k.shape[2] > 0 else None
+    wv = tensor4(window_v) if wk is not None else None
+    a = _lib.DecodeArgs()
+    a.q = ctypes.pointer(qt)
+    a.out = ctypes.pointer(ot)
+    a.window_k = ctypes.pointer(wk) if wk is not None else None
+    a.window_v = ctypes.pointer(wv) if wv is not None else None
+    a.n_tokens = int(n_tokens)
+    a.num_q_heads = q.shape[1]
+    a.scale = float(scale)
+    a.num_ctas = int(num_ctas)
+    a.phases = int(phases)
+    nbytes = lib.tq_decode_workspace_bytes(ctypes.byref(g), ctypes.byref(c), ctypes.byref(a))
+    if nbytes == 0:
+        raise _lib.TqError("tq_decode_workspace_bytes", _lib.TQ_ERR_INVALID, _lib.last_error())
+    ws = (workspace or DecodeWorkspace()).get(nbytes, q.device)
+    _lib.check("tq_decode_attn", lib.tq_decode_attn(
+        ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(a),
+        ws.data_ptr(), ws.numel(), _stream(q.device)))
+    return out

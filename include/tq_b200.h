@@ -1,0 +1,162 @@
+/*
+ * tq_b200.h — C ABI of the B200 (sm_100a) TurboQuant KV-cache kernels.
+ *
+ * Every entry point takes raw device pointers, explicit sizes and strides,
+ * and a cudaStream_t passed as `void*`.  Nothing here allocates device
+ * memory: scratch ("workspace") is supplied by the caller and sized with the
+ * matching *_workspace_bytes() query.  Work is stream-ordered and no entry
+ * point synchronises the host.  Every function returns TQ_OK (0) or a
+ * negative status; tq_last_error() gives a thread-local message for the last
+ * failure on the calling thread.
+ *
+ * Reference interfaces replaced (aditya25058/Bhaskera_col, paths relative to
+ * the project root):
+ *   tq_quantize_rotated  FastLloydMaxCodebook.quantize
+ *                        src/bhaskera/inference/kv_cache.py:105-113
+ *   tq_append            _LayerKVStore._compress_chunk (norm, rotate,
+ *                        bucketize, store)  kv_cache.py:355-420
+ *   tq_dequantize        _LayerKVStore._decode_range  kv_cache.py:422-439
+ *   tq_decode_attn       the HF attention over TurboQuantKVCache.update()'s
+ *                        output (torch SDPA, GQA), reached from
+ *                        src/bhaskera/inference/engine.py:389 through
+ *                        kv_cache.py:580-589
+ *   tq_prefill_attn      same, causal multi-token case
+ *
+ * Packed layout (per layer): an array of streams (stream = b * Hkv + h, the
+ * reference's B*H flattening at kv_cache.py:364-365), each an array of
+ * pages of TQ_PAGE_TOKENS tokens.  A page holds, in order:
+ *   kcodes [64][D*kb/8]   K codes, quad order, LSB-first bit stream
+ *   vcodes [64][D*vb/8]   V codes, octet order, LSB-first bit stream
+ *   kqjl   [64][D/8]      QJL residual signs (only when qjl != 0)
+ *   knorm  [64] fp16      ||k||
+ *   vnorm  [64] fp16      ||v||
+ *   krnorm [64] fp16      ||k|| * ||y - c[idx]||  (only when qjl != 0)
+ * Quad order: quad t (t = 0..3) lists, for each 16-coordinate chunk j,
+ * coordinates 16j+2t, 16j+2t+1, 16j+2t+8, 16j+2t+9.  Octet order: octet g
+ * (g = 0..7) lists coordinates g, g+8, g+16, ...
+ */
+#ifndef TQ_B200_H
+#define TQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TQ_PAGE_TOKENS 64
+
+/* status codes */
+#define TQ_OK 0
+#define TQ_ERR_INVALID (-1)     /* bad argument / unsupported shape        */
+#define TQ_ERR_CUDA (-2)        /* a CUDA runtime call or launch failed    */
+#define TQ_ERR_WORKSPACE (-3)   /* workspace missing or too small          */
+#define TQ_ERR_DEVICE (-4)      /* a kernel reported a device-side error   */
+
+/* element types */
+#define TQ_F32 0
+#define TQ_F16 1
+#define TQ_BF16 2
+
+/* device status word bits (written by kernels into the workspace) */
+#define TQ_DEV_WAIT_TIMEOUT 1u  /* a bounded mbarrier wait ran out          */
+
+typedef struct tq_geom {
+  int32_t head_dim;    /* D: multiple of 32, 32..256                        */
+  int32_t key_bits;    /* 1..8                                               */
+  int32_t value_bits;  /* 1..8                                               */
+  int32_t qjl;         /* 1: store the 1-bit QJL residual sketch of K        */
+} tq_geom;
+
+/* Per-layer constant tables, all fp32 device pointers. */
+typedef struct tq_tables {
+  const float* k_centroids;   /* [2^kb]                                     */
+  const float* k_boundaries;  /* [2^kb - 1], ascending                       */
+  const float* v_centroids;   /* [2^vb]                                      */
+  const float* v_boundaries;  /* [2^vb - 1]                                  */
+  const float* rot;           /* R [D][D] row-major; y = x R^T               */
+  const float* qjl;           /* S [D][D] row-major (NULL when qjl == 0)     */
+} tq_tables;
+
+/* Packed cache of one layer. */
+typedef struct tq_cache {
+  uint8_t* pages;             /* [streams][pages_per_stream][page_bytes]     */
+  int64_t streams;            /* B * Hkv                                     */
+  int64_t pages_per_stream;   /* capacity in pages                           */
+} tq_cache;
+
+/* A strided 4-d tensor view (B, H, T, D); strides in elements. */
+typedef struct tq_tensor4 {
+  void* data;
+  int32_t dtype;              /* TQ_F32 / TQ_F16 / TQ_BF16                   */
+  int64_t shape[4];
+  int64_t stride[4];
+} tq_tensor4;
+
+const char* tq_last_error(void);
+int32_t tq_version(void);
+int64_t tq_page_bytes(const tq_geom* g);
+
+/* Bit-exact scalar quantiser: codes[i] = #{ j : boundaries[j] < y[i] }
+ * (torch.bucketize, right=False) for n fp32 values, int16 output.
+ * Replaces FastLloydMaxCodebook.quantize (kv_cache.py:105-113). */
+int32_t tq_quantize_rotated(const float* y, int64_t n, const float* boundaries,
+                            int32_t n_boundaries, int16_t* codes,
+                            void* stream);
+
+/* Fused append of tokens [pos, pos + T) of every stream: fp32 norm,
+ * u = x / max(n, 1e-8), y = u R^T, codes = bucketize(y), pack, fp16 norms,
+ * optional QJL sign sketch of the rotated residual.  k and v are (B, Hkv,
+ * T, D) views with B * Hkv == cache->streams.
+ * Replaces _LayerKVStore._compress_chunk (kv_cache.py:355-420). */
+int32_t tq_append(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                  const tq_tensor4* k, const tq_tensor4* v, int64_t pos,
+                  void* stream);
+
+/* Dequantise tokens [t0, t1) of every stream into dense K/V views
+ * (B, Hkv, t1 - t0, D): x = (c[idx] R) * norm, cast to the view's dtype.
+ * Either output may be NULL.  Replaces _decode_range (kv_cache.py:422-439). */
+int32_t tq_dequantize(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                      int64_t t0, int64_t t1, const tq_tensor4* k_out,
+                      const tq_tensor4* v_out, void* stream);
+
+/* Single-token GQA decode attention straight off the packed cache, plus an
+ * optional full-precision window of the most recent tokens (not rotated).
+ * q: (B, Hq, 1, D); out: (B, Hq, 1, D); window_k/v: (B, Hkv, W, D) or NULL.
+ * Keys [0, n_tokens) of every stream are attended.  scale is the softmax
+ * scale (1/sqrt(D) for SDPA's default).  Workspace from
+ * tq_decode_workspace_bytes(). */
+typedef struct tq_decode_args {
+  const tq_tensor4* q;
+  const tq_tensor4* out;
+  const tq_tensor4* window_k;  /* may be NULL                                */
+  const tq_tensor4* window_v;  /* may be NULL                                */
+  int64_t n_tokens;            /* packed tokens per stream                   */
+  int64_t num_q_heads;         /* Hq (multiple of Hkv)                       */
+  float scale;
+  int32_t num_ctas;            /* 0: choose from the SM count                */
+  int32_t phases;              /* 0: all; else OR of TQ_PHASE_* (each phase  */
+                               /* reads what the previous one left in the   */
+                               /* same workspace)                            */
+} tq_decode_args;
+
+#define TQ_PHASE_QPREP 1       /* rotate + sketch the query                  */
+#define TQ_PHASE_DECODE 2      /* attend the packed pages (partials)         */
+#define TQ_PHASE_MERGE 4       /* combine partials + window, un-rotate       */
+
+size_t tq_decode_workspace_bytes(const tq_geom* g, const tq_cache* c,
+                                 const tq_decode_args* a);
+int32_t tq_decode_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                       const tq_decode_args* a, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* Read and clear the device status word kept at the start of a decode
+ * workspace (blocking copy on `stream`). */
+int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TQ_B200_H */

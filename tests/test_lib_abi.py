@@ -1,0 +1,98 @@
+"""The C-ABI library: loads without a GPU, exports every declared symbol, and
+rejects bad arguments before touching the device (CPU only)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from bhaskera_col_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "tq_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(tq_[a-z_]+)\s*\(", src)))
+
+
+def test_header_declares_the_binding_list():
+    assert declared_functions() == sorted(_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.tq_version() == 1
+
+
+def _geom(D=128, kb=4, vb=2, q=1):
+    return _lib.Geom(D, kb, vb, q)
+
+
+def test_invalid_geometry_rejected():
+    lib = _lib.load()
+    assert lib.tq_page_bytes(ctypes.byref(_geom(D=48))) == -1
+    assert "multiple of 32" in _lib.last_error()
+    assert lib.tq_page_bytes(ctypes.byref(_geom(kb=9))) == -1
+    assert "bit widths" in _lib.last_error()
+
+
+def test_append_argument_validation():
+    lib = _lib.load()
+    g = _geom()
+    t = _lib.Tables()                       # NULL tables
+    c = _lib.Cache()
+    k = _lib.Tensor4()
+    rc = lib.tq_append(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(k),
+                       ctypes.byref(k), 0, None)
+    assert rc == _lib.TQ_ERR_INVALID
+    assert "NULL" in _lib.last_error()
+    # all pointers non-null, but k/v disagree with the cache's stream count
+    t = _lib.Tables(*([16] * 6))
+    c = _lib.Cache(1024, 3, 4)
+    k = _lib.Tensor4(16, _lib.TQ_BF16, (ctypes.c_int64 * 4)(1, 2, 5, 128),
+                     (ctypes.c_int64 * 4)(1280, 640, 128, 1))
+    rc = lib.tq_append(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(k),
+                       ctypes.byref(k), 0, None)
+    assert rc == _lib.TQ_ERR_INVALID and "streams" in _lib.last_error()
+    # capacity overflow: 4 pages * 64 tokens
+    c = _lib.Cache(1024, 2, 4)
+    rc = lib.tq_append(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(k),
+                       ctypes.byref(k), 254, None)
+    assert rc == _lib.TQ_ERR_INVALID and "capacity" in _lib.last_error()
+
+
+def test_decode_argument_validation():
+    lib = _lib.load()
+    g = _geom()
+    t = _lib.Tables(*([16] * 6))
+    c = _lib.Cache(1024, 8, 4)
+    q = _lib.Tensor4(16, _lib.TQ_BF16, (ctypes.c_int64 * 4)(2, 6, 1, 128),
+                     (ctypes.c_int64 * 4)(768, 128, 128, 1))
+    a = _lib.DecodeArgs()
+    a.q = ctypes.pointer(q)
+    a.out = ctypes.pointer(q)
+    a.n_tokens = 10
+    a.num_q_heads = 6                       # 6 query heads over 4 kv heads: invalid
+    a.scale = 0.1
+    rc = lib.tq_decode_attn(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c),
+                            ctypes.byref(a), None, 0, None)
+    assert rc == _lib.TQ_ERR_INVALID and "multiple of Hkv" in _lib.last_error()
+    q.shape[1] = 8
+    a.num_q_heads = 8
+    a.n_tokens = 10_000                     # beyond 4 pages
+    rc = lib.tq_decode_attn(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c),
+                            ctypes.byref(a), None, 0, None)
+    assert rc == _lib.TQ_ERR_INVALID and "capacity" in _lib.last_error()
+
+
+def test_quantize_argument_validation():
+    lib = _lib.load()
+    rc = lib.tq_quantize_rotated(None, 10, None, 15, None, None)
+    assert rc == _lib.TQ_ERR_INVALID
+    rc = lib.tq_quantize_rotated(16, 10, 16, 300, 16, None)
+    assert rc == _lib.TQ_ERR_INVALID
