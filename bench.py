@@ -423,6 +423,49 @@ def bench_append(dev, args):
             "token_heads_per_s": th / (ms / 1e3), "algorithmic_bytes": alg}
 
 
+def run_profile(args):
+    """Small single-GPU cases for ncu captures (no JSON line):
+    --profile decode : one Mixtral layer (B16 Hkv8 T8192, K4+QJL/V2), 4 decode calls
+    --profile append : one prefill-append layer (B8 Hkv8 T4096 D128 4-bit), 4 calls
+    --profile step   : one layer's decode step (append 1 token + decode), 4 calls
+    """
+    import torch
+    from bhaskera_col_b200.inference import TurboQuantKVCache, ops
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    if args.profile == "append":
+        c = APPEND_CFG
+        cache = TurboQuantKVCache(num_layers=1, batch_size=c["B"], num_heads=c["H"],
+                                  head_dim=c["D"], key_bits=c["bits"], value_bits=c["bits"],
+                                  residual_window=0, protected_layers=0, device=dev,
+                                  max_seq_len=c["T"])
+        x = torch.randn((c["B"], c["H"], c["T"], c["D"]), device=dev,
+                        generator=gen).to(torch.bfloat16)
+        st = cache._stores[0]
+        st._lazy_alloc(c["B"], c["H"])
+        for _ in range(4):
+            ops.append(st.tables, st._pages, x, x, 0)
+        torch.cuda.synchronize()
+        return
+    cache = TurboQuantKVCache(num_layers=1, batch_size=B_PER_GPU, num_heads=HKV, head_dim=D,
+                              key_bits=KEY_BITS, value_bits=VALUE_BITS, residual_window=0,
+                              protected_layers=0, device=dev, max_seq_len=T_CTX + 64, qjl=QJL)
+    for c0 in range(0, T_CTX, 2048):
+        k = torch.randn((B_PER_GPU, HKV, 2048, D), device=dev, generator=gen).to(torch.bfloat16)
+        cache.append(k, k, 0)
+    q = torch.randn((B_PER_GPU, HQ, 1, D), device=dev, generator=gen).to(torch.bfloat16)
+    k1 = torch.randn((B_PER_GPU, HKV, 1, D), device=dev, generator=gen).to(torch.bfloat16)
+    st = cache._stores[0]
+    for _ in range(4):
+        if args.profile == "step":
+            ops.append(st.tables, st._pages, k1, k1, T_CTX)
+        ops.decode_attention(st.tables, st._pages, q, T_CTX + 1, workspace=st.workspace)
+    torch.cuda.synchronize()
+    if st.workspace.status() != 0:
+        raise RuntimeError("device status error")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -431,7 +474,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-append", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--profile", choices=["decode", "append", "step"], default=None,
+                    help="run a small single-layer case for ncu and exit")
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args)
+        return
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

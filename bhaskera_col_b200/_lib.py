@@ -46,7 +46,8 @@ class Geom(ctypes.Structure):
 class Tables(ctypes.Structure):
     _fields_ = [("k_centroids", ctypes.c_void_p), ("k_boundaries", ctypes.c_void_p),
                 ("v_centroids", ctypes.c_void_p), ("v_boundaries", ctypes.c_void_p),
-                ("rot", ctypes.c_void_p), ("qjl", ctypes.c_void_p)]
+                ("rot", ctypes.c_void_p), ("qjl", ctypes.c_void_p),
+                ("rot_t", ctypes.c_void_p), ("qjl_t", ctypes.c_void_p)]
 
 
 class Cache(ctypes.Structure):

@@ -36,8 +36,9 @@ struct AppendParams {
   PageGeom g;
   const float* cent[2];
   const float* bnd[2];
-  const float* R;
-  const float* S;
+  const float* RT;      // R^T row-major
+  const float* ST;      // S^T row-major (QJL)
+  int vt;               // vectors per tile (<= kVT)
   uint8_t* pages;
   int64_t pages_per_stream;
   const void* x[2];
@@ -71,11 +72,10 @@ append_kernel(AppendParams p) {
   int16_t* qinv = ord + D;                                    // [D] bit -> coord
 
   const int tid = threadIdx.x;
-  for (int i = tid; i < D * D; i += blockDim.x) {
-    int r = i / D, c = i % D;
-    RT[c * D + r] = p.R[i];                                   // RT[i][j] = R[j][i]
-    if (qjl) ST[c * D + r] = p.S[i];
-  }
+  // R^T (and S^T) as given, all 16-byte copies in flight at once
+  stage_async(RT, p.RT, D * D * 4, tid, blockDim.x);
+  if (qjl) stage_async(ST, p.ST, D * D * 4, tid, blockDim.x);
+  cp_async_wait_all();
   for (int i = tid; i < (1 << bits); i += blockDim.x) cb[i] = p.cent[which][i];
   for (int i = tid; i < nb; i += blockDim.x) bb[i] = p.bnd[which][i];
   for (int c = tid; c < D; c += blockDim.x) {
@@ -90,7 +90,8 @@ append_kernel(AppendParams p) {
   __syncthreads();
 
   const int64_t nvec = p.B * p.H * p.T;
-  const int64_t ntiles = (nvec + kVT - 1) / kVT;
+  const int vt = p.vt;
+  const int64_t ntiles = (nvec + vt - 1) / vt;
   const int lane = tid & 31, warp = tid >> 5;
   const int groups = kAppendThreads / D > 0 ? kAppendThreads / D : 1;
   const int rowbytes = which == 0 ? g.krow : g.vrow;
@@ -98,8 +99,8 @@ append_kernel(AppendParams p) {
   const int nsec = which == 0 ? g.off_kn : g.off_vn;
 
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int64_t v0 = tile * kVT;
-    const int nv = (int)tmin<int64_t>(kVT, nvec - v0);
+    const int64_t v0 = tile * vt;
+    const int nv = (int)tmin<int64_t>(vt, nvec - v0);
 
     // -- load + norm + normalise (one warp per vector) ----------------------
     for (int v = warp; v < nv; v += kAppendThreads / 32) {
@@ -281,7 +282,7 @@ int launch_append(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   p.g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
   p.cent[0] = t->k_centroids; p.cent[1] = t->v_centroids;
   p.bnd[0] = t->k_boundaries; p.bnd[1] = t->v_boundaries;
-  p.R = t->rot; p.S = t->qjl;
+  p.RT = t->rot_t; p.ST = t->qjl_t;
   p.pages = c->pages; p.pages_per_stream = c->pages_per_stream;
   p.x[0] = k->data; p.x[1] = v->data;
   p.dtype[0] = k->dtype; p.dtype[1] = v->dtype;
@@ -292,9 +293,14 @@ int launch_append(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   if (nvec == 0) return TQ_OK;
   const size_t smem = append_smem_bytes(p.g.D, p.g.qjl != 0);
   if (set_smem_attr((const void*)append_kernel, smem) != TQ_OK) return TQ_ERR_CUDA;
-  const int64_t tiles = (nvec + kVT - 1) / kVT;
   const int sms = device_sm_count();
-  dim3 grid((unsigned)tmin<int64_t>(tiles, (int64_t)sms * 2), 2);
+  const int occ = tmax(1, occupancy((const void*)append_kernel, kAppendThreads, smem));
+  // small appends (decode steps): few vectors per CTA so the grid fills the
+  // GPU; large appends: full tiles, persistent CTAs
+  const int64_t want = (nvec + (int64_t)sms * occ - 1) / ((int64_t)sms * occ);
+  p.vt = (int)tmax<int64_t>(1, tmin<int64_t>(kVT, 2 * want));
+  const int64_t tiles = (nvec + p.vt - 1) / p.vt;
+  dim3 grid((unsigned)tmin<int64_t>(tiles, (int64_t)sms * occ), 2);
   append_kernel<<<grid, kAppendThreads, smem, st>>>(p);
   return check_launch("tq_append");
 }

@@ -102,11 +102,17 @@ static int check_geom(const tq_geom* g, const char* fn) {
 }
 
 static int check_tables(const tq_geom* g, const tq_tables* t, const char* fn) {
-  if (!t || !t->k_centroids || !t->k_boundaries || !t->v_centroids || !t->v_boundaries || !t->rot) {
+  if (!t || !t->k_centroids || !t->k_boundaries || !t->v_centroids || !t->v_boundaries || !t->rot ||
+      !t->rot_t) {
     set_error("%s: a codebook or rotation table pointer is NULL", fn);
     return TQ_ERR_INVALID;
   }
-  if (g->qjl && !t->qjl) { set_error("%s: qjl enabled but the QJL matrix is NULL", fn); return TQ_ERR_INVALID; }
+  if (g->qjl && (!t->qjl || !t->qjl_t)) {
+    set_error("%s: qjl enabled but the QJL matrix is NULL", fn);
+    return TQ_ERR_INVALID;
+  }
+  const uintptr_t a = reinterpret_cast<uintptr_t>(t->rot_t) | reinterpret_cast<uintptr_t>(t->qjl_t);
+  if (a % 16) { set_error("%s: transposed tables must be 16-byte aligned", fn); return TQ_ERR_INVALID; }
   return TQ_OK;
 }
 
@@ -243,7 +249,7 @@ static int check_decode(const tq_geom* g, const tq_tables* t, const tq_cache* c,
       set_error("%s: window must be (B, Hkv, W, D)", fn);
       return TQ_ERR_INVALID;
     }
-    if (a->window_k->shape[2] > 4096) { set_error("%s: window longer than 4096 tokens", fn); return TQ_ERR_INVALID; }
+    if (a->window_k->shape[2] > 1024) { set_error("%s: window longer than 1024 tokens", fn); return TQ_ERR_INVALID; }
   }
   return TQ_OK;
 }

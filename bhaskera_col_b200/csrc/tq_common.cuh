@@ -151,6 +151,28 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---------------------------------------------------------------------------
+// cp.async staging of read-only tables (16-byte granules, all in flight at
+// once; the hardware wait needs no polling loop)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Copy `bytes` (a multiple of 16, both ends 16-byte aligned) into shared
+// memory cooperatively; caller synchronises the block afterwards.
+__device__ __forceinline__ void stage_async(void* dst, const void* src, int bytes, int tid,
+                                            int nthreads) {
+  char* d = static_cast<char*>(dst);
+  const char* s = static_cast<const char*>(src);
+  for (int off = tid * 16; off < bytes; off += nthreads * 16) cp_async16(d + off, s + off);
+}
+
+// ---------------------------------------------------------------------------
 // Tensor-core helpers (mma.sync m16n8k16 f16 -> f32, movmatrix)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4],

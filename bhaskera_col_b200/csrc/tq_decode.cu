@@ -16,12 +16,13 @@
 // Kernels per call:
 //   qprep_kernel   q_rot, S q_rot -> fp16 fragments (scale * log2e folded in)
 //   decode_kernel  persistent; each CTA owns a contiguous range of the
-//                  flattened (stream, page) space, streams 64-token pages
-//                  into shared memory with bulk async copies (no multicast),
-//                  dequantises codes into mma.sync fragments through
-//                  lane-replicated pair lookup tables, runs an online
-//                  softmax, and writes one partial (m, l, O_rot) per
-//                  (stream, head, CTA) it touches.
+//                  flattened (stream, page) space.  A producer warp streams
+//                  64-token pages into shared memory with bulk async copies
+//                  (no multicast) through full/empty mbarriers; four consumer
+//                  warps take 16 tokens of each page, dequantise codes
+//                  straight into mma.sync fragments through lane-replicated
+//                  pair lookup tables, and run an online softmax.  One partial
+//                  (m, l, O_rot) per (stream, head, CTA) touched.
 //   merge_kernel   combines the partials of each (stream, head), attends the
 //                  full-precision window, un-rotates, writes the output.
 #include "tq_common.cuh"
@@ -31,14 +32,13 @@
 
 namespace tq {
 
-constexpr int kDecThreads = 128;
-constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kConsumerWarps = 4;
+constexpr int kDecThreads = 32 * (kConsumerWarps + 1);   // + one producer warp
 constexpr int kStages = 4;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegInf = -INFINITY;
 
 struct DecodeParams {
-  PageGeom g;
   const uint8_t* pages;
   int64_t pages_per_stream;
   int64_t S, Pv, T, Q;
@@ -53,9 +53,49 @@ struct DecodeParams {
   uint32_t* status;
 };
 
+__host__ __device__ constexpr int align128(int x) { return (x + 127) & ~127; }
+__host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
 // ---------------------------------------------------------------------------
-// bit helpers (offsets become compile-time constants after unrolling)
+// lookup tables.  Pair tables (2 * bits <= 8): entry e = c_lo | c_hi << bits
+// holds half2(c[c_lo], c[c_hi]), replicated per lane so lane l reads bank l:
+// byte address (e << 7) | (lane << 2).  Wider codes use a plain fp16 table.
 // ---------------------------------------------------------------------------
+template <int BITS>
+struct Lut {
+  static constexpr bool kPair = 2 * BITS <= 8;
+  static constexpr int kBytes = kPair ? (1 << (2 * BITS)) * 128 : (1 << BITS) * 2;
+};
+
+template <int BITS>
+__device__ __forceinline__ void build_lut(unsigned char* base, const float* cent, int tid,
+                                          int nthreads) {
+  if constexpr (Lut<BITS>::kPair) {
+    uint32_t* lut = reinterpret_cast<uint32_t*>(base);
+    constexpr int E = 1 << (2 * BITS);
+    for (int i = tid; i < E * 32; i += nthreads) {
+      const int e = i >> 5;
+      lut[i] = pack_half2(__ldg(cent + (e & ((1 << BITS) - 1))), __ldg(cent + (e >> BITS)));
+    }
+  } else {
+    __half* h = reinterpret_cast<__half*>(base);
+    for (int i = tid; i < (1 << BITS); i += nthreads) h[i] = __float2half_rn(__ldg(cent + i));
+  }
+}
+
+// Byte offset (field << 7) | lane4 of the W-bit field starting at bit o of w[].
+template <int W, int NW>
+__device__ __forceinline__ uint32_t field_addr(const uint32_t (&w)[NW], int o, uint32_t lane4) {
+  const int wi = o >> 5, sh = o & 31;
+  uint32_t x;
+  if (sh + W <= 32 || wi + 1 >= NW) {
+    x = sh >= 7 ? (w[wi] >> (sh - 7)) : (w[wi] << (7 - sh));
+  } else {
+    x = __funnelshift_r(w[wi], w[wi + 1], sh) << 7;
+  }
+  return (x & (((1u << W) - 1u) << 7)) | lane4;
+}
+
 template <int NW>
 __device__ __forceinline__ uint32_t getbits(const uint32_t (&w)[NW], int o, int n) {
   const int wi = o >> 5, sh = o & 31;
@@ -65,13 +105,34 @@ __device__ __forceinline__ uint32_t getbits(const uint32_t (&w)[NW], int o, int 
   return v & ((1u << n) - 1u);
 }
 
-// Load NBITS bits starting at bit `bit_off` of a 4-byte aligned smem row.
+__device__ __forceinline__ uint32_t lds32(uint32_t byte_off) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  return *reinterpret_cast<const uint32_t*>(smem + byte_off);
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t byte_off) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  return *reinterpret_cast<const unsigned short*>(smem + byte_off);
+}
+
+// Load NBITS bits starting at bit `bit_off` of a 4-byte aligned shared row.
 template <int NBITS, bool ALIGNED>
 __device__ __forceinline__ void load_bits(const uint8_t* row, int bit_off,
                                           uint32_t (&w)[(NBITS + 31) / 32]) {
   constexpr int NW = (NBITS + 31) / 32;
   const uint32_t* p = reinterpret_cast<const uint32_t*>(row) + (bit_off >> 5);
-  if constexpr (ALIGNED) {
+  if constexpr (ALIGNED && NW % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < NW; i += 4) {
+      uint4 v = *reinterpret_cast<const uint4*>(p + i);
+      w[i] = v.x; w[i + 1] = v.y; w[i + 2] = v.z; w[i + 3] = v.w;
+    }
+  } else if constexpr (ALIGNED && NW % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < NW; i += 2) {
+      uint2 v = *reinterpret_cast<const uint2*>(p + i);
+      w[i] = v.x; w[i + 1] = v.y;
+    }
+  } else if constexpr (ALIGNED) {
 #pragma unroll
     for (int i = 0; i < NW; ++i) w[i] = p[i];
   } else {
@@ -86,61 +147,47 @@ __device__ __forceinline__ void load_bits(const uint8_t* row, int bit_off,
   }
 }
 
-// +-1 half2 from the two sign bits at positions pe (low half) and po (high).
+// +-1 half2 from the sign bits at positions pe (low half) and po (high half);
+// bit set <=> +1.
 __device__ __forceinline__ uint32_t sign_pair(uint32_t w, int pe, int po) {
-  if (po == pe + 16 && pe <= 15) return 0xBC00BC00u ^ ((w << (15 - pe)) & 0x80008000u);
+  if (po == pe + 16 && pe <= 15) return ((w << (15 - pe)) & 0x80008000u) ^ 0xBC00BC00u;
   uint32_t e = (w >> pe) & 1u, o = (w >> po) & 1u;
   return 0xBC00BC00u ^ ((e << 15) | (o << 31));
 }
 
-template <int BITS>
-struct Lut {
-  // pair tables for BITS <= 4: (1 << 2B) entries x 32 lanes of half2;
-  // single-code tables otherwise: (1 << B) halves.
-  static constexpr bool kPair = 2 * BITS <= 8;
-  static constexpr int kWords = kPair ? (1 << (2 * BITS)) * 32 : ((1 << BITS) + 1) / 2;
-};
-
-template <int BITS>
-__device__ __forceinline__ void build_lut(uint32_t* lut, const float* cent) {
-  if constexpr (Lut<BITS>::kPair) {
-    constexpr int E = 1 << (2 * BITS);
-    for (int i = threadIdx.x; i < E * 32; i += blockDim.x) {
-      int e = i >> 5;
-      lut[i] = pack_half2(cent[e & ((1 << BITS) - 1)], cent[e >> BITS]);
-    }
-  } else {
-    __half* h = reinterpret_cast<__half*>(lut);
-    for (int i = threadIdx.x; i < (1 << BITS); i += blockDim.x) h[i] = __float2half_rn(cent[i]);
-  }
+__device__ __forceinline__ void named_bar(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// half2 of the codes (c_lo, c_hi)
-template <int BITS>
-__device__ __forceinline__ uint32_t lut_pair(const uint32_t* lut, uint32_t c_lo, uint32_t c_hi,
-                                             int lane) {
-  if constexpr (Lut<BITS>::kPair) {
-    return lut[(((c_hi << BITS) | c_lo) << 5) + lane];
-  } else {
-    const unsigned short* h = reinterpret_cast<const unsigned short*>(lut);
-    return (uint32_t)h[c_lo] | ((uint32_t)h[c_hi] << 16);
-  }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // ---------------------------------------------------------------------------
 // decode kernel
 // ---------------------------------------------------------------------------
 template <int D, int KB, int VB, bool QJL>
-struct DecSmem {
-  static constexpr int kLutK = Lut<KB>::kWords;
-  static constexpr int kLutV = Lut<VB>::kWords;
-  static constexpr int kComb = kDecWarps * (16 + 8 * D);
+struct Dec {
+  // page geometry (compile time; matches make_geom)
+  static constexpr int KROW = D * KB / 8, VROW = D * VB / 8, QROW = QJL ? D / 8 : 0;
+  static constexpr int OFF_V = 64 * KROW, OFF_Q = OFF_V + 64 * VROW;
+  static constexpr int OFF_KN = OFF_Q + 64 * QROW, OFF_VN = OFF_KN + 128, OFF_KR = OFF_VN + 128;
+  static constexpr int PAGE = OFF_KR + (QJL ? 128 : 0);
+  static constexpr int PB = align128(PAGE);
+  // shared memory map: [K table | combine scratch] [V table] [stages] [barriers]
+  static constexpr int COMB = kConsumerWarps * (16 + 8 * D) * 4;
+  static constexpr int REGION0 = align128(cmax(Lut<KB>::kBytes, COMB));
+  static constexpr int LUTV = REGION0;
+  static constexpr int STAGE0 = align128(LUTV + Lut<VB>::kBytes);
+  static constexpr int BARS = STAGE0 + kStages * PB;
+  static constexpr int SMEM = BARS + 2 * kStages * 8;
 };
 
 template <int D, int KB, int VB, bool QJL>
-__global__ void __launch_bounds__(kDecThreads)
+__global__ void __launch_bounds__(kDecThreads, 3)
 decode_kernel(DecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
+  using G = Dec<D, KB, VB, QJL>;
   constexpr int NJ = D / 16;                 // 16-coordinate chunks
   constexpr int KQB = (D / 4) * KB;          // bits per K quad
   constexpr int KQW = (KQB + 31) / 32;
@@ -151,48 +198,63 @@ decode_kernel(DecodeParams p) {
   constexpr int QQB = D / 4;                 // QJL bits per quad
   constexpr int QQW = (QQB + 31) / 32;
   constexpr int SP = (D / 8) < 16 ? (D / 8) : 16;
-  using SM = DecSmem<D, KB, VB, QJL>;
+  constexpr bool VINTER = Lut<VB>::kPair && (32 % VB == 0) && VOA;
 
-  const PageGeom& g = p.g;
-  const int pb = (g.page_bytes + 127) & ~127;
-  uint8_t* stage_buf = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * pb);
-  uint32_t* lutK = reinterpret_cast<uint32_t*>(full + kStages);
-  uint32_t* lutV = lutK + SM::kLutK;
-  float* comb = reinterpret_cast<float*>(lutV + SM::kLutV);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::BARS);
+  uint64_t* empty = full + kStages;
   __shared__ int s_abort;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int gq = lane >> 2, tq = lane & 3;
   const int hc = blockIdx.y;
-
   const int64_t TP = p.S * p.Pv;
   const int64_t gp0 = (int64_t)blockIdx.x * p.Q;
   const int64_t gp1 = tmin<int64_t>(gp0 + p.Q, TP);
   const int npages = (int)tmax<int64_t>(0, gp1 - gp0);
+  constexpr int NCT = 32 * kConsumerWarps;   // consumer threads
 
-  build_lut<KB>(lutK, p.kc);
-  build_lut<VB>(lutV, p.vc);
   if (tid == 0) {
     s_abort = 0;
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
     fence_mbar_init();
+  }
+  if (warp < kConsumerWarps) {
+    build_lut<KB>(smem, p.kc, tid, NCT);
+    build_lut<VB>(smem + G::LUTV, p.vc, tid, NCT);
   }
   __syncthreads();
 
-  auto issue = [&](int i) {
-    const int64_t gp = gp0 + i;
-    const int64_t s = gp / p.Pv, pg = gp % p.Pv;
-    const uint8_t* src = p.pages + (s * p.pages_per_stream + pg) * (int64_t)g.page_bytes;
-    uint64_t* bar = &full[i % kStages];
-    mbar_expect_tx(bar, (uint32_t)g.page_bytes);
-    bulk_g2s(stage_buf + (i % kStages) * pb, src, (uint32_t)g.page_bytes, bar);
-  };
-  if (tid == 0) {
-    for (int i = 0; i < kStages && i < npages; ++i) issue(i);
+  // ------------------------------------------------------------ producer
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      int64_t s = gp0 / p.Pv, pg = gp0 - s * p.Pv;
+      for (int i = 0; i < npages; ++i) {
+        const int st = i % kStages;
+        if (i >= kStages && !s_abort) {
+          if (!mbar_wait_bounded(&empty[st], (uint32_t)(((i / kStages) - 1) & 1))) {
+            atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
+            s_abort = 1;
+          }
+        }
+        if (s_abort) break;
+        const uint8_t* src = p.pages + (s * p.pages_per_stream + pg) * (int64_t)G::PAGE;
+        if (++pg == p.Pv) { pg = 0; ++s; }
+        mbar_expect_tx(&full[st], (uint32_t)G::PAGE);
+        bulk_g2s(smem + G::STAGE0 + st * G::PB, src, (uint32_t)G::PAGE, &full[st]);
+      }
+      if (s_abort) {   // never leave with a copy still writing shared memory
+        for (int i = tmax(0, npages - kStages); i < npages; ++i)
+          mbar_wait_bounded(&full[i % kStages], (uint32_t)((i / kStages) & 1), 1u << 16);
+      }
+    }
+    return;
   }
 
-  // per-thread state
+  // ------------------------------------------------------------ consumers
+  const int gq = lane >> 2, tq = lane & 3;
+  const uint32_t lane4 = (uint32_t)lane << 2;
   uint32_t qf[NJ][2], sqf[NJ][2];
   float O[NJ][4];
   float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
@@ -208,73 +270,79 @@ decode_kernel(DecodeParams p) {
     const uint32_t* sb = p.sqf + ((s * p.nch + hc) * 8 + gq) * (D / 2);
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
-      qf[j][0] = qb[8 * j + tq];
-      qf[j][1] = qb[8 * j + tq + 4];
+      qf[j][0] = __ldg(qb + 8 * j + tq);
+      qf[j][1] = __ldg(qb + 8 * j + tq + 4);
       if constexpr (QJL) {
-        sqf[j][0] = sb[8 * j + tq];
-        sqf[j][1] = sb[8 * j + tq + 4];
+        sqf[j][0] = __ldg(sb + 8 * j + tq);
+        sqf[j][1] = __ldg(sb + 8 * j + tq + 4);
       }
     }
   };
   reset_state();
 
-  for (int i = 0; i < npages; ++i) {
-    const int64_t gp = gp0 + i;
-    const int64_t s = gp / p.Pv, pg = gp % p.Pv;
+  int64_t s = gp0 / p.Pv, pg = gp0 - s * p.Pv;   // advanced incrementally below
+  for (int i = 0; i < npages; ++i, ++pg) {
+    if (pg == p.Pv) { pg = 0; ++s; }
+    const int st = i % kStages;
     if (s != cur_s) { load_q(s); cur_s = s; }
-
-    if (!mbar_wait_bounded(&full[i % kStages], (uint32_t)((i / kStages) & 1))) {
+    if (!s_abort && !mbar_wait_bounded(&full[st], (uint32_t)((i / kStages) & 1))) {
       atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
       s_abort = 1;
     }
-    const uint8_t* pgb = stage_buf + (i % kStages) * pb;
+    const uint8_t* pgb = smem + G::STAGE0 + st * G::PB;
     const int64_t tok0 = pg * kPageTokens + warp * 16;
 
     if (tok0 < p.T) {
       // ---------------- scores: S^T tile (16 tokens x 8 heads) --------------
       const int r0 = warp * 16 + gq, r1 = r0 + 8;
       uint32_t wk0[KQW], wk1[KQW];
-      load_bits<KQB, KQA>(pgb + g.off_k + r0 * g.krow, tq * KQB, wk0);
-      load_bits<KQB, KQA>(pgb + g.off_k + r1 * g.krow, tq * KQB, wk1);
+      load_bits<KQB, KQA>(pgb + r0 * G::KROW, tq * KQB, wk0);
+      load_bits<KQB, KQA>(pgb + r1 * G::KROW, tq * KQB, wk1);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       float acc2[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t wq0[QQW], wq1[QQW];
       if constexpr (QJL) {
-        load_bits<QQB, (QQB % 32) == 0>(pgb + g.off_q + r0 * g.qrow, tq * QQB, wq0);
-        load_bits<QQB, (QQB % 32) == 0>(pgb + g.off_q + r1 * g.qrow, tq * QQB, wq1);
+        load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r0 * G::QROW, tq * QQB, wq0);
+        load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r1 * G::QROW, tq * QQB, wq1);
       }
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
         uint32_t a[4];
-        const int e0 = 4 * j;   // quad entries 4j..4j+3
-        a[0] = lut_pair<KB>(lutK, getbits(wk0, e0 * KB, KB), getbits(wk0, (e0 + 1) * KB, KB), lane);
-        a[1] = lut_pair<KB>(lutK, getbits(wk1, e0 * KB, KB), getbits(wk1, (e0 + 1) * KB, KB), lane);
-        a[2] = lut_pair<KB>(lutK, getbits(wk0, (e0 + 2) * KB, KB), getbits(wk0, (e0 + 3) * KB, KB), lane);
-        a[3] = lut_pair<KB>(lutK, getbits(wk1, (e0 + 2) * KB, KB), getbits(wk1, (e0 + 3) * KB, KB), lane);
+        const int o0 = (4 * j) * KB, o1 = (4 * j + 2) * KB;   // quad entries 4j.., 4j+2..
+        if constexpr (Lut<KB>::kPair) {
+          a[0] = lds32(field_addr<2 * KB>(wk0, o0, lane4));
+          a[1] = lds32(field_addr<2 * KB>(wk1, o0, lane4));
+          a[2] = lds32(field_addr<2 * KB>(wk0, o1, lane4));
+          a[3] = lds32(field_addr<2 * KB>(wk1, o1, lane4));
+        } else {
+          a[0] = lds16(getbits(wk0, o0, KB) << 1) | (lds16(getbits(wk0, o0 + KB, KB) << 1) << 16);
+          a[1] = lds16(getbits(wk1, o0, KB) << 1) | (lds16(getbits(wk1, o0 + KB, KB) << 1) << 16);
+          a[2] = lds16(getbits(wk0, o1, KB) << 1) | (lds16(getbits(wk0, o1 + KB, KB) << 1) << 16);
+          a[3] = lds16(getbits(wk1, o1, KB) << 1) | (lds16(getbits(wk1, o1 + KB, KB) << 1) << 16);
+        }
         mma_f16_16816(acc, a, qf[j][0], qf[j][1]);
         if constexpr (QJL) {
           uint32_t b[4];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int pr = 2 * j + h;                 // pair index in quad
+            const int pr = 2 * j + h;                 // pair index in the quad
             const int ch = pr / SP, pin = pr % SP;
             const int pe = ch * 2 * SP + pin, po = pe + SP;
             const int wi = pe >> 5;
             b[2 * h + 0] = sign_pair(wq0[wi], pe & 31, po - (wi << 5));
             b[2 * h + 1] = sign_pair(wq1[wi], pe & 31, po - (wi << 5));
           }
-          uint32_t aq[4] = {b[0], b[1], b[2], b[3]};
-          mma_f16_16816(acc2, aq, sqf[j][0], sqf[j][1]);
+          mma_f16_16816(acc2, b, sqf[j][0], sqf[j][1]);
         }
       }
-      const __half* kn = reinterpret_cast<const __half*>(pgb + g.off_kn);
-      const __half* vn = reinterpret_cast<const __half*>(pgb + g.off_vn);
+      const __half* kn = reinterpret_cast<const __half*>(pgb + G::OFF_KN);
+      const __half* vn = reinterpret_cast<const __half*>(pgb + G::OFF_VN);
       const bool ok0 = tok0 + gq < p.T, ok1 = tok0 + gq + 8 < p.T;
-      float n0 = __half2float(kn[r0]), n1 = __half2float(kn[r1]);
+      const float n0 = __half2float(kn[r0]), n1 = __half2float(kn[r1]);
       float s00 = acc[0] * n0, s01 = acc[1] * n0, s10 = acc[2] * n1, s11 = acc[3] * n1;
       if constexpr (QJL) {
-        const __half* kr = reinterpret_cast<const __half*>(pgb + g.off_kr);
-        float g0 = __half2float(kr[r0]), g1 = __half2float(kr[r1]);
+        const __half* kr = reinterpret_cast<const __half*>(pgb + G::OFF_KR);
+        const float g0 = __half2float(kr[r0]), g1 = __half2float(kr[r1]);
         s00 = fmaf(acc2[0], g0, s00); s01 = fmaf(acc2[1], g0, s01);
         s10 = fmaf(acc2[2], g1, s10); s11 = fmaf(acc2[3], g1, s11);
       }
@@ -288,18 +356,25 @@ decode_kernel(DecodeParams p) {
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
       }
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float b0s = mn0 == kNegInf ? 0.f : mn0, b1s = mn1 == kNegInf ? 0.f : mn1;
-      const float c0 = fast_exp2(m0 - b0s), c1 = fast_exp2(m1 - b1s);
+      if (mx0 > m0) {            // rescale only when the running max grows
+        const float c = fast_exp2(m0 - mx0);
+        l0 *= c;
+#pragma unroll
+        for (int i2 = 0; i2 < NJ; ++i2) { O[i2][0] *= c; O[i2][2] *= c; }
+        m0 = mx0;
+      }
+      if (mx1 > m1) {
+        const float c = fast_exp2(m1 - mx1);
+        l1 *= c;
+#pragma unroll
+        for (int i2 = 0; i2 < NJ; ++i2) { O[i2][1] *= c; O[i2][3] *= c; }
+        m1 = mx1;
+      }
+      const float b0s = m0 == kNegInf ? 0.f : m0, b1s = m1 == kNegInf ? 0.f : m1;
       const float p00 = fast_exp2(s00 - b0s), p01 = fast_exp2(s01 - b1s);
       const float p10 = fast_exp2(s10 - b0s), p11 = fast_exp2(s11 - b1s);
-      l0 = fmaf(l0, c0, p00 + p10);
-      l1 = fmaf(l1, c1, p01 + p11);
-      m0 = mn0; m1 = mn1;
-#pragma unroll
-      for (int i2 = 0; i2 < NJ; ++i2) {
-        O[i2][0] *= c0; O[i2][1] *= c1; O[i2][2] *= c0; O[i2][3] *= c1;
-      }
+      l0 += p00 + p10;
+      l1 += p01 + p11;
 
       // ---------------- P' = p * ||v|| -> B fragments -----------------------
       const float v0 = ok0 ? __half2float(vn[r0]) : 0.f;
@@ -310,19 +385,52 @@ decode_kernel(DecodeParams p) {
       // ---------------- O^T += V^T P ----------------------------------------
       const int t0r = warp * 16 + 2 * tq;
       uint32_t wa[VOW], wb[VOW], wc[VOW], wd[VOW];
-      load_bits<VOB, VOA>(pgb + g.off_v + (t0r + 0) * g.vrow, gq * VOB, wa);
-      load_bits<VOB, VOA>(pgb + g.off_v + (t0r + 1) * g.vrow, gq * VOB, wb);
-      load_bits<VOB, VOA>(pgb + g.off_v + (t0r + 8) * g.vrow, gq * VOB, wc);
-      load_bits<VOB, VOA>(pgb + g.off_v + (t0r + 9) * g.vrow, gq * VOB, wd);
+      load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 0) * G::VROW, gq * VOB, wa);
+      load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 1) * G::VROW, gq * VOB, wb);
+      load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 8) * G::VROW, gq * VOB, wc);
+      load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 9) * G::VROW, gq * VOB, wd);
+      if constexpr (VINTER) {
+        // combine the two tokens of each pair word-wise: field c of lo/hi is
+        // (code of token a) | (code of token b) << VB
+        constexpr uint32_t M = VB == 1 ? 0x55555555u : VB == 2 ? 0x33333333u : 0x0F0F0F0Fu;
+        uint32_t lab[VOW], hab[VOW], lcd[VOW], hcd[VOW];
 #pragma unroll
-      for (int i2 = 0; i2 < NJ; ++i2) {
-        uint32_t a[4];
-        const int c0p = (2 * i2) * VB, c1p = (2 * i2 + 1) * VB;
-        a[0] = lut_pair<VB>(lutV, getbits(wa, c0p, VB), getbits(wb, c0p, VB), lane);
-        a[1] = lut_pair<VB>(lutV, getbits(wa, c1p, VB), getbits(wb, c1p, VB), lane);
-        a[2] = lut_pair<VB>(lutV, getbits(wc, c0p, VB), getbits(wd, c0p, VB), lane);
-        a[3] = lut_pair<VB>(lutV, getbits(wc, c1p, VB), getbits(wd, c1p, VB), lane);
-        mma_f16_16816(O[i2], a, pb0, pb1);
+        for (int x = 0; x < VOW; ++x) {
+          lab[x] = (wa[x] & M) | ((wb[x] << VB) & ~M);
+          hab[x] = ((wa[x] >> VB) & M) | (wb[x] & ~M);
+          lcd[x] = (wc[x] & M) | ((wd[x] << VB) & ~M);
+          hcd[x] = ((wc[x] >> VB) & M) | (wd[x] & ~M);
+        }
+        constexpr int PER = 32 / VB;                 // codes per word
+#pragma unroll
+        for (int i2 = 0; i2 < NJ; ++i2) {
+          const int c0 = 2 * i2;                     // even position -> lo, odd -> hi
+          const int o = ((c0 % PER) & ~1) * VB + (c0 / PER) * 32;
+          uint32_t a[4];
+          a[0] = lds32(G::LUTV + field_addr<2 * VB>(lab, o, lane4));
+          a[1] = lds32(G::LUTV + field_addr<2 * VB>(hab, o, lane4));
+          a[2] = lds32(G::LUTV + field_addr<2 * VB>(lcd, o, lane4));
+          a[3] = lds32(G::LUTV + field_addr<2 * VB>(hcd, o, lane4));
+          mma_f16_16816(O[i2], a, pb0, pb1);
+        }
+      } else {
+#pragma unroll
+        for (int i2 = 0; i2 < NJ; ++i2) {
+          const int c0p = (2 * i2) * VB, c1p = (2 * i2 + 1) * VB;
+          uint32_t a[4];
+          if constexpr (Lut<VB>::kPair) {
+            a[0] = lds32(G::LUTV + (((getbits(wb, c0p, VB) << VB) | getbits(wa, c0p, VB)) << 7 | lane4));
+            a[1] = lds32(G::LUTV + (((getbits(wb, c1p, VB) << VB) | getbits(wa, c1p, VB)) << 7 | lane4));
+            a[2] = lds32(G::LUTV + (((getbits(wd, c0p, VB) << VB) | getbits(wc, c0p, VB)) << 7 | lane4));
+            a[3] = lds32(G::LUTV + (((getbits(wd, c1p, VB) << VB) | getbits(wc, c1p, VB)) << 7 | lane4));
+          } else {
+            a[0] = lds16(G::LUTV + (getbits(wa, c0p, VB) << 1)) | (lds16(G::LUTV + (getbits(wb, c0p, VB) << 1)) << 16);
+            a[1] = lds16(G::LUTV + (getbits(wa, c1p, VB) << 1)) | (lds16(G::LUTV + (getbits(wb, c1p, VB) << 1)) << 16);
+            a[2] = lds16(G::LUTV + (getbits(wc, c0p, VB) << 1)) | (lds16(G::LUTV + (getbits(wd, c0p, VB) << 1)) << 16);
+            a[3] = lds16(G::LUTV + (getbits(wc, c1p, VB) << 1)) | (lds16(G::LUTV + (getbits(wd, c1p, VB) << 1)) << 16);
+          }
+          mma_f16_16816(O[i2], a, pb0, pb1);
+        }
       }
     }
 
@@ -335,6 +443,8 @@ decode_kernel(DecodeParams p) {
         L0 += __shfl_xor_sync(0xffffffffu, L0, o);
         L1 += __shfl_xor_sync(0xffffffffu, L1, o);
       }
+      named_bar(1, NCT);                       // everyone is done with the K table
+      float* comb = reinterpret_cast<float*>(smem);
       float* cm = comb + warp * (16 + 8 * D);
       float* cl = cm + 8;
       float* co = cm + 16;
@@ -349,18 +459,18 @@ decode_kernel(DecodeParams p) {
         co[(2 * tq) * D + 16 * i2 + gq + 8] = O[i2][2];
         co[(2 * tq + 1) * D + 16 * i2 + gq + 8] = O[i2][3];
       }
-      __syncthreads();
+      named_bar(1, NCT);
       const int64_t first = (s * p.Pv) / p.Q;
       const int slot = (int)(blockIdx.x - first);
-      for (int idx = tid; idx < 8 * D; idx += kDecThreads) {
+      for (int idx = tid; idx < 8 * D; idx += NCT) {
         const int h = idx / D, d = idx % D;
         float M = kNegInf;
 #pragma unroll
-        for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, comb[w * (16 + 8 * D) + h]);
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, comb[w * (16 + 8 * D) + h]);
         float Lsum = 0.f, Osum = 0.f;
         if (M != kNegInf) {
 #pragma unroll
-          for (int w = 0; w < kDecWarps; ++w) {
+          for (int w = 0; w < kConsumerWarps; ++w) {
             const float* cw = comb + w * (16 + 8 * D);
             const float wt = fast_exp2(cw[h] - M);
             Lsum = fmaf(wt, cw[8 + h], Lsum);
@@ -374,29 +484,27 @@ decode_kernel(DecodeParams p) {
           p.part_l[hrow * p.maxslot + slot] = Lsum;
         }
       }
+      named_bar(1, NCT);
+      if (i != npages - 1) {                   // restore the K table
+        build_lut<KB>(smem, p.kc, tid, NCT);
+        named_bar(1, NCT);
+      }
       reset_state();
     }
-    __syncthreads();
-    if (s_abort) break;
-    if (tid == 0 && i + kStages < npages) issue(i + kStages);
-  }
-  // Drain: make sure no bulk copy is still writing this CTA's shared memory.
-  if (s_abort && tid == 0) {
-    for (int i = 0; i < npages && i < kStages; ++i) {
-      // bounded; a copy that never lands leaves the status flag set
-      mbar_wait_bounded(&full[i], 0u, 1u << 16);
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
   }
 }
 
 // ---------------------------------------------------------------------------
 // query preparation: q_rot = q R^T, sq = S q_rot, scaled, packed to half2
-// grid = (S, nch), 128 threads
+// grid = (S, nch), 128 threads; thread j owns output coordinate j of all 8
+// heads so R^T and S^T are each read once per CTA, coalesced.
 // ---------------------------------------------------------------------------
 struct QPrepParams {
   int D, g, Hkv, nch;
   const void* q; int q_dtype; int64_t q_stride[4];
-  const float* R; const float* Sm;
+  const float* RT; const float* ST;   // R^T, S^T (row-major)
   float scale_q, scale_s;
   uint32_t* qf; uint32_t* sqf;
 };
@@ -404,27 +512,37 @@ struct QPrepParams {
 __global__ void __launch_bounds__(128) qprep_kernel(QPrepParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int D = p.D;
-  float* qs = reinterpret_cast<float*>(smem);   // [8][D]
+  float* rt = reinterpret_cast<float*>(smem);   // [D][D] R^T
+  float* stt = rt + D * D;                       // [D][D] S^T (QJL only)
+  float* qs = stt + (p.ST ? D * D : 0);          // [8][D]
   float* qr = qs + 8 * D;                        // [8][D]
   const int64_t s = blockIdx.x;
   const int hc = blockIdx.y;
   const int64_t b = s / p.Hkv, kvh = s % p.Hkv;
+  const int nh = tmin(8, p.g - hc * 8);
+  stage_async(rt, p.RT, D * D * 4, threadIdx.x, blockDim.x);
+  if (p.ST) stage_async(stt, p.ST, D * D * 4, threadIdx.x, blockDim.x);
   for (int i = threadIdx.x; i < 8 * D; i += blockDim.x) {
     const int hl = i / D, c = i % D;
-    const int hg = hc * 8 + hl;
     float v = 0.f;
-    if (hg < p.g) {
-      const int64_t hq = kvh * p.g + hg;
+    if (hl < nh) {
+      const int64_t hq = kvh * p.g + hc * 8 + hl;
       v = load_elem(p.q, p.q_dtype, b * p.q_stride[0] + hq * p.q_stride[1] + c * p.q_stride[3]);
     }
     qs[i] = v;
   }
+  cp_async_wait_all();
   __syncthreads();
-  for (int i = threadIdx.x; i < 8 * D; i += blockDim.x) {
-    const int hl = i / D, j = i % D;
-    float acc = 0.f;
-    for (int k = 0; k < D; ++k) acc = fmaf(qs[hl * D + k], __ldg(p.R + j * D + k), acc);
-    qr[i] = acc;
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int k = 0; k < D; ++k) {
+      const float r = rt[k * D + j];
+#pragma unroll
+      for (int h = 0; h < 8; ++h) acc[h] = fmaf(qs[h * D + k], r, acc[h]);
+    }
+#pragma unroll
+    for (int h = 0; h < 8; ++h) qr[h * D + j] = acc[h];
   }
   __syncthreads();
   uint32_t* qo = p.qf + (s * p.nch + hc) * 8 * (D / 2);
@@ -432,12 +550,18 @@ __global__ void __launch_bounds__(128) qprep_kernel(QPrepParams p) {
     const int hl = i / (D / 2), c2 = i % (D / 2);
     qo[i] = pack_half2(qr[hl * D + 2 * c2] * p.scale_q, qr[hl * D + 2 * c2 + 1] * p.scale_q);
   }
-  if (p.Sm) {
-    for (int i = threadIdx.x; i < 8 * D; i += blockDim.x) {
-      const int hl = i / D, j = i % D;
-      float acc = 0.f;
-      for (int k = 0; k < D; ++k) acc = fmaf(qr[hl * D + k], __ldg(p.Sm + j * D + k), acc);
-      qs[i] = acc;
+  if (p.ST) {
+    // sq -> qs (q itself is no longer needed)
+    for (int j = threadIdx.x; j < D; j += blockDim.x) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int k = 0; k < D; ++k) {
+        const float r = stt[k * D + j];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) acc[h] = fmaf(qr[h * D + k], r, acc[h]);
+      }
+#pragma unroll
+      for (int h = 0; h < 8; ++h) qs[h * D + j] = acc[h];
     }
     __syncthreads();
     uint32_t* so = p.sqf + (s * p.nch + hc) * 8 * (D / 2);
@@ -463,102 +587,119 @@ struct MergeParams {
   void* out; int out_dtype; int64_t out_stride[4];
 };
 
+constexpr int kMaxSlots = 64;
+
 __global__ void __launch_bounds__(128) merge_kernel(MergeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int D = p.D;
-  float* orot = reinterpret_cast<float*>(smem);   // [D]
-  float* qv = orot + D;                            // [D]
-  float* ow = qv + D;                              // [D]
-  float* sc = ow + D;                              // [W]
-  __shared__ float s_red[32];
-  __shared__ float s_stats[4];
+  const int64_t W = p.W;
+  float* rs = reinterpret_cast<float*>(smem);     // [D][D] R
+  float* orot = rs + D * D;                        // [8][D]
+  float* qv = orot + 8 * D;                        // [8][D]  (window only)
+  float* sc = qv + 8 * D;                          // [8][W]  (window only)
+  __shared__ float s_wt[8][kMaxSlots];
+  __shared__ float s_M[8], s_L[8];
   const int64_t s = blockIdx.x;
   const int hc = blockIdx.y;
   const int64_t b = s / p.Hkv, kvh = s % p.Hkv;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nh = tmin(8, p.g - hc * 8);
   int nslot = 0;
   if (p.Pv > 0) {
     const int64_t first = (s * p.Pv) / p.Q, last = ((s + 1) * p.Pv - 1) / p.Q;
     nslot = (int)(last - first + 1);
   }
-  for (int hl = 0; hl < 8 && hc * 8 + hl < p.g; ++hl) {
-    const int64_t hq = kvh * p.g + hc * 8 + hl;
-    const int64_t hrow = (s * p.nch + hc) * 8 + hl;
-    // --- window scores (unrotated) -----------------------------------------
-    float mw = -INFINITY;
-    if (p.W > 0) {
-      for (int c = tid; c < D; c += blockDim.x)
-        qv[c] = load_elem(p.q, p.q_dtype, b * p.q_stride[0] + hq * p.q_stride[1] + c * p.q_stride[3]);
-      __syncthreads();
-      const int warp = tid >> 5, lane = tid & 31;
-      for (int64_t t = warp; t < p.W; t += blockDim.x / 32) {
-        float acc = 0.f;
-        for (int c = lane; c < D; c += 32)
-          acc = fmaf(qv[c], load_elem(p.wk, p.w_dtype, b * p.wk_stride[0] + kvh * p.wk_stride[1] +
-                                                         t * p.wk_stride[2] + c * p.wk_stride[3]), acc);
-        acc = warp_sum(acc);
-        if (lane == 0) sc[t] = acc * p.scale_log2;
-      }
-      __syncthreads();
-      float mloc = -INFINITY;
-      for (int64_t t = tid; t < p.W; t += blockDim.x) mloc = fmaxf(mloc, sc[t]);
-      for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
-      if ((tid & 31) == 0) s_red[tid >> 5] = mloc;
-      __syncthreads();
-      if (tid == 0) {
-        float m = -INFINITY;
-        for (int w = 0; w < (int)(blockDim.x / 32); ++w) m = fmaxf(m, s_red[w]);
-        s_stats[0] = m;
-      }
-      __syncthreads();
-      mw = s_stats[0];
+  const int64_t hrow0 = (s * p.nch + hc) * 8;
+  stage_async(rs, p.R, D * D * 4, tid, blockDim.x);
+
+  // --- window scores (unrotated), all heads --------------------------------
+  if (W > 0) {
+    for (int i = tid; i < 8 * D; i += blockDim.x) {
+      const int hl = i / D, c = i % D;
+      qv[i] = hl < nh ? load_elem(p.q, p.q_dtype, b * p.q_stride[0] +
+                                  (kvh * p.g + hc * 8 + hl) * p.q_stride[1] + c * p.q_stride[3])
+                      : 0.f;
     }
-    // --- global max ----------------------------------------------------------
-    float M = mw;
-    for (int k = 0; k < nslot; ++k) M = fmaxf(M, p.part_m[hrow * p.maxslot + k]);
-    const float Ms = (M == -INFINITY) ? 0.f : M;
-    // --- rotated partial combination ---------------------------------------
+    __syncthreads();
+    for (int64_t t = warp; t < W; t += blockDim.x / 32) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int c = lane; c < D; c += 32) {
+        const float kx = load_elem(p.wk, p.w_dtype, b * p.wk_stride[0] + kvh * p.wk_stride[1] +
+                                                        t * p.wk_stride[2] + c * p.wk_stride[3]);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) acc[h] = fmaf(qv[h * D + c], kx, acc[h]);
+      }
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        const float v = warp_sum(acc[h]);
+        if (lane == 0) sc[h * W + t] = v * p.scale_log2;
+      }
+    }
+    __syncthreads();
+  }
+  // --- per-head max, partial weights, denominators --------------------------
+  if (tid < 8) {
+    const int h = tid;
+    float M = kNegInf;
+    if (h < nh) {
+      for (int k = 0; k < nslot; ++k) M = fmaxf(M, p.part_m[(hrow0 + h) * p.maxslot + k]);
+      for (int64_t t = 0; t < W; ++t) M = fmaxf(M, sc[h * W + t]);
+    }
+    const float Ms = M == kNegInf ? 0.f : M;
     float L = 0.f;
     for (int k = 0; k < nslot; ++k) {
-      const float mk = p.part_m[hrow * p.maxslot + k];
-      if (mk != -INFINITY) L = fmaf(exp2f(mk - Ms), p.part_l[hrow * p.maxslot + k], L);
+      const float mk = p.part_m[(hrow0 + h) * p.maxslot + k];
+      const float wt = (h < nh && mk != kNegInf) ? exp2f(mk - Ms) : 0.f;
+      s_wt[h][k] = wt;
+      L = fmaf(wt, p.part_l[(hrow0 + h) * p.maxslot + k], L);
     }
-    for (int d = tid; d < D; d += blockDim.x) {
-      float acc = 0.f;
-      for (int k = 0; k < nslot; ++k) {
-        const float mk = p.part_m[hrow * p.maxslot + k];
-        if (mk != -INFINITY)
-          acc = fmaf(exp2f(mk - Ms), p.part_o[(hrow * p.maxslot + k) * D + d], acc);
-      }
-      orot[d] = acc;
-    }
-    // --- window contribution (unrotated) -----------------------------------
-    float lw = 0.f;
-    for (int d = tid; d < D; d += blockDim.x) ow[d] = 0.f;
-    __syncthreads();
-    if (p.W > 0) {
-      for (int64_t t = tid; t < p.W; t += blockDim.x) sc[t] = exp2f(sc[t] - Ms);
-      __syncthreads();
-      for (int64_t t = 0; t < p.W; ++t) lw += sc[t];
-      for (int d = tid; d < D; d += blockDim.x) {
-        float acc = 0.f;
-        for (int64_t t = 0; t < p.W; ++t)
-          acc = fmaf(sc[t], load_elem(p.wv, p.w_dtype, b * p.wv_stride[0] + kvh * p.wv_stride[1] +
-                                                        t * p.wv_stride[2] + d * p.wv_stride[3]), acc);
-        ow[d] = acc;
-      }
-      __syncthreads();
-    }
-    const float Ltot = L + lw;
-    const float inv = Ltot > 0.f ? 1.f / Ltot : 0.f;
-    for (int j = tid; j < D; j += blockDim.x) {
-      float acc = 0.f;
-      for (int d = 0; d < D; ++d) acc = fmaf(orot[d], __ldg(p.R + d * D + j), acc);
-      store_elem(p.out, p.out_dtype,
-                 b * p.out_stride[0] + hq * p.out_stride[1] + j * p.out_stride[3],
-                 (acc + ow[j]) * inv);
+    s_M[h] = Ms;
+    s_L[h] = L;
+  }
+  __syncthreads();
+  if (W > 0) {
+    for (int64_t i = tid; i < 8 * W; i += blockDim.x) {
+      const int h = (int)(i / W);
+      sc[i] = h < nh ? exp2f(sc[i] - s_M[h]) : 0.f;
     }
     __syncthreads();
+    if (tid < 8) {
+      float lw = 0.f;
+      for (int64_t t = 0; t < W; ++t) lw += sc[tid * W + t];
+      s_L[tid] += lw;
+    }
+  }
+  // --- rotated partial combination -------------------------------------------
+  for (int i = tid; i < 8 * D; i += blockDim.x) {
+    const int h = i / D, d = i % D;
+    float acc = 0.f;
+    for (int k = 0; k < nslot; ++k)
+      acc = fmaf(s_wt[h][k], p.part_o[((hrow0 + h) * p.maxslot + k) * D + d], acc);
+    orot[i] = acc;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  // --- un-rotate (o = O_rot R), add the window, normalise, store --------------
+  for (int j = tid; j < D; j += blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int d = 0; d < D; ++d) {
+      const float r = rs[d * D + j];
+#pragma unroll
+      for (int h = 0; h < 8; ++h) acc[h] = fmaf(orot[h * D + d], r, acc[h]);
+    }
+    for (int64_t t = 0; t < W; ++t) {
+      const float vx = load_elem(p.wv, p.w_dtype, b * p.wv_stride[0] + kvh * p.wv_stride[1] +
+                                                      t * p.wv_stride[2] + j * p.wv_stride[3]);
+#pragma unroll
+      for (int h = 0; h < 8; ++h) acc[h] = fmaf(sc[h * W + t], vx, acc[h]);
+    }
+    for (int h = 0; h < nh; ++h) {
+      const float L = s_L[h];
+      const int64_t hq = kvh * p.g + hc * 8 + h;
+      store_elem(p.out, p.out_dtype, b * p.out_stride[0] + hq * p.out_stride[1] + j * p.out_stride[3],
+                 L > 0.f ? acc[h] / L : 0.f);
+    }
   }
 }
 
@@ -576,16 +717,12 @@ struct Plan {
 using DecodeFn = void (*)(DecodeParams);
 
 template <int D, int KB, int VB, bool QJL>
-size_t dec_smem_bytes(int page_bytes) {
-  using SM = DecSmem<D, KB, VB, QJL>;
-  const size_t pb = (size_t)((page_bytes + 127) & ~127);
-  return kStages * pb + kStages * 8 + (size_t)(SM::kLutK + SM::kLutV) * 4 + (size_t)SM::kComb * 4;
-}
+size_t dec_smem_bytes() { return (size_t)Dec<D, KB, VB, QJL>::SMEM; }
 
 struct Variant {
   int D, kb, vb, qjl;
   DecodeFn fn;
-  size_t (*smem)(int);
+  size_t (*smem)();
 };
 
 #define TQ_VARIANT(D_, KB_, VB_, Q_) \
@@ -622,6 +759,8 @@ Plan make_plan(const tq_geom* G, const tq_cache* c, const tq_decode_args* a, int
   int64_t slots = a->num_ctas > 0 ? a->num_ctas : (int64_t)device_sm_count() * tmax(occ, 1);
   slots = tmax<int64_t>(1, slots / tmax(pl.nch, 1));
   pl.Q = TP > 0 ? (TP + slots - 1) / slots : 1;
+  // every stream's partials must fit the merge kernel's slot table
+  if (pl.Pv > 0) pl.Q = tmax<int64_t>(pl.Q, (pl.Pv + kMaxSlots - 2) / (kMaxSlots - 1));
   pl.ctas = TP > 0 ? (int)((TP + pl.Q - 1) / pl.Q) : 0;
   pl.maxslot = pl.Pv > 0 ? (int)((pl.Pv + pl.Q - 1) / pl.Q + 1) : 1;
   size_t off = 256;
@@ -646,8 +785,7 @@ int occupancy_of(const Variant* v, size_t smem) {
 size_t decode_workspace_bytes(const tq_geom* g, const tq_cache* c, const tq_decode_args* a) {
   const Variant* v = find_variant(g);
   if (!v) return 0;
-  const PageGeom pg = make_geom(g->head_dim, g->key_bits, g->value_bits, g->qjl);
-  const size_t smem = v->smem(pg.page_bytes);
+  const size_t smem = v->smem();
   if (set_smem_attr((const void*)v->fn, smem) != TQ_OK) return 0;
   return make_plan(g, c, a, occupancy_of(v, smem)).total;
 }
@@ -660,8 +798,7 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
               G->head_dim, G->key_bits, G->value_bits, G->qjl);
     return TQ_ERR_INVALID;
   }
-  const PageGeom pg = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
-  const size_t smem = v->smem(pg.page_bytes);
+  const size_t smem = v->smem();
   if (set_smem_attr((const void*)v->fn, smem) != TQ_OK) return TQ_ERR_CUDA;
   const Plan pl = make_plan(G, c, a, occupancy_of(v, smem));
   if (ws == nullptr || ws_bytes < pl.total) {
@@ -671,24 +808,25 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   uint8_t* w = static_cast<uint8_t*>(ws);
   const int64_t Hkv = c->streams / a->q->shape[0];
   const float alpha = sqrtf(3.14159265358979f / 2.f) / (float)pl.D;
+  const int phases = a->phases ? a->phases : (TQ_PHASE_QPREP | TQ_PHASE_DECODE | TQ_PHASE_MERGE);
 
   QPrepParams qp;
   qp.D = pl.D; qp.g = pl.g; qp.Hkv = (int)Hkv; qp.nch = pl.nch;
   qp.q = a->q->data; qp.q_dtype = a->q->dtype;
   for (int i = 0; i < 4; ++i) qp.q_stride[i] = a->q->stride[i];
-  qp.R = t->rot; qp.Sm = G->qjl ? t->qjl : nullptr;
+  qp.RT = t->rot_t; qp.ST = G->qjl ? t->qjl_t : nullptr;
   qp.scale_q = a->scale * kLog2e;
   qp.scale_s = a->scale * kLog2e * alpha;
   qp.qf = reinterpret_cast<uint32_t*>(w + pl.off_qf);
   qp.sqf = reinterpret_cast<uint32_t*>(w + pl.off_sqf);
-  const int phases = a->phases ? a->phases : (TQ_PHASE_QPREP | TQ_PHASE_DECODE | TQ_PHASE_MERGE);
   if (pl.S > 0 && (phases & TQ_PHASE_QPREP)) {
-    qprep_kernel<<<dim3((unsigned)pl.S, pl.nch), 128, 2 * 8 * pl.D * 4, st>>>(qp);
+    const size_t qsmem = (size_t)(2 * 8 * pl.D + (G->qjl ? 2 : 1) * pl.D * pl.D) * 4;
+    if (set_smem_attr((const void*)qprep_kernel, qsmem) != TQ_OK) return TQ_ERR_CUDA;
+    qprep_kernel<<<dim3((unsigned)pl.S, pl.nch), 128, qsmem, st>>>(qp);
     if (check_launch("tq_decode_attn/qprep") != TQ_OK) return TQ_ERR_CUDA;
   }
 
   DecodeParams dp;
-  dp.g = pg;
   dp.pages = c->pages; dp.pages_per_stream = c->pages_per_stream;
   dp.S = pl.S; dp.Pv = pl.Pv; dp.T = pl.T; dp.Q = pl.Q;
   dp.nch = pl.nch; dp.maxslot = pl.maxslot;
@@ -724,7 +862,7 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   mp.out = a->out->data; mp.out_dtype = a->out->dtype;
   for (int i = 0; i < 4; ++i) mp.out_stride[i] = a->out->stride[i];
   if (pl.S > 0 && (phases & TQ_PHASE_MERGE)) {
-    const size_t msmem = (size_t)(3 * pl.D + (mp.W > 0 ? mp.W : 1)) * 4;
+    const size_t msmem = (size_t)(pl.D * pl.D + 16 * pl.D + 8 * (mp.W > 0 ? mp.W : 1)) * 4;
     if (set_smem_attr((const void*)merge_kernel, msmem) != TQ_OK) return TQ_ERR_CUDA;
     merge_kernel<<<dim3((unsigned)pl.S, pl.nch), 128, msmem, st>>>(mp);
     if (check_launch("tq_decode_attn/merge") != TQ_OK) return TQ_ERR_CUDA;

@@ -55,6 +55,15 @@ class LayerTables:
     v_boundaries: torch.Tensor
     rot: torch.Tensor
     qjl_mat: Optional[torch.Tensor] = None
+    rot_t: Optional[torch.Tensor] = None
+    qjl_t: Optional[torch.Tensor] = None
+
+    def __post_init__(self):
+        self.rot = self.rot.contiguous().float()
+        self.rot_t = self.rot.t().contiguous()
+        if self.qjl_mat is not None:
+            self.qjl_mat = self.qjl_mat.contiguous().float()
+            self.qjl_t = self.qjl_mat.t().contiguous()
 
     def geom(self) -> _lib.Geom:
         return _lib.Geom(self.head_dim, self.key_bits, self.value_bits, 1 if self.qjl else 0)
@@ -67,6 +76,8 @@ class LayerTables:
         t.v_boundaries = self.v_boundaries.data_ptr()
         t.rot = self.rot.data_ptr()
         t.qjl = self.qjl_mat.data_ptr() if self.qjl_mat is not None else None
+        t.rot_t = self.rot_t.data_ptr()
+        t.qjl_t = self.qjl_t.data_ptr() if self.qjl_t is not None else None
         return t
 
 

@@ -77,6 +77,8 @@ typedef struct tq_tables {
   const float* v_boundaries;  /* [2^vb - 1]                                  */
   const float* rot;           /* R [D][D] row-major; y = x R^T               */
   const float* qjl;           /* S [D][D] row-major (NULL when qjl == 0)     */
+  const float* rot_t;         /* R^T [D][D] row-major                        */
+  const float* qjl_t;         /* S^T [D][D] row-major (NULL when qjl == 0)   */
 } tq_tables;
 
 /* Packed cache of one layer. */
