@@ -201,11 +201,11 @@ def run_ours(args, rank, world, local_rank):
     def step(phased_events=None):
         for layer in range(LAYERS):
             st = stores[layer]
-            ops.append(st.tables, st._pages, k_new[layer], v_new[layer], T_CTX)
             if phased_events is None:
-                ops.decode_attention(st.tables, st._pages, q_dev[layer], n_tok,
-                                     out=o_loc[layer], workspace=ws)
+                ops.decode_step(st.tables, st._pages, k_new[layer], v_new[layer], T_CTX,
+                                q_dev[layer], out=o_loc[layer], workspace=ws)
             else:
+                ops.append(st.tables, st._pages, k_new[layer], v_new[layer], T_CTX)
                 ops.decode_attention(st.tables, st._pages, q_dev[layer], n_tok,
                                      out=o_loc[layer], workspace=ws,
                                      phases=_lib.PHASE_QPREP)
@@ -303,8 +303,7 @@ def run_ours(args, rank, world, local_rank):
             qd = q_h[layer % 4].to(dev, non_blocking=True)
             kd = k_h[layer % 4].to(dev, non_blocking=True)
             vd = v_h[layer % 4].to(dev, non_blocking=True)
-            cache.append(kd, vd, layer)
-            o = cache.attend(qd, layer)
+            o = cache.decode(qd, kd, vd, layer)
             if world > 1:
                 dist.all_gather_into_tensor(o_all[layer], o)
                 o_h.copy_(o_all[layer], non_blocking=True)
@@ -367,9 +366,9 @@ def run_ours(args, rank, world, local_rank):
             "cpu_baseline": cpu_line,
             "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "path": "TurboQuantKVCache.append + .attend per layer, pinned host "
-                            "q/k/v in, output out"},
-            "gpu_launches": args.steps * LAYERS * 4,
+                    "path": "TurboQuantKVCache.decode per layer (fused store + attend), "
+                            "pinned host q/k/v in, output out"},
+            "gpu_launches": args.steps * LAYERS * 3,
             "clocks": clocks,
             "append": append_line,
             "device_status": status,
@@ -427,7 +426,7 @@ def run_profile(args):
     """Small single-GPU cases for ncu captures (no JSON line):
     --profile decode : one Mixtral layer (B16 Hkv8 T8192, K4+QJL/V2), 4 decode calls
     --profile append : one prefill-append layer (B8 Hkv8 T4096 D128 4-bit), 4 calls
-    --profile step   : one layer's decode step (append 1 token + decode), 4 calls
+    --profile step   : one layer's fused decode step (tq_decode_step), 4 calls
     """
     import torch
     from bhaskera_col_b200.inference import TurboQuantKVCache, ops
@@ -459,8 +458,9 @@ def run_profile(args):
     st = cache._stores[0]
     for _ in range(4):
         if args.profile == "step":
-            ops.append(st.tables, st._pages, k1, k1, T_CTX)
-        ops.decode_attention(st.tables, st._pages, q, T_CTX + 1, workspace=st.workspace)
+            ops.decode_step(st.tables, st._pages, k1, k1, T_CTX, q, workspace=st.workspace)
+        else:
+            ops.decode_attention(st.tables, st._pages, q, T_CTX + 1, workspace=st.workspace)
     torch.cuda.synchronize()
     if st.workspace.status() != 0:
         raise RuntimeError("device status error")

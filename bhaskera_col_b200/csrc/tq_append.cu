@@ -6,6 +6,7 @@
 //   dequantise + un-rotate + rescale               kv_cache.py:422-439
 #include "tq_common.cuh"
 #include "tq_internal.h"
+#include "tq_vec.cuh"
 
 namespace tq {
 
@@ -48,12 +49,14 @@ struct AppendParams {
   int64_t pos;
 };
 
+template <int D>
 __global__ void __launch_bounds__(kAppendThreads)
 append_kernel(AppendParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int GR = kAppendThreads / D;  // vector groups
+  constexpr int NV = (kVT + GR - 1) / GR; // vectors per thread
   const int which = blockIdx.y;           // 0: K, 1: V
   const PageGeom& g = p.g;
-  const int D = g.D;
   const int bits = which == 0 ? g.kb : g.vb;
   const bool qjl = (which == 0) && g.qjl;
   const int nb = (1 << bits) - 1;
@@ -78,22 +81,14 @@ append_kernel(AppendParams p) {
   cp_async_wait_all();
   for (int i = tid; i < (1 << bits); i += blockDim.x) cb[i] = p.cent[which][i];
   for (int i = tid; i < nb; i += blockDim.x) bb[i] = p.bnd[which][i];
-  for (int c = tid; c < D; c += blockDim.x) {
-    if (which == 0) {
-      int kp = k_pos_of(c, D);
-      ord[kp] = (int16_t)c;
-      qinv[qjl_bit_of(kp, D)] = (int16_t)c;
-    } else {
-      ord[v_pos_of(c, D)] = (int16_t)c;
-    }
-  }
+  if (which == 0) build_orders(ord, nullptr, qinv, D, tid, blockDim.x);
+  else build_orders(nullptr, ord, nullptr, D, tid, blockDim.x);
   __syncthreads();
 
   const int64_t nvec = p.B * p.H * p.T;
   const int vt = p.vt;
   const int64_t ntiles = (nvec + vt - 1) / vt;
   const int lane = tid & 31, warp = tid >> 5;
-  const int groups = kAppendThreads / D > 0 ? kAppendThreads / D : 1;
   const int rowbytes = which == 0 ? g.krow : g.vrow;
   const int sec = which == 0 ? g.off_k : g.off_v;
   const int nsec = which == 0 ? g.off_kn : g.off_vn;
@@ -107,29 +102,25 @@ append_kernel(AppendParams p) {
       int64_t gv = v0 + v;
       int64_t t = gv % p.T, bh = gv / p.T, h = bh % p.H, b = bh / p.H;
       const int64_t* st = p.stride[which];
-      int64_t base = b * st[0] + h * st[1] + t * st[2];
-      float ss = 0.f;
-      for (int c = lane; c < D; c += 32) {
-        float xv = load_elem(p.x[which], p.dtype[which], base + c * st[3]);
-        u[v * D + c] = xv;
-        ss = fmaf(xv, xv, ss);
-      }
-      ss = warp_sum(ss);
-      float n = sqrtf(ss);
-      float den = fmaxf(n, 1e-8f);
-      for (int c = lane; c < D; c += 32) u[v * D + c] = u[v * D + c] / den;
+      const int64_t base = b * st[0] + h * st[1] + t * st[2];
+      const float n = warp_normalize(p.x[which], p.dtype[which], base, st[3], u + v * D, D, lane);
       if (lane == 0) nrm[v] = n;
     }
     __syncthreads();
 
-    // -- rotate: y[v][j] = sum_i u[v][i] R[j][i] ----------------------------
-    if (tid < groups * D) {
+    // -- rotate: y[v][j] = sum_i u[v][i] R[j][i], all of a thread's vectors --
+    {
       const int j = tid % D, grp = tid / D;
-      for (int v = grp; v < nv; v += groups) {
-        float acc = 0.f;
-        for (int i = 0; i < D; ++i) acc = fmaf(u[v * D + i], RT[i * D + j], acc);
-        yv[v * D + j] = acc;
-        code[v * D + j] = (uint8_t)bucketize_lt(bb, nb, acc);
+      const int mine = (grp < GR && nv > grp) ? (nv - grp + GR - 1) / GR : 0;
+      float acc[NV];
+      rot_multi<D, NV>(u + grp * D, GR * D, mine, RT, j, acc);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        if (k < mine) {
+          const int v = grp + k * GR;
+          yv[v * D + j] = acc[k];
+          code[v * D + j] = (uint8_t)bucketize_lt(bb, nb, acc[k]);
+        }
       }
     }
     __syncthreads();
@@ -138,13 +129,14 @@ append_kernel(AppendParams p) {
     if (qjl) {
       for (int i = tid; i < nv * D; i += blockDim.x) u[i] = yv[i] - cb[code[i]];
       __syncthreads();
-      if (tid < groups * D) {
+      {
         const int j = tid % D, grp = tid / D;
-        for (int v = grp; v < nv; v += groups) {
-          float z = 0.f;
-          for (int i = 0; i < D; ++i) z = fmaf(u[v * D + i], ST[i * D + j], z);
-          qb[v * D + j] = z >= 0.f ? 1 : 0;
-        }
+        const int mine = (grp < GR && nv > grp) ? (nv - grp + GR - 1) / GR : 0;
+        float acc[NV];
+        rot_multi<D, NV>(u + grp * D, GR * D, mine, ST, j, acc);
+#pragma unroll
+        for (int k = 0; k < NV; ++k)
+          if (k < mine) qb[(grp + k * GR) * D + j] = acc[k] >= 0.f ? 1 : 0;
       }
       for (int v = warp; v < nv; v += kAppendThreads / 32) {
         float ss = 0.f;
@@ -163,15 +155,8 @@ append_kernel(AppendParams p) {
       const int64_t t = gv % p.T + p.pos, s = gv / p.T;
       uint8_t* page = p.pages + (s * p.pages_per_stream + t / kPageTokens) * (int64_t)g.page_bytes;
       const int slot = (int)(t % kPageTokens);
-      const int b0 = 32 * w;
-      const int n0 = b0 / bits, n1 = (b0 + 31) / bits;
-      uint64_t acc = 0;
-      for (int n = n0; n <= n1 && n < D; ++n) {
-        uint64_t cv = code[v * D + ord[n]];
-        int rel = n * bits - b0;
-        acc |= rel >= 0 ? (cv << rel) : (cv >> (-rel));
-      }
-      reinterpret_cast<uint32_t*>(page + sec + slot * rowbytes)[w] = (uint32_t)acc;
+      reinterpret_cast<uint32_t*>(page + sec + slot * rowbytes)[w] =
+          pack_word(code + v * D, ord, bits, w, D);
     }
     if (qjl) {
       const int qwords = D / 32;
@@ -181,9 +166,8 @@ append_kernel(AppendParams p) {
         const int64_t t = gv % p.T + p.pos, s = gv / p.T;
         uint8_t* page = p.pages + (s * p.pages_per_stream + t / kPageTokens) * (int64_t)g.page_bytes;
         const int slot = (int)(t % kPageTokens);
-        uint32_t word = 0;
-        for (int bit = 0; bit < 32; ++bit) word |= (uint32_t)qb[v * D + qinv[32 * w + bit]] << bit;
-        reinterpret_cast<uint32_t*>(page + g.off_q + slot * g.qrow)[w] = word;
+        reinterpret_cast<uint32_t*>(page + g.off_q + slot * g.qrow)[w] =
+            pack_qjl_word(qb + v * D, qinv, w);
       }
     }
     for (int v = tid; v < nv; v += blockDim.x) {
@@ -292,16 +276,19 @@ int launch_append(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   const int64_t nvec = p.B * p.H * p.T;
   if (nvec == 0) return TQ_OK;
   const size_t smem = append_smem_bytes(p.g.D, p.g.qjl != 0);
-  if (set_smem_attr((const void*)append_kernel, smem) != TQ_OK) return TQ_ERR_CUDA;
+  void (*fn)(AppendParams) = p.g.D == 32 ? append_kernel<32>
+                           : p.g.D == 64 ? append_kernel<64>
+                           : p.g.D == 96 ? append_kernel<96> : append_kernel<128>;
+  if (set_smem_attr((const void*)fn, smem) != TQ_OK) return TQ_ERR_CUDA;
   const int sms = device_sm_count();
-  const int occ = tmax(1, occupancy((const void*)append_kernel, kAppendThreads, smem));
+  const int occ = tmax(1, occupancy((const void*)fn, kAppendThreads, smem));
   // small appends (decode steps): few vectors per CTA so the grid fills the
   // GPU; large appends: full tiles, persistent CTAs
   const int64_t want = (nvec + (int64_t)sms * occ - 1) / ((int64_t)sms * occ);
   p.vt = (int)tmax<int64_t>(1, tmin<int64_t>(kVT, 2 * want));
   const int64_t tiles = (nvec + p.vt - 1) / p.vt;
   dim3 grid((unsigned)tmin<int64_t>(tiles, (int64_t)sms * occ), 2);
-  append_kernel<<<grid, kAppendThreads, smem, st>>>(p);
+  fn<<<grid, kAppendThreads, smem, st>>>(p);
   return check_launch("tq_append");
 }
 

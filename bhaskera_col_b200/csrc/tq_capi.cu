@@ -22,6 +22,16 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
+int launch_result(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) e = cudaGetLastError();
+  else cudaGetLastError();   // clear the sticky launch error
+  if (e != cudaSuccess) {
+    set_error("%s: launch failed: %s", what, cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return TQ_OK;
+}
+
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -268,6 +278,35 @@ int32_t tq_decode_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
   int rc = check_decode(g, t, c, a, fn);
   if (rc) return rc;
   return launch_decode(g, t, c, a, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int32_t tq_decode_step(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                       const tq_tensor4* k_new, const tq_tensor4* v_new, int64_t pos,
+                       const tq_decode_args* a, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  const char* fn = "tq_decode_step";
+  int rc = check_decode(g, t, c, a, fn);
+  if (rc) return rc;
+  if ((rc = check_t4(k_new, "k_new", fn)) || (rc = check_t4(v_new, "v_new", fn))) return rc;
+  if (g->head_dim > 128) {
+    set_error("%s: head_dim %d > 128 is not supported by the append path", fn, g->head_dim);
+    return TQ_ERR_INVALID;
+  }
+  for (int i = 0; i < 4; ++i)
+    if (k_new->shape[i] != v_new->shape[i]) { set_error("%s: k_new and v_new shapes differ", fn); return TQ_ERR_INVALID; }
+  if (k_new->shape[0] != a->q->shape[0] || k_new->shape[0] * k_new->shape[1] != c->streams ||
+      k_new->shape[2] != 1 || k_new->shape[3] != g->head_dim) {
+    set_error("%s: k_new/v_new must be (B, Hkv, 1, D) with B*Hkv = %lld streams", fn,
+              (long long)c->streams);
+    return TQ_ERR_INVALID;
+  }
+  if (pos < 0 || a->n_tokens != pos + 1) {
+    set_error("%s: n_tokens (%lld) must equal pos + 1 (%lld)", fn, (long long)a->n_tokens,
+              (long long)(pos + 1));
+    return TQ_ERR_INVALID;
+  }
+  StepInput step{k_new, v_new, pos};
+  return launch_decode(g, t, c, a, workspace, workspace_bytes, (cudaStream_t)stream, &step);
 }
 
 int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream) {

@@ -173,6 +173,17 @@ __device__ __forceinline__ void stage_async(void* dst, const void* src, int byte
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start while its predecessor is still running; it must
+// call pdl_wait() before touching anything the predecessor writes or reads.
+// Without the launch attribute both are no-ops in effect.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Tensor-core helpers (mma.sync m16n8k16 f16 -> f32, movmatrix)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4],

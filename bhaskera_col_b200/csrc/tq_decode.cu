@@ -7,14 +7,15 @@
 //
 // Math.  With R the layer rotation and k_t = n_t (c[idx_t] R), the score is
 //   <q, k_t> = n_t <q R^T, c[idx_t]>,
-// so the query is rotated once (qprep_kernel) and keys are never
+// so the query is rotated once (prep_kernel) and keys are never
 // un-rotated.  Likewise o = sum_t p_t n_t (c_v[idx_t] R) = (sum_t p_t n_t
 // c_v[idx_t]) R: values are accumulated in the rotated basis and un-rotated
 // once per head in merge_kernel.  The optional QJL term adds
 // gamma_t * alpha * <S q_rot, sign_t>.
 //
 // Kernels per call:
-//   qprep_kernel   q_rot, S q_rot -> fp16 fragments (scale * log2e folded in)
+//   prep_kernel    q_rot, S q_rot -> fp16 fragments (scale * log2e folded in);
+//                  in a decode step also the append of the new token
 //   decode_kernel  persistent; each CTA owns a contiguous range of the
 //                  flattened (stream, page) space.  A producer warp streams
 //                  64-token pages into shared memory with bulk async copies
@@ -27,6 +28,7 @@
 //                  full-precision window, un-rotates, writes the output.
 #include "tq_common.cuh"
 #include "tq_internal.h"
+#include "tq_vec.cuh"
 
 #include <math.h>
 
@@ -220,11 +222,13 @@ decode_kernel(DecodeParams p) {
     }
     fence_mbar_init();
   }
+  pdl_launch_dependents();
   if (warp < kConsumerWarps) {
     build_lut<KB>(smem, p.kc, tid, NCT);
     build_lut<VB>(smem + G::LUTV, p.vc, tid, NCT);
   }
   __syncthreads();
+  pdl_wait();   // pages and query fragments come from the preceding kernels
 
   // ------------------------------------------------------------ producer
   if (warp == kConsumerWarps) {
@@ -497,9 +501,15 @@ decode_kernel(DecodeParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// query preparation: q_rot = q R^T, sq = S q_rot, scaled, packed to half2
-// grid = (S, nch), 128 threads; thread j owns output coordinate j of all 8
-// heads so R^T and S^T are each read once per CTA, coalesced.
+// Query preparation (and, for a decode step, the append of the new token).
+//
+// q_rot = q R^T and Sq = S q_rot for the <= 8 query heads of a head chunk
+// become fp16 fragments for decode_kernel (softmax scale * log2e folded in).
+// With `append` set, the CTAs of head chunk 0 also store the stream's new
+// K/V token at position `pos`, with the same math and summation order as
+// append_kernel (kv_cache.py:382-398), so the page bytes are identical to a
+// tq_append of that token.  grid = (S, nch), 256 threads; thread (j, grp)
+// owns output coordinate j of the vectors grp, grp + G, ... (G = 256 / D).
 // ---------------------------------------------------------------------------
 struct QPrepParams {
   int D, g, Hkv, nch;
@@ -509,65 +519,159 @@ struct QPrepParams {
   uint32_t* qf; uint32_t* sqf;
 };
 
-__global__ void __launch_bounds__(128) qprep_kernel(QPrepParams p) {
+struct PrepParams {
+  QPrepParams q;
+  int append;
+  PageGeom g;
+  const float* kc; const float* kb; const float* vc; const float* vb;
+  const void* kx; const void* vx; int k_dtype, v_dtype; int64_t ks[4], vs[4];
+  uint8_t* pages; int64_t pages_per_stream; int64_t pos;
+};
+
+constexpr int kPrepThreads = 256;
+
+template <int D>
+struct PrepSmem {
+  // floats: R^T, S^T, xs[10][D] (q x8, k, v), ys[10][D], codebooks 4x256, norms 4
+  static size_t bytes(bool qjl) {
+    return ((qjl ? 2 : 1) * (size_t)D * D + 20 * D + 4 * 256 + 4) * 4 + 3 * D + 3 * D * 2 + 16;
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   extern __shared__ __align__(128) unsigned char smem[];
-  const int D = p.D;
-  float* rt = reinterpret_cast<float*>(smem);   // [D][D] R^T
+  constexpr int G = kPrepThreads / D;            // vector groups
+  constexpr int NA = (10 + G - 1) / G;           // vectors per thread, phase A
+  constexpr int NB = (9 + G - 1) / G;            // vectors per thread, phase B
+  const QPrepParams& p = pp.q;
+  const PageGeom& g = pp.g;
+  const bool qjl = p.ST != nullptr;
+  float* rt = reinterpret_cast<float*>(smem);    // [D][D] R^T
   float* stt = rt + D * D;                       // [D][D] S^T (QJL only)
-  float* qs = stt + (p.ST ? D * D : 0);          // [8][D]
-  float* qr = qs + 8 * D;                        // [8][D]
+  float* xs = stt + (qjl ? D * D : 0);           // [10][D]: q heads, u_k, u_v; later Sq
+  float* ys = xs + 10 * D;                       // [10][D]: q_rot, y_k (-> residual), y_v
+  float* cb = ys + 10 * D;                       // [4][256] k cent, k bnd, v cent, v bnd
+  float* nrm = cb + 4 * 256;                     // ||k||, ||v||, gamma
+  uint8_t* code = reinterpret_cast<uint8_t*>(nrm + 4);   // [2][D]
+  uint8_t* qb = code + 2 * D;                    // [D]
+  int16_t* ordk = reinterpret_cast<int16_t*>(qb + D);
+  int16_t* ordv = ordk + D;
+  int16_t* qinv = ordv + D;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int j = tid % D, grp = tid / D;
   const int64_t s = blockIdx.x;
   const int hc = blockIdx.y;
   const int64_t b = s / p.Hkv, kvh = s % p.Hkv;
   const int nh = tmin(8, p.g - hc * 8);
-  stage_async(rt, p.RT, D * D * 4, threadIdx.x, blockDim.x);
-  if (p.ST) stage_async(stt, p.ST, D * D * 4, threadIdx.x, blockDim.x);
-  for (int i = threadIdx.x; i < 8 * D; i += blockDim.x) {
+  const bool app = pp.append && hc == 0;
+  const int nbk = (1 << g.kb) - 1, nbv = (1 << g.vb) - 1;
+
+  stage_async(rt, p.RT, D * D * 4, tid, kPrepThreads);
+  if (qjl) stage_async(stt, p.ST, D * D * 4, tid, kPrepThreads);
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int i = tid; i < 8 * D; i += kPrepThreads) {
     const int hl = i / D, c = i % D;
-    float v = 0.f;
-    if (hl < nh) {
-      const int64_t hq = kvh * p.g + hc * 8 + hl;
-      v = load_elem(p.q, p.q_dtype, b * p.q_stride[0] + hq * p.q_stride[1] + c * p.q_stride[3]);
+    xs[i] = hl < nh ? load_elem(p.q, p.q_dtype, b * p.q_stride[0] +
+                                (kvh * p.g + hc * 8 + hl) * p.q_stride[1] + c * p.q_stride[3])
+                    : 0.f;
+  }
+  if (app) {
+    if (warp == 0) {
+      const float n = warp_normalize(pp.kx, pp.k_dtype, b * pp.ks[0] + kvh * pp.ks[1], pp.ks[3],
+                                     xs + 8 * D, D, lane);
+      if (lane == 0) nrm[0] = n;
+    } else if (warp == 1) {
+      const float n = warp_normalize(pp.vx, pp.v_dtype, b * pp.vs[0] + kvh * pp.vs[1], pp.vs[3],
+                                     xs + 9 * D, D, lane);
+      if (lane == 0) nrm[1] = n;
     }
-    qs[i] = v;
+    for (int i = tid; i < 256; i += kPrepThreads) {
+      if (i <= nbk) cb[i] = pp.kc[i];
+      if (i < nbk) cb[256 + i] = pp.kb[i];
+      if (i <= nbv) cb[512 + i] = pp.vc[i];
+      if (i < nbv) cb[768 + i] = pp.vb[i];
+    }
+    build_orders(ordk, ordv, qinv, D, tid, kPrepThreads);
   }
   cp_async_wait_all();
   __syncthreads();
-  for (int j = threadIdx.x; j < D; j += blockDim.x) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-    for (int k = 0; k < D; ++k) {
-      const float r = rt[k * D + j];
+
+  // phase A: rotate the query heads (and u_k, u_v)
+  {
+    const int nvec = app ? 10 : 8;
+    const int mine = (grp < G && nvec > grp) ? (nvec - grp + G - 1) / G : 0;
+    float acc[NA];
+    rot_multi<D, NA>(xs + grp * D, G * D, mine, rt, j, acc);
 #pragma unroll
-      for (int h = 0; h < 8; ++h) acc[h] = fmaf(qs[h * D + k], r, acc[h]);
+    for (int k = 0; k < NA; ++k) {
+      const int v = grp + k * G;
+      if (k < mine) {
+        ys[v * D + j] = acc[k];
+        if (v == 8) code[j] = (uint8_t)bucketize_lt(cb + 256, nbk, acc[k]);
+        if (v == 9) code[D + j] = (uint8_t)bucketize_lt(cb + 768, nbv, acc[k]);
+      }
     }
+  }
+  __syncthreads();
+  if (qjl) {
+    if (app && tid < D) ys[8 * D + tid] -= cb[code[tid]];   // K residual y - c[idx]
+    __syncthreads();
+    // phase B: S q_rot for the heads, S r for the K residual
+    const int nvec = app ? 9 : 8;
+    const int mine = (grp < G && nvec > grp) ? (nvec - grp + G - 1) / G : 0;
+    float acc[NB];
+    rot_multi<D, NB>(ys + grp * D, G * D, mine, stt, j, acc);
 #pragma unroll
-    for (int h = 0; h < 8; ++h) qr[h * D + j] = acc[h];
+    for (int k = 0; k < NB; ++k) {
+      const int v = grp + k * G;
+      if (k < mine) {
+        if (v < 8) xs[v * D + j] = acc[k];
+        else qb[j] = acc[k] >= 0.f ? 1 : 0;
+      }
+    }
+    if (app && warp == 0) {
+      float ss = 0.f;
+      for (int c = lane; c < D; c += 32) ss = fmaf(ys[8 * D + c], ys[8 * D + c], ss);
+      ss = warp_sum(ss);
+      if (lane == 0) nrm[2] = nrm[0] * sqrtf(ss);
+    }
   }
   __syncthreads();
   uint32_t* qo = p.qf + (s * p.nch + hc) * 8 * (D / 2);
-  for (int i = threadIdx.x; i < 8 * (D / 2); i += blockDim.x) {
+  for (int i = tid; i < 8 * (D / 2); i += kPrepThreads) {
     const int hl = i / (D / 2), c2 = i % (D / 2);
-    qo[i] = pack_half2(qr[hl * D + 2 * c2] * p.scale_q, qr[hl * D + 2 * c2 + 1] * p.scale_q);
+    qo[i] = pack_half2(ys[hl * D + 2 * c2] * p.scale_q, ys[hl * D + 2 * c2 + 1] * p.scale_q);
   }
-  if (p.ST) {
-    // sq -> qs (q itself is no longer needed)
-    for (int j = threadIdx.x; j < D; j += blockDim.x) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-      for (int k = 0; k < D; ++k) {
-        const float r = stt[k * D + j];
-#pragma unroll
-        for (int h = 0; h < 8; ++h) acc[h] = fmaf(qr[h * D + k], r, acc[h]);
-      }
-#pragma unroll
-      for (int h = 0; h < 8; ++h) qs[h * D + j] = acc[h];
-    }
-    __syncthreads();
+  if (qjl) {
     uint32_t* so = p.sqf + (s * p.nch + hc) * 8 * (D / 2);
-    for (int i = threadIdx.x; i < 8 * (D / 2); i += blockDim.x) {
+    for (int i = tid; i < 8 * (D / 2); i += kPrepThreads) {
       const int hl = i / (D / 2), c2 = i % (D / 2);
-      so[i] = pack_half2(qs[hl * D + 2 * c2] * p.scale_s, qs[hl * D + 2 * c2 + 1] * p.scale_s);
+      so[i] = pack_half2(xs[hl * D + 2 * c2] * p.scale_s, xs[hl * D + 2 * c2 + 1] * p.scale_s);
+    }
+  }
+  if (app) {
+    const int64_t t = pp.pos;
+    uint8_t* page = pp.pages + (s * pp.pages_per_stream + t / kPageTokens) * (int64_t)g.page_bytes;
+    const int slot = (int)(t % kPageTokens);
+    const int kw = g.krow / 4, vw = g.vrow / 4, qw = qjl ? D / 32 : 0;
+    for (int i = tid; i < kw + vw + qw; i += kPrepThreads) {
+      if (i < kw) {
+        reinterpret_cast<uint32_t*>(page + g.off_k + slot * g.krow)[i] = pack_word(code, ordk, g.kb, i, D);
+      } else if (i < kw + vw) {
+        reinterpret_cast<uint32_t*>(page + g.off_v + slot * g.vrow)[i - kw] =
+            pack_word(code + D, ordv, g.vb, i - kw, D);
+      } else {
+        reinterpret_cast<uint32_t*>(page + g.off_q + slot * g.qrow)[i - kw - vw] =
+            pack_qjl_word(qb, qinv, i - kw - vw);
+      }
+    }
+    if (tid == 0) {
+      reinterpret_cast<__half*>(page + g.off_kn)[slot] = __float2half_rn(nrm[0]);
+      reinterpret_cast<__half*>(page + g.off_vn)[slot] = __float2half_rn(nrm[1]);
+      if (qjl) reinterpret_cast<__half*>(page + g.off_kr)[slot] = __float2half_rn(nrm[2]);
     }
   }
 }
@@ -588,14 +692,20 @@ struct MergeParams {
 };
 
 constexpr int kMaxSlots = 64;
+constexpr int kMergeThreads = 256;
+constexpr int kSlotChunk = 8;
 
-__global__ void __launch_bounds__(128) merge_kernel(MergeParams p) {
+// grid = (S, nch), 256 threads.  Shared memory: R [D][D], the rotated
+// combination orot [8][D], a chunk of partials [8][kSlotChunk][D], and for
+// the window q [8][D] and scores/probabilities [8][W].
+template <int D>
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
-  const int D = p.D;
   const int64_t W = p.W;
   float* rs = reinterpret_cast<float*>(smem);     // [D][D] R
   float* orot = rs + D * D;                        // [8][D]
-  float* qv = orot + 8 * D;                        // [8][D]  (window only)
+  float* po = orot + 8 * D;                        // [8][kSlotChunk][D]
+  float* qv = po + 8 * kSlotChunk * D;             // [8][D]  (window only)
   float* sc = qv + 8 * D;                          // [8][W]  (window only)
   __shared__ float s_wt[8][kMaxSlots];
   __shared__ float s_M[8], s_L[8];
@@ -603,6 +713,7 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeParams p) {
   const int hc = blockIdx.y;
   const int64_t b = s / p.Hkv, kvh = s % p.Hkv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NWARP = kMergeThreads / 32;
   const int nh = tmin(8, p.g - hc * 8);
   int nslot = 0;
   if (p.Pv > 0) {
@@ -610,18 +721,20 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeParams p) {
     nslot = (int)(last - first + 1);
   }
   const int64_t hrow0 = (s * p.nch + hc) * 8;
-  stage_async(rs, p.R, D * D * 4, tid, blockDim.x);
+  stage_async(rs, p.R, D * D * 4, tid, kMergeThreads);
+  pdl_launch_dependents();
+  pdl_wait();
 
   // --- window scores (unrotated), all heads --------------------------------
   if (W > 0) {
-    for (int i = tid; i < 8 * D; i += blockDim.x) {
+    for (int i = tid; i < 8 * D; i += kMergeThreads) {
       const int hl = i / D, c = i % D;
       qv[i] = hl < nh ? load_elem(p.q, p.q_dtype, b * p.q_stride[0] +
                                   (kvh * p.g + hc * 8 + hl) * p.q_stride[1] + c * p.q_stride[3])
                       : 0.f;
     }
     __syncthreads();
-    for (int64_t t = warp; t < W; t += blockDim.x / 32) {
+    for (int64_t t = warp; t < W; t += NWARP) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int c = lane; c < D; c += 32) {
         const float kx = load_elem(p.wk, p.w_dtype, b * p.wk_stride[0] + kvh * p.wk_stride[1] +
@@ -637,68 +750,89 @@ __global__ void __launch_bounds__(128) merge_kernel(MergeParams p) {
     }
     __syncthreads();
   }
-  // --- per-head max, partial weights, denominators --------------------------
-  if (tid < 8) {
-    const int h = tid;
+  // --- per-head max and partial weights: warp h handles head h ---------------
+  if (warp < 8) {
+    const int h = warp;
     float M = kNegInf;
     if (h < nh) {
-      for (int k = 0; k < nslot; ++k) M = fmaxf(M, p.part_m[(hrow0 + h) * p.maxslot + k]);
-      for (int64_t t = 0; t < W; ++t) M = fmaxf(M, sc[h * W + t]);
+      for (int k = lane; k < nslot; k += 32) M = fmaxf(M, p.part_m[(hrow0 + h) * p.maxslot + k]);
+      for (int64_t t = lane; t < W; t += 32) M = fmaxf(M, sc[h * W + t]);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     const float Ms = M == kNegInf ? 0.f : M;
     float L = 0.f;
-    for (int k = 0; k < nslot; ++k) {
+    for (int k = lane; k < nslot; k += 32) {
       const float mk = p.part_m[(hrow0 + h) * p.maxslot + k];
       const float wt = (h < nh && mk != kNegInf) ? exp2f(mk - Ms) : 0.f;
       s_wt[h][k] = wt;
       L = fmaf(wt, p.part_l[(hrow0 + h) * p.maxslot + k], L);
     }
-    s_M[h] = Ms;
-    s_L[h] = L;
+    for (int64_t t = lane; t < W; t += 32) {
+      const float e = h < nh ? exp2f(sc[h * W + t] - Ms) : 0.f;
+      sc[h * W + t] = e;
+      L += e;
+    }
+    L = warp_sum(L);
+    if (lane == 0) { s_M[h] = Ms; s_L[h] = L; }
   }
   __syncthreads();
-  if (W > 0) {
-    for (int64_t i = tid; i < 8 * W; i += blockDim.x) {
-      const int h = (int)(i / W);
-      sc[i] = h < nh ? exp2f(sc[i] - s_M[h]) : 0.f;
+  // --- rotated partial combination, slots staged in chunks ------------------
+  constexpr int OUT = 4;                          // outputs per thread (8 * 128 / 256)
+  float acc[OUT] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < nslot; k0 += kSlotChunk) {
+    const int kn = tmin(kSlotChunk, nslot - k0);
+    for (int h = 0; h < 8; ++h)
+      stage_async(po + h * kSlotChunk * D, p.part_o + ((hrow0 + h) * p.maxslot + k0) * D,
+                  kn * D * 4, tid, kMergeThreads);
+    cp_async_wait_all();
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < OUT; ++r) {
+      const int i = tid + r * kMergeThreads;
+      if (i < 8 * D) {
+        const int h = i / D, d = i % D;
+        for (int k = 0; k < kn; ++k) acc[r] = fmaf(s_wt[h][k0 + k], po[(h * kSlotChunk + k) * D + d], acc[r]);
+      }
     }
     __syncthreads();
-    if (tid < 8) {
-      float lw = 0.f;
-      for (int64_t t = 0; t < W; ++t) lw += sc[tid * W + t];
-      s_L[tid] += lw;
-    }
   }
-  // --- rotated partial combination -------------------------------------------
-  for (int i = tid; i < 8 * D; i += blockDim.x) {
-    const int h = i / D, d = i % D;
-    float acc = 0.f;
-    for (int k = 0; k < nslot; ++k)
-      acc = fmaf(s_wt[h][k], p.part_o[((hrow0 + h) * p.maxslot + k) * D + d], acc);
-    orot[i] = acc;
+#pragma unroll
+  for (int r = 0; r < OUT; ++r) {
+    const int i = tid + r * kMergeThreads;
+    if (i < 8 * D) orot[i] = acc[r];
   }
   cp_async_wait_all();
   __syncthreads();
   // --- un-rotate (o = O_rot R), add the window, normalise, store --------------
-  for (int j = tid; j < D; j += blockDim.x) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  // thread (j, half) handles heads half*4 .. half*4+3 of coordinate j
+  constexpr int groups = kMergeThreads / D;       // 2 for D = 128
+  constexpr int hpg = 8 / groups;                 // heads per group
+  for (int x = tid; x < D * groups; x += kMergeThreads) {
+    const int j = x % D, h0 = (x / D) * hpg;
+    float o[hpg];
+#pragma unroll
+    for (int h = 0; h < hpg; ++h) o[h] = 0.f;
 #pragma unroll 4
     for (int d = 0; d < D; ++d) {
       const float r = rs[d * D + j];
 #pragma unroll
-      for (int h = 0; h < 8; ++h) acc[h] = fmaf(orot[h * D + d], r, acc[h]);
+      for (int h = 0; h < hpg; ++h) o[h] = fmaf(orot[(h0 + h) * D + d], r, o[h]);
     }
     for (int64_t t = 0; t < W; ++t) {
       const float vx = load_elem(p.wv, p.w_dtype, b * p.wv_stride[0] + kvh * p.wv_stride[1] +
                                                       t * p.wv_stride[2] + j * p.wv_stride[3]);
 #pragma unroll
-      for (int h = 0; h < 8; ++h) acc[h] = fmaf(sc[h * W + t], vx, acc[h]);
+      for (int h = 0; h < hpg; ++h) o[h] = fmaf(sc[(h0 + h) * W + t], vx, o[h]);
     }
-    for (int h = 0; h < nh; ++h) {
-      const float L = s_L[h];
-      const int64_t hq = kvh * p.g + hc * 8 + h;
+#pragma unroll
+    for (int h = 0; h < hpg; ++h) {
+      const int hh = h0 + h;
+      if (hh >= nh) break;
+      const float L = s_L[hh];
+      const int64_t hq = kvh * p.g + hc * 8 + hh;
       store_elem(p.out, p.out_dtype, b * p.out_stride[0] + hq * p.out_stride[1] + j * p.out_stride[3],
-                 L > 0.f ? acc[h] / L : 0.f);
+                 L > 0.f ? o[h] / L : 0.f);
     }
   }
 }
@@ -790,8 +924,20 @@ size_t decode_workspace_bytes(const tq_geom* g, const tq_cache* c, const tq_deco
   return make_plan(g, c, a, occupancy_of(v, smem)).total;
 }
 
+using PrepFn = void (*)(PrepParams);
+
+static bool prep_for(int D, PrepFn* fn, size_t* smem, bool qjl) {
+  switch (D) {
+    case 32: *fn = prep_kernel<32>; *smem = PrepSmem<32>::bytes(qjl); return true;
+    case 64: *fn = prep_kernel<64>; *smem = PrepSmem<64>::bytes(qjl); return true;
+    case 128: *fn = prep_kernel<128>; *smem = PrepSmem<128>::bytes(qjl); return true;
+    default: return false;
+  }
+}
+
 int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
-                  const tq_decode_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
+                  const tq_decode_args* a, void* ws, size_t ws_bytes, cudaStream_t st,
+                  const StepInput* step) {
   const Variant* v = find_variant(G);
   if (!v) {
     set_error("tq_decode_attn: no kernel for head_dim=%d key_bits=%d value_bits=%d qjl=%d",
@@ -819,11 +965,32 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   qp.scale_s = a->scale * kLog2e * alpha;
   qp.qf = reinterpret_cast<uint32_t*>(w + pl.off_qf);
   qp.sqf = reinterpret_cast<uint32_t*>(w + pl.off_sqf);
-  if (pl.S > 0 && (phases & TQ_PHASE_QPREP)) {
-    const size_t qsmem = (size_t)(2 * 8 * pl.D + (G->qjl ? 2 : 1) * pl.D * pl.D) * 4;
-    if (set_smem_attr((const void*)qprep_kernel, qsmem) != TQ_OK) return TQ_ERR_CUDA;
-    qprep_kernel<<<dim3((unsigned)pl.S, pl.nch), 128, qsmem, st>>>(qp);
-    if (check_launch("tq_decode_attn/qprep") != TQ_OK) return TQ_ERR_CUDA;
+  if (pl.S > 0 && (step || (phases & TQ_PHASE_QPREP))) {
+    PrepParams pp;
+    pp.q = qp;
+    pp.append = step != nullptr;
+    pp.g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
+    pp.kc = t->k_centroids; pp.kb = t->k_boundaries;
+    pp.vc = t->v_centroids; pp.vb = t->v_boundaries;
+    pp.kx = pp.vx = nullptr; pp.k_dtype = pp.v_dtype = 0;
+    for (int i = 0; i < 4; ++i) pp.ks[i] = pp.vs[i] = 0;
+    pp.pages = c->pages; pp.pages_per_stream = c->pages_per_stream; pp.pos = 0;
+    if (step) {
+      pp.kx = step->k->data; pp.vx = step->v->data;
+      pp.k_dtype = step->k->dtype; pp.v_dtype = step->v->dtype;
+      for (int i = 0; i < 4; ++i) { pp.ks[i] = step->k->stride[i]; pp.vs[i] = step->v->stride[i]; }
+      pp.pos = step->pos;
+    }
+    PrepFn pfn;
+    size_t psmem;
+    if (!prep_for(pl.D, &pfn, &psmem, G->qjl != 0)) {
+      set_error("tq_decode_attn: head_dim %d has no query-preparation kernel", pl.D);
+      return TQ_ERR_INVALID;
+    }
+    if (set_smem_attr((const void*)pfn, psmem) != TQ_OK) return TQ_ERR_CUDA;
+    if (launch_result(launch_pdl(pfn, dim3((unsigned)pl.S, pl.nch), dim3(kPrepThreads), psmem, st, pp),
+                      step ? "tq_decode_step/prep" : "tq_decode_attn/qprep") != TQ_OK)
+      return TQ_ERR_CUDA;
   }
 
   DecodeParams dp;
@@ -837,8 +1004,9 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   dp.part_o = reinterpret_cast<float*>(w + pl.off_o);
   dp.status = reinterpret_cast<uint32_t*>(w);
   if (pl.ctas > 0 && (phases & TQ_PHASE_DECODE)) {
-    v->fn<<<dim3(pl.ctas, pl.nch), kDecThreads, smem, st>>>(dp);
-    if (check_launch("tq_decode_attn/decode") != TQ_OK) return TQ_ERR_CUDA;
+    if (launch_result(launch_pdl(v->fn, dim3(pl.ctas, pl.nch), dim3(kDecThreads), smem, st, dp),
+                      "tq_decode_attn/decode") != TQ_OK)
+      return TQ_ERR_CUDA;
   }
 
   MergeParams mp;
@@ -862,10 +1030,14 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   mp.out = a->out->data; mp.out_dtype = a->out->dtype;
   for (int i = 0; i < 4; ++i) mp.out_stride[i] = a->out->stride[i];
   if (pl.S > 0 && (phases & TQ_PHASE_MERGE)) {
-    const size_t msmem = (size_t)(pl.D * pl.D + 16 * pl.D + 8 * (mp.W > 0 ? mp.W : 1)) * 4;
-    if (set_smem_attr((const void*)merge_kernel, msmem) != TQ_OK) return TQ_ERR_CUDA;
-    merge_kernel<<<dim3((unsigned)pl.S, pl.nch), 128, msmem, st>>>(mp);
-    if (check_launch("tq_decode_attn/merge") != TQ_OK) return TQ_ERR_CUDA;
+    const size_t msmem =
+        (size_t)(pl.D * pl.D + 16 * pl.D + 8 * kSlotChunk * pl.D + 8 * (mp.W > 0 ? mp.W : 1)) * 4;
+    void (*mfn)(MergeParams) = pl.D == 32 ? merge_kernel<32> : pl.D == 64 ? merge_kernel<64>
+                                                                          : merge_kernel<128>;
+    if (set_smem_attr((const void*)mfn, msmem) != TQ_OK) return TQ_ERR_CUDA;
+    if (launch_result(launch_pdl(mfn, dim3((unsigned)pl.S, pl.nch), dim3(kMergeThreads), msmem, st, mp),
+                      "tq_decode_attn/merge") != TQ_OK)
+      return TQ_ERR_CUDA;
   }
   return TQ_OK;
 }

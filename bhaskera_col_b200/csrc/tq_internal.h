@@ -12,6 +12,8 @@ namespace tq {
 void set_error(const char* fmt, ...);
 // Returns TQ_OK, or TQ_ERR_CUDA with the launch error recorded.
 int check_launch(const char* what);
+// Same for the return code of an explicit launch (cudaLaunchKernelEx).
+int launch_result(cudaError_t e, const char* what);
 int set_smem_attr(const void* kernel, size_t bytes);
 int device_sm_count();
 // Resident CTAs per SM for a kernel (cached per device).
@@ -27,7 +29,32 @@ int launch_dequant(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                    cudaStream_t st);
 size_t decode_workspace_bytes(const tq_geom* g, const tq_cache* c,
                               const tq_decode_args* a);
+// The new token of a decode step (tq_decode_step): stored at `pos` by the
+// query-preparation kernel before attention.
+struct StepInput {
+  const tq_tensor4* k;
+  const tq_tensor4* v;
+  int64_t pos;
+};
 int launch_decode(const tq_geom* g, const tq_tables* t, const tq_cache* c,
-                  const tq_decode_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
+                  const tq_decode_args* a, void* ws, size_t ws_bytes, cudaStream_t st,
+                  const StepInput* step = nullptr);
+
+// cudaLaunchKernelEx with programmatic stream serialisation (see pdl_wait).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
 
 }  // namespace tq

@@ -1,0 +1,89 @@
+// tq_vec.cuh — per-vector append math shared by the append and decode-step
+// kernels, so both write bit-identical pages.
+//
+// Follows _LayerKVStore._compress_chunk (aditya25058/Bhaskera_col
+// src/bhaskera/inference/kv_cache.py:382-398): fp32 norm, u = x / max(n,
+// 1e-8), y = u R^T, code = #{boundaries < y}, stored norm = fp16(n).
+#pragma once
+
+#include "tq_common.cuh"
+
+namespace tq {
+
+// One warp: u[0..D) = x / max(||x||, 1e-8) (x read with stride sd from
+// base), returns ||x|| on every lane.
+__device__ __forceinline__ float warp_normalize(const void* x, int dtype, int64_t base,
+                                                int64_t sd, float* u, int D, int lane) {
+  float ss = 0.f;
+  for (int c = lane; c < D; c += 32) {
+    const float xv = load_elem(x, dtype, base + c * sd);
+    u[c] = xv;
+    ss = fmaf(xv, xv, ss);
+  }
+  ss = warp_sum(ss);
+  const float n = sqrtf(ss);
+  const float den = fmaxf(n, 1e-8f);
+  __syncwarp();
+  for (int c = lane; c < D; c += 32) u[c] = u[c] / den;
+  return n;
+}
+
+// y_j = sum_i u[i] T[i][j] (T row-major, i ascending).
+__device__ __forceinline__ float rot_coord(const float* u, const float* T, int j, int D) {
+  float acc = 0.f;
+  for (int i = 0; i < D; ++i) acc = fmaf(u[i], T[i * D + j], acc);
+  return acc;
+}
+
+// acc[v] = sum_i x[v * ldx + i] T[i][j] for NV vectors at once (same per-vector
+// summation order as rot_coord, so results are bit-identical); vectors with
+// v >= nv are skipped.
+template <int D, int NV>
+__device__ __forceinline__ void rot_multi(const float* x, int ldx, int nv, const float* T, int j,
+                                          float (&acc)[NV]) {
+#pragma unroll
+  for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < D; ++i) {
+    const float t = T[i * D + j];
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+      if (v < nv) acc[v] = fmaf(x[v * ldx + i], t, acc[v]);
+  }
+}
+
+// Word w of a packed row: LSB-first stream of `bits`-bit codes taken in the
+// order ord[position] -> coordinate.
+__device__ __forceinline__ uint32_t pack_word(const uint8_t* code, const int16_t* ord, int bits,
+                                              int w, int D) {
+  const int b0 = 32 * w;
+  const int n0 = b0 / bits, n1 = (b0 + 31) / bits;
+  uint64_t acc = 0;
+  for (int n = n0; n <= n1 && n < D; ++n) {
+    const uint64_t cv = code[ord[n]];
+    const int rel = n * bits - b0;
+    acc |= rel >= 0 ? (cv << rel) : (cv >> (-rel));
+  }
+  return (uint32_t)acc;
+}
+
+// Word w of a QJL row from 0/1 signs; qinv[bit] -> coordinate.
+__device__ __forceinline__ uint32_t pack_qjl_word(const uint8_t* qb, const int16_t* qinv, int w) {
+  uint32_t word = 0;
+  for (int bit = 0; bit < 32; ++bit) word |= (uint32_t)qb[qinv[32 * w + bit]] << bit;
+  return word;
+}
+
+// Position -> coordinate tables of the K (quad) and V (octet) row orders and
+// the QJL bit -> coordinate table.
+__device__ __forceinline__ void build_orders(int16_t* ordk, int16_t* ordv, int16_t* qinv, int D,
+                                             int tid, int nthreads) {
+  for (int c = tid; c < D; c += nthreads) {
+    const int kp = k_pos_of(c, D);
+    if (ordk) ordk[kp] = (int16_t)c;
+    if (qinv) qinv[qjl_bit_of(kp, D)] = (int16_t)c;
+    if (ordv) ordv[v_pos_of(c, D)] = (int16_t)c;
+  }
+}
+
+}  // namespace tq

@@ -340,6 +340,36 @@ class _LayerKVStore:
                                     self._win_k, self._win_v, scale=scale, out=out,
                                     workspace=self.workspace)
 
+    def decode(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, residual_window: int,
+               scale: Optional[float] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Store one new token and attend q to everything stored, in one fused
+        call when exactly one token moves into packed storage this step."""
+        B, H, T, D = k.shape
+        self._lazy_alloc(B, H)
+        k = k.to(self.dtype)
+        v = v.to(self.dtype)
+        W = 0 if self._win_k is None else self._win_k.shape[2]
+        if T == 1 and residual_window <= 0 and W == 0:
+            self._ensure_capacity(1)
+            out = ops.decode_step(self.tables, self._pages, k, v, self._comp_ptr, q, scale=scale,
+                                  out=out, workspace=self.workspace)
+            self._comp_ptr += 1
+            return out
+        if T == 1 and 0 < residual_window == W:
+            # the oldest window token is evicted into packed storage
+            ek, ev = self._win_k[:, :, :1], self._win_v[:, :, :1]
+            wk = torch.cat([self._win_k[:, :, 1:], k], dim=2)
+            wv = torch.cat([self._win_v[:, :, 1:], v], dim=2)
+            self._ensure_capacity(1)
+            out = ops.decode_step(self.tables, self._pages, ek, ev, self._comp_ptr, q,
+                                  window_k=wk, window_v=wv, scale=scale, out=out,
+                                  workspace=self.workspace)
+            self._comp_ptr += 1
+            self._win_k, self._win_v = wk, wv
+            return out
+        self.store(k, v, residual_window)
+        return self.attend(q, scale=scale, out=out)
+
     def reset(self) -> None:
         self._comp_ptr = 0
         self._win_k = self._win_v = None
@@ -423,6 +453,16 @@ class TurboQuantKVCache(BaseKVCache):
         """Decode attention of a single-token query (B, Hq, 1, D) over layer
         ``layer_idx``'s packed history and window (GQA: Hq % Hkv == 0)."""
         return self._stores[layer_idx].attend(query_states, scale=scale, out=out)
+
+    def decode(self, query_states: torch.Tensor, key_states: torch.Tensor,
+               value_states: torch.Tensor, layer_idx: int, scale: Optional[float] = None,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One decode step of one layer: store the new token(s) (reference
+        update() semantics, including the residual window) and return the
+        attention of query_states (B, Hq, 1, D) over the whole cache, without
+        materialising dense K/V."""
+        return self._stores[layer_idx].decode(query_states, key_states, value_states,
+                                              self.residual_window, scale=scale, out=out)
 
     def device_status(self) -> int:
         """OR of the device status words of all layers (synchronises)."""

@@ -157,6 +157,51 @@ class DecodeWorkspace:
         return int(st.value)
 
 
+def _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, keep):
+    qt, ot = tensor4(q), tensor4(out)
+    wk = tensor4(window_k) if window_k is not None and window_k.shape[2] > 0 else None
+    wv = tensor4(window_v) if wk is not None else None
+    keep += [qt, ot, wk, wv]
+    a = _lib.DecodeArgs()
+    a.q = ctypes.pointer(qt)
+    a.out = ctypes.pointer(ot)
+    a.window_k = ctypes.pointer(wk) if wk is not None else None
+    a.window_v = ctypes.pointer(wv) if wv is not None else None
+    a.n_tokens = int(n_tokens)
+    a.num_q_heads = q.shape[1]
+    a.scale = float(scale if scale is not None else 1.0 / math.sqrt(q.shape[-1]))
+    a.num_ctas = int(num_ctas)
+    a.phases = int(phases)
+    return a
+
+
+def decode_step(tables: LayerTables, pages: torch.Tensor, k_new: torch.Tensor,
+                v_new: torch.Tensor, pos: int, q: torch.Tensor,
+                window_k: Optional[torch.Tensor] = None,
+                window_v: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                out: Optional[torch.Tensor] = None,
+                workspace: Optional[DecodeWorkspace] = None,
+                num_ctas: int = 0) -> torch.Tensor:
+    """Store the new (B, Hkv, 1, D) token at ``pos`` and attend q over tokens
+    [0, pos + 1) plus the window, in one call (tq_decode_step)."""
+    _require_cuda(pages, q, k_new, v_new)
+    lib = _lib.load()
+    if out is None:
+        out = torch.empty_like(q)
+    g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
+    keep = []
+    a = _decode_args(q, out, pos + 1, window_k, window_v, scale, num_ctas, 0, keep)
+    kt, vt = tensor4(k_new), tensor4(v_new)
+    nbytes = lib.tq_decode_workspace_bytes(ctypes.byref(g), ctypes.byref(c), ctypes.byref(a))
+    if nbytes == 0:
+        raise _lib.TqError("tq_decode_workspace_bytes", _lib.TQ_ERR_INVALID, _lib.last_error())
+    ws = (workspace or DecodeWorkspace()).get(nbytes, q.device)
+    _lib.check("tq_decode_step", lib.tq_decode_step(
+        ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(kt), ctypes.byref(vt),
+        int(pos), ctypes.byref(a), ws.data_ptr(), ws.numel(), _stream(q.device)))
+    return out
+
+
 def decode_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
                      n_tokens: int, window_k: Optional[torch.Tensor] = None,
                      window_v: Optional[torch.Tensor] = None, scale: Optional[float] = None,
@@ -172,23 +217,9 @@ def decode_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
     lib = _lib.load()
     if out is None:
         out = torch.empty_like(q)
-    D = q.shape[-1]
-    if scale is None:
-        scale = 1.0 / math.sqrt(D)
     g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
-    qt, ot = tensor4(q), tensor4(out)
-    wk = tensor4(window_k) if window_k is not None and window_k.shape[2] > 0 else None
-    wv = tensor4(window_v) if wk is not None else None
-    a = _lib.DecodeArgs()
-    a.q = ctypes.pointer(qt)
-    a.out = ctypes.pointer(ot)
-    a.window_k = ctypes.pointer(wk) if wk is not None else None
-    a.window_v = ctypes.pointer(wv) if wv is not None else None
-    a.n_tokens = int(n_tokens)
-    a.num_q_heads = q.shape[1]
-    a.scale = float(scale)
-    a.num_ctas = int(num_ctas)
-    a.phases = int(phases)
+    keep = []
+    a = _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, keep)
     nbytes = lib.tq_decode_workspace_bytes(ctypes.byref(g), ctypes.byref(c), ctypes.byref(a))
     if nbytes == 0:
         raise _lib.TqError("tq_decode_workspace_bytes", _lib.TQ_ERR_INVALID, _lib.last_error())

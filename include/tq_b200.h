@@ -153,6 +153,19 @@ int32_t tq_decode_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                        const tq_decode_args* a, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* One decode step of one layer: quantise and store the new token of every
+ * stream (k_new, v_new: (B, Hkv, 1, D)) at position `pos`, then attend q
+ * over tokens [0, pos + 1) plus the window.  a->n_tokens must be pos + 1.
+ * Same pages and outputs as tq_append(..., pos) followed by tq_decode_attn,
+ * but the append is fused into the query preparation (three kernels, each
+ * launched so its prologue overlaps the previous kernel).  Replaces the
+ * per-layer update() + attention of a decode step (kv_cache.py:445-490 then
+ * engine.py:389).  Workspace from tq_decode_workspace_bytes(). */
+int32_t tq_decode_step(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                       const tq_tensor4* k_new, const tq_tensor4* v_new, int64_t pos,
+                       const tq_decode_args* a, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
 /* Read and clear the device status word kept at the start of a decode
  * workspace (blocking copy on `stream`). */
 int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream);

@@ -351,3 +351,49 @@ def test_full_size_mixtral_decode_property():
     want = F.scaled_dot_product_attention(q.float(), dk, dv, enable_gqa=True)
     assert cosine(got.cpu(), want.cpu()) >= 0.9995
     assert (got - want).abs().max().item() <= 1e-2
+
+
+# ------------------------------------------------------- fused decode step
+@pytest.mark.parametrize("D,kb,vb,qjl,B,Hkv,g,T,W", [
+    (128, 4, 2, True, 2, 4, 4, 300, 0), (128, 3, 3, False, 1, 2, 5, 64, 0),
+    (64, 4, 2, True, 1, 2, 8, 17, 6), (128, 6, 4, True, 1, 1, 16, 129, 0),
+    (32, 4, 2, False, 2, 1, 3, 0, 0)])
+def test_decode_step_equals_append_then_attend(D, kb, vb, qjl, B, Hkv, g, T, W):
+    """tq_decode_step writes the same page bytes as tq_append and returns the
+    same output as tq_decode_attn over tokens [0, T + 1)."""
+    t = make_tables(D, kb, vb, qjl)
+    k, v = rand_kv((B, Hkv, T + 1, D), 30).to(DEV), rand_kv((B, Hkv, T + 1, D), 31).to(DEV)
+    q = rand_kv((B, Hkv * g, 1, D), 32, outliers=0).to(DEV)
+    wk = rand_kv((B, Hkv, W, D), 33).to(DEV) if W else None
+    wv = rand_kv((B, Hkv, W, D), 34).to(DEV) if W else None
+    pa, pb = new_pages(B * Hkv, T + 1, t), new_pages(B * Hkv, T + 1, t)
+    if T:
+        ops.append(t, pa, k[:, :, :T], v[:, :, :T], 0)
+        ops.append(t, pb, k[:, :, :T], v[:, :, :T], 0)
+    ops.append(t, pa, k[:, :, T:], v[:, :, T:], T)
+    want = ops.decode_attention(t, pa, q, T + 1, wk, wv)
+    got = ops.decode_step(t, pb, k[:, :, T:], v[:, :, T:], T, q, wk, wv)
+    torch.cuda.synchronize()
+    assert torch.equal(pa, pb)
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("rw", [0, 4])
+def test_cache_decode_matches_store_then_attend(rw):
+    B, Hkv, g, T, D = 2, 4, 4, 150, 128
+    kw = dict(num_layers=1, batch_size=B, num_heads=Hkv, head_dim=D, key_bits=4, value_bits=2,
+              residual_window=rw, protected_layers=0, dtype=torch.bfloat16, device=DEV,
+              max_seq_len=T + 8, qjl=True)
+    c1, c2 = TurboQuantKVCache(**kw), TurboQuantKVCache(**kw)
+    k, v = rand_kv((B, Hkv, T + 5, D), 40).to(DEV), rand_kv((B, Hkv, T + 5, D), 41).to(DEV)
+    c1.append(k[:, :, :T], v[:, :, :T], 0)
+    c2.append(k[:, :, :T], v[:, :, :T], 0)
+    for i in range(5):
+        q = rand_kv((B, Hkv * g, 1, D), 50 + i, outliers=0).to(DEV)
+        kt, vt = k[:, :, T + i:T + i + 1], v[:, :, T + i:T + i + 1]
+        got = c1.decode(q, kt, vt, 0)
+        c2.append(kt, vt, 0)
+        want = c2.attend(q, 0)
+        assert torch.equal(got, want), i
+    assert torch.equal(c1._stores[0]._pages, c2._stores[0]._pages)
+    assert c1.device_status() == 0
