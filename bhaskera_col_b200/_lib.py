@@ -26,7 +26,7 @@ PHASE_QPREP, PHASE_DECODE, PHASE_MERGE = 1, 2, 4
 EXPORTED = (
     "tq_last_error", "tq_version", "tq_page_bytes", "tq_quantize_rotated",
     "tq_append", "tq_dequantize", "tq_decode_workspace_bytes", "tq_decode_attn",
-    "tq_decode_step", "tq_workspace_status",
+    "tq_decode_step", "tq_decode_attn_noalloc", "tq_workspace_status",
 )
 
 
@@ -97,6 +97,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             "tq_decode_attn": (I32, [P(Geom), P(Tables), P(Cache), P(DecodeArgs), VP, SZ, VP]),
             "tq_decode_step": (I32, [P(Geom), P(Tables), P(Cache), P(Tensor4), P(Tensor4), I64,
                                      P(DecodeArgs), VP, SZ, VP]),
+            "tq_decode_attn_noalloc": (I32, [P(Geom), P(Tables), P(Cache), P(DecodeArgs), VP]),
             "tq_workspace_status": (I32, [VP, P(ctypes.c_uint32), VP]),
         }
         for name, (res, args) in sig.items():

@@ -166,6 +166,19 @@ int32_t tq_decode_step(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                        const tq_decode_args* a, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* tq_decode_attn for callers that cannot allocate device memory (a runtime
+ * that owns all device memory through its own pool, or code that must not
+ * call an allocator while serving).  Same arguments and result as
+ * tq_decode_attn, minus the workspace: the scratch is a fixed 8 MiB array
+ * inside this library (held on every GPU that loads it until exit).  Calls
+ * needing more scratch than that fail with TQ_ERR_WORKSPACE.  The first call
+ * on a device looks the array's address up (do it before any stream
+ * capture).  Calls share the array, so calls that overlap on the GPU race;
+ * serialise them.  Device-side wait timeouts are recorded in the array's
+ * status word, which each call clears.  No counterpart in the reference. */
+int32_t tq_decode_attn_noalloc(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                               const tq_decode_args* a, void* stream);
+
 /* Read and clear the device status word kept at the start of a decode
  * workspace (blocking copy on `stream`). */
 int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream);
