@@ -139,14 +139,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `hint_ns`
+// (instead of a short system default) while the phase is incomplete, so a
+// waiting warp costs no issue slots.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity,
+                                                   uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: returns false (and never hangs) if the phase does not
-// complete within ~`limit` polls.
+// complete within `limit` suspended polls of at most 1 ms each.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  uint32_t limit = (1u << 22)) {
-  for (uint32_t i = 0; i < limit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (i > 64) __nanosleep(64);
-  }
+                                                  uint32_t limit = 1000u) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
   return false;
 }
 

@@ -36,7 +36,7 @@ namespace tq {
 
 constexpr int kConsumerWarps = 4;
 constexpr int kDecThreads = 32 * (kConsumerWarps + 1);   // + one producer warp
-constexpr int kStages = 4;
+constexpr int kStages = 5;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegInf = -INFINITY;
 
@@ -107,13 +107,13 @@ __device__ __forceinline__ uint32_t getbits(const uint32_t (&w)[NW], int o, int 
   return v & ((1u << n) - 1u);
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t byte_off) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  return *reinterpret_cast<const uint32_t*>(smem + byte_off);
+// Loads from a lookup table in (static) shared memory; with a static table
+// the table's address folds into the load's immediate offset.
+__device__ __forceinline__ uint32_t lds32(const unsigned char* base, uint32_t byte_off) {
+  return *reinterpret_cast<const uint32_t*>(base + byte_off);
 }
-__device__ __forceinline__ uint32_t lds16(uint32_t byte_off) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  return *reinterpret_cast<const unsigned short*>(smem + byte_off);
+__device__ __forceinline__ uint32_t lds16(const unsigned char* base, uint32_t byte_off) {
+  return *reinterpret_cast<const unsigned short*>(base + byte_off);
 }
 
 // Load NBITS bits starting at bit `bit_off` of a 4-byte aligned shared row.
@@ -176,11 +176,14 @@ struct Dec {
   static constexpr int OFF_KN = OFF_Q + 64 * QROW, OFF_VN = OFF_KN + 128, OFF_KR = OFF_VN + 128;
   static constexpr int PAGE = OFF_KR + (QJL ? 128 : 0);
   static constexpr int PB = align128(PAGE);
-  // shared memory map: [K table | combine scratch] [V table] [stages] [barriers]
+  // static shared memory: the K table (aliased by the combine scratch) and,
+  // when both fit, the V table.  Dynamic: [V table] [stages] [barriers].
   static constexpr int COMB = kConsumerWarps * (16 + 8 * D) * 4;
   static constexpr int REGION0 = align128(cmax(Lut<KB>::kBytes, COMB));
-  static constexpr int LUTV = REGION0;
-  static constexpr int STAGE0 = align128(LUTV + Lut<VB>::kBytes);
+  static constexpr bool VSTATIC = REGION0 + Lut<VB>::kBytes <= 45 * 1024;
+  static constexpr int LUTV_STATIC = VSTATIC ? Lut<VB>::kBytes : 16;
+  static constexpr int LUTV = 0;   // offset of the V table in the dynamic region
+  static constexpr int STAGE0 = VSTATIC ? 0 : align128(Lut<VB>::kBytes);
   static constexpr int BARS = STAGE0 + kStages * PB;
   static constexpr int SMEM = BARS + 2 * kStages * 8;
 };
@@ -202,6 +205,10 @@ decode_kernel(DecodeParams p) {
   constexpr int SP = (D / 8) < 16 ? (D / 8) : 16;
   constexpr bool VINTER = Lut<VB>::kPair && (32 % VB == 0) && VOA;
 
+  __shared__ __align__(128) unsigned char s_lut0[G::REGION0];
+  __shared__ __align__(128) unsigned char s_lutv_static[G::LUTV_STATIC];
+  unsigned char* lutk = s_lut0;
+  unsigned char* lutv = G::VSTATIC ? s_lutv_static : smem + G::LUTV;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::BARS);
   uint64_t* empty = full + kStages;
   __shared__ int s_abort;
@@ -212,6 +219,7 @@ decode_kernel(DecodeParams p) {
   const int64_t gp0 = (int64_t)blockIdx.x * p.Q;
   const int64_t gp1 = tmin<int64_t>(gp0 + p.Q, TP);
   const int npages = (int)tmax<int64_t>(0, gp1 - gp0);
+  const int T32 = (int)p.T, Pv32 = (int)p.Pv;   // token and page indices fit 32 bits
   constexpr int NCT = 32 * kConsumerWarps;   // consumer threads
 
   if (tid == 0) {
@@ -224,8 +232,8 @@ decode_kernel(DecodeParams p) {
   }
   pdl_launch_dependents();
   if (warp < kConsumerWarps) {
-    build_lut<KB>(smem, p.kc, tid, NCT);
-    build_lut<VB>(smem + G::LUTV, p.vc, tid, NCT);
+    build_lut<KB>(lutk, p.kc, tid, NCT);
+    build_lut<VB>(lutv, p.vc, tid, NCT);
   }
   __syncthreads();
   pdl_wait();   // pages and query fragments come from the preceding kernels
@@ -250,7 +258,7 @@ decode_kernel(DecodeParams p) {
       }
       if (s_abort) {   // never leave with a copy still writing shared memory
         for (int i = tmax(0, npages - kStages); i < npages; ++i)
-          mbar_wait_bounded(&full[i % kStages], (uint32_t)((i / kStages) & 1), 1u << 16);
+          mbar_wait_bounded(&full[i % kStages], (uint32_t)((i / kStages) & 1), 16u);
       }
     }
     return;
@@ -284,9 +292,10 @@ decode_kernel(DecodeParams p) {
   };
   reset_state();
 
-  int64_t s = gp0 / p.Pv, pg = gp0 - s * p.Pv;   // advanced incrementally below
+  int64_t s = gp0 / p.Pv;                       // advanced incrementally below
+  int pg = (int)(gp0 - s * p.Pv);
   for (int i = 0; i < npages; ++i, ++pg) {
-    if (pg == p.Pv) { pg = 0; ++s; }
+    if (pg == Pv32) { pg = 0; ++s; }
     const int st = i % kStages;
     if (s != cur_s) { load_q(s); cur_s = s; }
     if (!s_abort && !mbar_wait_bounded(&full[st], (uint32_t)((i / kStages) & 1))) {
@@ -294,9 +303,9 @@ decode_kernel(DecodeParams p) {
       s_abort = 1;
     }
     const uint8_t* pgb = smem + G::STAGE0 + st * G::PB;
-    const int64_t tok0 = pg * kPageTokens + warp * 16;
+    const int tok0 = pg * kPageTokens + warp * 16;
 
-    if (tok0 < p.T) {
+    if (tok0 < T32) {
       // ---------------- scores: S^T tile (16 tokens x 8 heads) --------------
       const int r0 = warp * 16 + gq, r1 = r0 + 8;
       uint32_t wk0[KQW], wk1[KQW];
@@ -314,15 +323,15 @@ decode_kernel(DecodeParams p) {
         uint32_t a[4];
         const int o0 = (4 * j) * KB, o1 = (4 * j + 2) * KB;   // quad entries 4j.., 4j+2..
         if constexpr (Lut<KB>::kPair) {
-          a[0] = lds32(field_addr<2 * KB>(wk0, o0, lane4));
-          a[1] = lds32(field_addr<2 * KB>(wk1, o0, lane4));
-          a[2] = lds32(field_addr<2 * KB>(wk0, o1, lane4));
-          a[3] = lds32(field_addr<2 * KB>(wk1, o1, lane4));
+          a[0] = lds32(lutk, field_addr<2 * KB>(wk0, o0, lane4));
+          a[1] = lds32(lutk, field_addr<2 * KB>(wk1, o0, lane4));
+          a[2] = lds32(lutk, field_addr<2 * KB>(wk0, o1, lane4));
+          a[3] = lds32(lutk, field_addr<2 * KB>(wk1, o1, lane4));
         } else {
-          a[0] = lds16(getbits(wk0, o0, KB) << 1) | (lds16(getbits(wk0, o0 + KB, KB) << 1) << 16);
-          a[1] = lds16(getbits(wk1, o0, KB) << 1) | (lds16(getbits(wk1, o0 + KB, KB) << 1) << 16);
-          a[2] = lds16(getbits(wk0, o1, KB) << 1) | (lds16(getbits(wk0, o1 + KB, KB) << 1) << 16);
-          a[3] = lds16(getbits(wk1, o1, KB) << 1) | (lds16(getbits(wk1, o1 + KB, KB) << 1) << 16);
+          a[0] = lds16(lutk, getbits(wk0, o0, KB) << 1) | (lds16(lutk, getbits(wk0, o0 + KB, KB) << 1) << 16);
+          a[1] = lds16(lutk, getbits(wk1, o0, KB) << 1) | (lds16(lutk, getbits(wk1, o0 + KB, KB) << 1) << 16);
+          a[2] = lds16(lutk, getbits(wk0, o1, KB) << 1) | (lds16(lutk, getbits(wk0, o1 + KB, KB) << 1) << 16);
+          a[3] = lds16(lutk, getbits(wk1, o1, KB) << 1) | (lds16(lutk, getbits(wk1, o1 + KB, KB) << 1) << 16);
         }
         mma_f16_16816(acc, a, qf[j][0], qf[j][1]);
         if constexpr (QJL) {
@@ -341,7 +350,7 @@ decode_kernel(DecodeParams p) {
       }
       const __half* kn = reinterpret_cast<const __half*>(pgb + G::OFF_KN);
       const __half* vn = reinterpret_cast<const __half*>(pgb + G::OFF_VN);
-      const bool ok0 = tok0 + gq < p.T, ok1 = tok0 + gq + 8 < p.T;
+      const bool ok0 = tok0 + gq < T32, ok1 = tok0 + gq + 8 < T32;
       const float n0 = __half2float(kn[r0]), n1 = __half2float(kn[r1]);
       float s00 = acc[0] * n0, s01 = acc[1] * n0, s10 = acc[2] * n1, s11 = acc[3] * n1;
       if constexpr (QJL) {
@@ -411,10 +420,10 @@ decode_kernel(DecodeParams p) {
           const int c0 = 2 * i2;                     // even position -> lo, odd -> hi
           const int o = ((c0 % PER) & ~1) * VB + (c0 / PER) * 32;
           uint32_t a[4];
-          a[0] = lds32(G::LUTV + field_addr<2 * VB>(lab, o, lane4));
-          a[1] = lds32(G::LUTV + field_addr<2 * VB>(hab, o, lane4));
-          a[2] = lds32(G::LUTV + field_addr<2 * VB>(lcd, o, lane4));
-          a[3] = lds32(G::LUTV + field_addr<2 * VB>(hcd, o, lane4));
+          a[0] = lds32(lutv, field_addr<2 * VB>(lab, o, lane4));
+          a[1] = lds32(lutv, field_addr<2 * VB>(hab, o, lane4));
+          a[2] = lds32(lutv, field_addr<2 * VB>(lcd, o, lane4));
+          a[3] = lds32(lutv, field_addr<2 * VB>(hcd, o, lane4));
           mma_f16_16816(O[i2], a, pb0, pb1);
         }
       } else {
@@ -423,15 +432,15 @@ decode_kernel(DecodeParams p) {
           const int c0p = (2 * i2) * VB, c1p = (2 * i2 + 1) * VB;
           uint32_t a[4];
           if constexpr (Lut<VB>::kPair) {
-            a[0] = lds32(G::LUTV + (((getbits(wb, c0p, VB) << VB) | getbits(wa, c0p, VB)) << 7 | lane4));
-            a[1] = lds32(G::LUTV + (((getbits(wb, c1p, VB) << VB) | getbits(wa, c1p, VB)) << 7 | lane4));
-            a[2] = lds32(G::LUTV + (((getbits(wd, c0p, VB) << VB) | getbits(wc, c0p, VB)) << 7 | lane4));
-            a[3] = lds32(G::LUTV + (((getbits(wd, c1p, VB) << VB) | getbits(wc, c1p, VB)) << 7 | lane4));
+            a[0] = lds32(lutv, (((getbits(wb, c0p, VB) << VB) | getbits(wa, c0p, VB)) << 7 | lane4));
+            a[1] = lds32(lutv, (((getbits(wb, c1p, VB) << VB) | getbits(wa, c1p, VB)) << 7 | lane4));
+            a[2] = lds32(lutv, (((getbits(wd, c0p, VB) << VB) | getbits(wc, c0p, VB)) << 7 | lane4));
+            a[3] = lds32(lutv, (((getbits(wd, c1p, VB) << VB) | getbits(wc, c1p, VB)) << 7 | lane4));
           } else {
-            a[0] = lds16(G::LUTV + (getbits(wa, c0p, VB) << 1)) | (lds16(G::LUTV + (getbits(wb, c0p, VB) << 1)) << 16);
-            a[1] = lds16(G::LUTV + (getbits(wa, c1p, VB) << 1)) | (lds16(G::LUTV + (getbits(wb, c1p, VB) << 1)) << 16);
-            a[2] = lds16(G::LUTV + (getbits(wc, c0p, VB) << 1)) | (lds16(G::LUTV + (getbits(wd, c0p, VB) << 1)) << 16);
-            a[3] = lds16(G::LUTV + (getbits(wc, c1p, VB) << 1)) | (lds16(G::LUTV + (getbits(wd, c1p, VB) << 1)) << 16);
+            a[0] = lds16(lutv, (getbits(wa, c0p, VB) << 1)) | (lds16(lutv, (getbits(wb, c0p, VB) << 1)) << 16);
+            a[1] = lds16(lutv, (getbits(wa, c1p, VB) << 1)) | (lds16(lutv, (getbits(wb, c1p, VB) << 1)) << 16);
+            a[2] = lds16(lutv, (getbits(wc, c0p, VB) << 1)) | (lds16(lutv, (getbits(wd, c0p, VB) << 1)) << 16);
+            a[3] = lds16(lutv, (getbits(wc, c1p, VB) << 1)) | (lds16(lutv, (getbits(wd, c1p, VB) << 1)) << 16);
           }
           mma_f16_16816(O[i2], a, pb0, pb1);
         }
@@ -439,7 +448,7 @@ decode_kernel(DecodeParams p) {
     }
 
     // ---------------- segment end: combine warps, emit partial ---------------
-    const bool seg_end = (pg == p.Pv - 1) || (i == npages - 1);
+    const bool seg_end = (pg == Pv32 - 1) || (i == npages - 1);
     if (seg_end) {
       float L0 = l0, L1 = l1;
 #pragma unroll
@@ -448,7 +457,7 @@ decode_kernel(DecodeParams p) {
         L1 += __shfl_xor_sync(0xffffffffu, L1, o);
       }
       named_bar(1, NCT);                       // everyone is done with the K table
-      float* comb = reinterpret_cast<float*>(smem);
+      float* comb = reinterpret_cast<float*>(lutk);
       float* cm = comb + warp * (16 + 8 * D);
       float* cl = cm + 8;
       float* co = cm + 16;
@@ -490,7 +499,7 @@ decode_kernel(DecodeParams p) {
       }
       named_bar(1, NCT);
       if (i != npages - 1) {                   // restore the K table
-        build_lut<KB>(smem, p.kc, tid, NCT);
+        build_lut<KB>(lutk, p.kc, tid, NCT);
         named_bar(1, NCT);
       }
       reset_state();
