@@ -26,7 +26,8 @@ PHASE_QPREP, PHASE_DECODE, PHASE_MERGE = 1, 2, 4
 EXPORTED = (
     "tq_last_error", "tq_version", "tq_page_bytes", "tq_quantize_rotated",
     "tq_append", "tq_dequantize", "tq_decode_workspace_bytes", "tq_decode_attn",
-    "tq_decode_step", "tq_decode_attn_noalloc", "tq_workspace_status",
+    "tq_decode_step", "tq_decode_attn_noalloc", "tq_workspace_status", "tq_device_status",
+    "tq_append_tensor_core",
 )
 
 
@@ -47,7 +48,8 @@ class Tables(ctypes.Structure):
     _fields_ = [("k_centroids", ctypes.c_void_p), ("k_boundaries", ctypes.c_void_p),
                 ("v_centroids", ctypes.c_void_p), ("v_boundaries", ctypes.c_void_p),
                 ("rot", ctypes.c_void_p), ("qjl", ctypes.c_void_p),
-                ("rot_t", ctypes.c_void_p), ("qjl_t", ctypes.c_void_p)]
+                ("rot_t", ctypes.c_void_p), ("qjl_t", ctypes.c_void_p),
+                ("rot_bf16x3", ctypes.c_void_p)]
 
 
 class Cache(ctypes.Structure):

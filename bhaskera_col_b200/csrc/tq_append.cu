@@ -275,6 +275,7 @@ int launch_append(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   p.pos = pos;
   const int64_t nvec = p.B * p.H * p.T;
   if (nvec == 0) return TQ_OK;
+  if (const int rc = launch_append_tc(G, t, c, k, v, pos, st); rc != 1) return rc;
   const size_t smem = append_smem_bytes(p.g.D, p.g.qjl != 0);
   void (*fn)(AppendParams) = p.g.D == 32 ? append_kernel<32>
                            : p.g.D == 64 ? append_kernel<64>

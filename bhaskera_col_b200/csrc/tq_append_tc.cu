@@ -1,0 +1,473 @@
+// tq_append_tc.cu — tensor-core append for head_dim 128 (no QJL sketch).
+//
+// Same result as append_kernel (kv_cache.py:382-398: fp32 norm of x,
+// u = x / max(n, 1e-8), y = u R^T, codes = bucketize(y), fp16 norm) with the
+// rotation on tcgen05 tensor cores:
+//   * x (bf16) tiles of 128 consecutive tokens of one stream are loaded
+//     exactly by TMA (128-byte swizzle, two 64-column halves);
+//   * R = R_hi + R_mid + R_lo, three bf16 terms (24 significant bits), so
+//     x R^T is the sum of three exact bf16 x bf16 products accumulated in fp32
+//     in tensor memory (codes differ from an fp32 matmul only where y sits
+//     within rounding of a boundary);
+//   * the rows of each R term are permuted into the packed order of the row
+//     (K quad order / V octet order), so TMEM column p holds the coordinate
+//     stored at position p and every thread packs consecutive positions;
+//   * the norm is ||x|| in fp32, summed from the bf16 tile in shared memory;
+//   * one warp issues TMA, one warp issues the MMAs (M = N = 128, K = 16;
+//     24 per tile) into one of two TMEM accumulators; kSplit epilogue warps
+//     per TMEM lane quarter each take 128 / kSplit positions of 32 vectors.
+//
+// Bucketize: v = y / max(n, 1e-8) lies in [-1, 1].  With w = 0.4 x the
+// smallest boundary gap, cell c = round(v / w) + L (L = ceil(1.0625 / w) + 2,
+// one FFMA against 2^23 + L, whose float holds the integer in its low bits)
+// has the window [c - L - 1, c - L + 1] x w around v with at most one boundary
+// in it; the table holds {#boundaries below the window, that boundary or +inf},
+// so code = base + (v > b) = #{boundaries < v} exactly (torch.bucketize,
+// right=False).  Tables whose boundaries leave (-1, 1) or need more than
+// kMaxCells cells use a binary search instead.
+//
+// Every wait is bounded (mbar_wait_bounded); on expiry the kernel sets
+// TQ_DEV_WAIT_TIMEOUT in a device status word (tq_device_status), drains its
+// own copies and MMAs, frees its tensor memory and returns.
+#include "tq_common.cuh"
+#include "tq_internal.h"
+#include "tq_tc.cuh"
+
+#include <mutex>
+
+namespace tq {
+namespace {
+
+constexpr int kD = 128;
+constexpr int kM = 128;                    // vectors (tokens of one stream) per tile
+constexpr int kAStages = 3;
+constexpr int kHalf = kM * 64 * 2;         // 16 KB: 128 rows x 64 bf16, 128-byte swizzle
+constexpr int kABytes = 2 * kHalf;         // one x tile
+constexpr int kBBytes = 6 * kHalf;         // 3 terms of R x 2 K-halves
+constexpr int kMaxCells = 2048;
+constexpr int kSplit = 2;                  // epilogue warps per TMEM lane quarter
+constexpr int kCW = kD / kSplit;           // positions per epilogue thread
+constexpr int kEpiWarps = 4 * kSplit;
+constexpr int kThreads = 32 * (2 + kEpiWarps);   // warp 0 TMA, warp 1 MMA, then epilogue
+constexpr uint32_t kTmemCols = 256;        // two 128-column fp32 accumulators
+constexpr float kRange = 1.0625f;          // |v| <= 1 up to rounding
+
+constexpr int OFF_B = 0;
+constexpr int OFF_A = OFF_B + kBBytes;
+constexpr int OFF_LUT = OFF_A + kAStages * kABytes;
+constexpr int OFF_BND = OFF_LUT + kMaxCells * 8;
+constexpr int OFF_XN = OFF_BND + 256 * 4;                 // [2][kSplit][kM] partial ||x||^2
+constexpr int OFF_BAR = OFF_XN + 2 * kSplit * kM * 4;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;          // + slack to align the base to 1 KB
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+static_assert(OFF_A % 1024 == 0 && kABytes % 1024 == 0, "swizzled tiles need 1 KB alignment");
+
+struct TcParams {
+  const float* bnd;
+  int nb;
+  uint8_t* pages;
+  int64_t pages_per_stream;
+  int page_bytes, row_bytes, sec_off, norm_off;
+  int64_t H, T, pos, ntiles, nblk;
+};
+
+__device__ uint32_t g_tc_status;           // TQ_DEV_WAIT_TIMEOUT when a wait expired
+
+__device__ __forceinline__ void fail() { atomicOr(&g_tc_status, TQ_DEV_WAIT_TIMEOUT); }
+
+// bar.sync on a named barrier with an AND-reduction of `pred`: every thread
+// of the group gets the same answer.
+__device__ __forceinline__ bool group_and(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n"
+      " bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(nthreads) : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+template <int BITS>
+__global__ void __launch_bounds__(kThreads, 1)
+append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+                 TcParams p, int b_row0) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* b_full = bars;                      // 1
+  uint64_t* a_full = bars + 1;                  // kAStages
+  uint64_t* a_empty = a_full + kAStages;        // kAStages
+  uint64_t* acc_full = a_empty + kAStages;      // 2
+  uint64_t* acc_empty = acc_full + 2;           // 2
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 3);
+  float* lutpar = reinterpret_cast<float*>(acc_empty + 4);   // 5 floats
+  float2* lut = reinterpret_cast<float2*>(sm + OFF_LUT);
+  float* bnd = reinterpret_cast<float*>(sm + OFF_BND);
+  float* xn = reinterpret_cast<float*>(sm + OFF_XN);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nb = p.nb;
+
+  if (tid == 0) {
+    mbar_init(b_full, 1);
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1 + kEpiWarps);    // MMA commit + every epilogue warp's x read
+    }
+    for (int a = 0; a < 2; ++a) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], kEpiWarps); }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  for (int i = tid; i < nb; i += kThreads) bnd[i] = p.bnd[i];
+  __syncthreads();
+  if (tid == 0) {
+    float gap = 1.f;
+    for (int i = 0; i + 1 < nb; ++i) gap = fminf(gap, bnd[i + 1] - bnd[i]);
+    const float w = 0.4f * gap;
+    const float L = ceilf(kRange / w) + 2.f;
+    const float nc = 2.f * L + 1.f;
+    const bool ok = w > 0.f && nc <= (float)kMaxCells && bnd[0] > -1.f && bnd[nb - 1] < 1.f;
+    lutpar[0] = 1.f / w;
+    lutpar[1] = ok ? 8388608.f + L : 0.f;    // exact: L < 2^11
+    lutpar[2] = ok ? nc : 0.f;
+    lutpar[3] = w;
+    lutpar[4] = L;
+  }
+  __syncthreads();
+  const int ncells = (int)lutpar[2];
+  const bool use_lut = ncells > 0;
+  {
+    const float w = lutpar[3], L = lutpar[4];
+    for (int c = tid; c < ncells; c += kThreads) {
+      const float wl = ((float)c - L - 1.f) * w, wh = ((float)c - L + 1.f) * w;
+      int base = 0, hi = nb;                 // #boundaries < wl
+      while (base < hi) {
+        const int mid = (base + hi) >> 1;
+        if (bnd[mid] < wl) base = mid + 1; else hi = mid;
+      }
+      const float b = (base < nb && bnd[base] <= wh) ? bnd[base] : INFINITY;
+      lut[c] = make_float2(__int_as_float(base), b);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(b_full, kBBytes);
+      for (int sp = 0; sp < 3; ++sp)
+        for (int kh = 0; kh < 2; ++kh)
+          tc::tma_load_2d(sm + OFF_B + (sp * 2 + kh) * kHalf, &bmap, kh * 64, b_row0 + sp * kD,
+                          b_full);
+      int it = 0, issued = 0;
+      for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++it) {
+        const int st = it % kAStages;
+        if (it >= kAStages &&
+            !mbar_wait_bounded(&a_empty[st], (uint32_t)(((it / kAStages) - 1) & 1))) {
+          fail();
+          *abort_flag = 1;
+        }
+        if (*abort_flag) break;
+        const int64_t s = tile / p.nblk, tb = tile % p.nblk;
+        const int b = (int)(s / p.H), h = (int)(s % p.H), t0 = (int)(tb * kM);
+        unsigned char* dst = sm + OFF_A + st * kABytes;
+        mbar_expect_tx(&a_full[st], kABytes);
+        tc::tma_load_4d(dst, &amap, 0, t0, h, b, &a_full[st]);
+        tc::tma_load_4d(dst + kHalf, &amap, 64, t0, h, b, &a_full[st]);
+        issued = it + 1;
+      }
+      // never leave with a copy still writing shared memory
+      for (int i = tmax(0, issued - kAStages); i < issued; ++i)
+        mbar_wait_bounded(&a_full[i % kAStages], (uint32_t)((i / kAStages) & 1), 16u);
+      mbar_wait_bounded(b_full, 0u, 16u);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(kM, kD);
+      const bool ok = mbar_wait_bounded(b_full, 0u);
+      if (!ok) { fail(); *abort_flag = 1; }
+      int it = 0, issued = 0;
+      const uint32_t bbase = smem_u32(sm + OFF_B);
+      for (int64_t tile = blockIdx.x; ok && tile < p.ntiles; tile += gridDim.x, ++it) {
+        const int st = it % kAStages, ac = it & 1;
+        if (*abort_flag ||
+            !mbar_wait_bounded(&a_full[st], (uint32_t)((it / kAStages) & 1)) ||
+            (it >= 2 && !mbar_wait_bounded(&acc_empty[ac], (uint32_t)(((it / 2) - 1) & 1)))) {
+          fail();
+          *abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t abase = smem_u32(sm + OFF_A + st * kABytes);
+        const uint32_t d = tmem + (uint32_t)(ac * kD);
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+            for (int sp = 0; sp < 3; ++sp) {
+              // K step of 16 bf16 = 32 bytes inside the 128-byte swizzled rows
+              const uint64_t ad = tc::sdesc_kmajor_sw128(abase + kh * kHalf + ks * 32);
+              const uint64_t bd = tc::sdesc_kmajor_sw128(bbase + (sp * 2 + kh) * kHalf + ks * 32);
+              tc::umma_bf16(d, ad, bd, idesc, (kh | ks | sp) ? 1u : 0u);
+            }
+        tc::umma_commit(&a_empty[st]);
+        tc::umma_commit(&acc_full[ac]);
+        issued = it + 1;
+      }
+      if (issued > 0)   // the last commit tracks every MMA issued before it
+        mbar_wait_bounded(&acc_full[(issued - 1) & 1], (uint32_t)(((issued - 1) / 2) & 1), 16u);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
+    const int q = warp & 3;                 // TMEM lane quarter this warp may read
+    const int part = ew >> 2;               // which kCW positions of the row
+    const int r = q * 32 + lane;            // tile row = vector
+    const float inv_w = lutpar[0], tofs = lutpar[1];
+    int it = 0;
+    for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++it) {
+      const int st = it % kAStages, ac = it & 1;
+      // (1) ||x||^2 over this part's kCW coordinates, from the swizzled tile
+      bool ok = !*abort_flag && mbar_wait_bounded(&a_full[st], (uint32_t)((it / kAStages) & 1));
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        const unsigned char* xa = sm + OFF_A + st * kABytes;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < kCW / 8; ++c) {
+          const int chunk = part * (kCW / 8) + c;        // 16-byte chunk of the row
+          const int half = chunk >> 3, c8 = chunk & 7;
+          const uint4 u = *reinterpret_cast<const uint4*>(xa + half * kHalf + r * 128 +
+                                                          ((c8 ^ (r & 7)) << 4));
+          s0 = fmaf(bf_lo(u.x), bf_lo(u.x), s0); s1 = fmaf(bf_hi(u.x), bf_hi(u.x), s1);
+          s0 = fmaf(bf_lo(u.y), bf_lo(u.y), s0); s1 = fmaf(bf_hi(u.y), bf_hi(u.y), s1);
+          s0 = fmaf(bf_lo(u.z), bf_lo(u.z), s0); s1 = fmaf(bf_hi(u.z), bf_hi(u.z), s1);
+          s0 = fmaf(bf_lo(u.w), bf_lo(u.w), s0); s1 = fmaf(bf_hi(u.w), bf_hi(u.w), s1);
+        }
+        xn[((it & 1) * kSplit + part) * kM + r] = s0 + s1;
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive_cta(&a_empty[st]);
+      }
+      // (2) the rotated row from tensor memory
+      uint32_t yb[kCW];
+      bool ok2 = ok && mbar_wait_bounded(&acc_full[ac], (uint32_t)((it / 2) & 1));
+      ok2 = __all_sync(0xffffffffu, ok2);
+      if (ok2) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kCW / 32; ++c)
+          tc::tmem_ld_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ac * kD + part * kCW + c * 32),
+                          *reinterpret_cast<uint32_t(*)[32]>(yb + c * 32));
+        tc::tmem_wait_ld();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive_cta(&acc_empty[ac]);
+      }
+      // (3) the lane quarter's kSplit warps agree to go on (named barrier 1 + q)
+      if (!group_and(1 + q, 32 * kSplit, ok2)) {
+        if (lane == 0) { fail(); *abort_flag = 1; }
+        break;
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int h = 0; h < kSplit; ++h) ss += xn[((it & 1) * kSplit + h) * kM + r];
+      const float n = sqrtf(ss);
+      const float inv = 1.f / fmaxf(n, 1e-8f);
+
+      constexpr int NW = kCW * BITS / 32;
+      uint32_t words[NW];
+#pragma unroll
+      for (int x = 0; x < NW; ++x) words[x] = 0u;
+#pragma unroll
+      for (int j = 0; j < kCW; ++j) {
+        const float v = __uint_as_float(yb[j]) * inv;
+        uint32_t code;
+        if (use_lut) {
+          const float vc = fminf(fmaxf(v, -kRange), kRange);
+          const int cell = __float_as_int(fmaf(vc, inv_w, tofs)) - 0x4B000000;
+          const float2 e = lut[cell];
+          code = (uint32_t)__float_as_int(e.x) + (v > e.y ? 1u : 0u);
+        } else {
+          code = (uint32_t)bucketize_lt(bnd, nb, v);
+        }
+        const int bo = j * BITS, wi = bo >> 5, sh = bo & 31;
+        if (sh + BITS <= 32) {
+          words[wi] = tc::bfi(code, words[wi], sh, BITS);
+        } else {
+          words[wi] = tc::bfi(code, words[wi], sh, 32 - sh);
+          words[wi + 1] = tc::bfi(code >> (32 - sh), words[wi + 1], 0, BITS - (32 - sh));
+        }
+      }
+      const int64_t s = tile / p.nblk, tb = tile % p.nblk;
+      const int64_t t = tb * kM + r;
+      if (t < p.T) {
+        const int64_t tp = p.pos + t;
+        uint8_t* page = p.pages + (s * p.pages_per_stream + tp / kPageTokens) * (int64_t)p.page_bytes;
+        const int slot = (int)(tp % kPageTokens);
+        uint8_t* row = page + p.sec_off + slot * p.row_bytes + part * (kCW * BITS / 8);
+        if constexpr (NW % 4 == 0) {
+#pragma unroll
+          for (int x = 0; x < NW / 4; ++x)
+            reinterpret_cast<uint4*>(row)[x] =
+                make_uint4(words[4 * x], words[4 * x + 1], words[4 * x + 2], words[4 * x + 3]);
+        } else {
+#pragma unroll
+          for (int x = 0; x < NW / 2; ++x)
+            reinterpret_cast<uint2*>(row)[x] = make_uint2(words[2 * x], words[2 * x + 1]);
+        }
+        if (part == 0) reinterpret_cast<__half*>(page + p.norm_off)[slot] = __float2half_rn(n);
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static std::once_flag once;
+  static EncodeTiled fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(f);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+using TcFn = void (*)(CUtensorMap, CUtensorMap, TcParams, int);
+
+TcFn tc_fn(int bits) {
+  switch (bits) {
+    case 1: return append_tc_kernel<1>;
+    case 2: return append_tc_kernel<2>;
+    case 3: return append_tc_kernel<3>;
+    case 4: return append_tc_kernel<4>;
+    case 5: return append_tc_kernel<5>;
+    case 6: return append_tc_kernel<6>;
+    case 7: return append_tc_kernel<7>;
+    case 8: return append_tc_kernel<8>;
+    default: return nullptr;
+  }
+}
+
+bool tc_view_ok(const tq_tensor4* x) {
+  if (x->dtype != TQ_BF16 || x->shape[3] != kD || x->stride[3] != 1) return false;
+  if (reinterpret_cast<uintptr_t>(x->data) % 16) return false;
+  for (int i = 0; i < 3; ++i)
+    if (x->stride[i] <= 0 || (x->stride[i] * 2) % 16) return false;
+  return true;
+}
+
+}  // namespace
+
+bool append_tc_applies(const tq_geom* G, const tq_tables* t, const tq_tensor4* k,
+                       const tq_tensor4* v) {
+  if (G->head_dim != kD || G->qjl || !t->rot_bf16x3) return false;
+  if (!tc_view_ok(k) || !tc_view_ok(v) || k->shape[2] < 32) return false;
+  if (!tc_fn(G->key_bits) || !tc_fn(G->value_bits)) return false;
+  if (reinterpret_cast<uintptr_t>(t->rot_bf16x3) % 16) return false;
+  return encoder() != nullptr;
+}
+
+// Returns TQ_OK when launched, 1 when this path does not apply (the caller
+// then uses the CUDA-core kernel), or an error.
+int launch_append_tc(const tq_geom* G, const tq_tables* t, const tq_cache* c,
+                     const tq_tensor4* k, const tq_tensor4* v, int64_t pos, cudaStream_t st) {
+  if (!append_tc_applies(G, t, k, v)) return 1;
+  EncodeTiled enc = encoder();
+  const PageGeom g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
+  // R terms: [2 orders][3 terms][128 rows][128] bf16, rows in packed order
+  CUtensorMap bmap;
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)kD, (cuuint64_t)(6 * kD)};
+    const cuuint64_t strides[1] = {(cuuint64_t)kD * 2};
+    const cuuint32_t box[2] = {64, kD};
+    const cuuint32_t es[2] = {1, 1};
+    if (enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)t->rot_bf16x3, dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return 1;
+  }
+  const int64_t B = k->shape[0], H = k->shape[1], T = k->shape[2];
+  const int64_t nblk = (T + kM - 1) / kM;
+  CUtensorMap amap[2];
+  for (int which = 0; which < 2; ++which) {
+    const tq_tensor4* x = which == 0 ? k : v;
+    const cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+    const cuuint64_t strides[3] = {(cuuint64_t)x->stride[2] * 2, (cuuint64_t)x->stride[1] * 2,
+                                   (cuuint64_t)x->stride[0] * 2};
+    const cuuint32_t box[4] = {64, kM, 1, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    if (enc(&amap[which], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, x->data, dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return 1;
+  }
+  TcFn fns[2] = {tc_fn(G->key_bits), tc_fn(G->value_bits)};
+  for (int which = 0; which < 2; ++which)
+    if (set_smem_attr((const void*)fns[which], SMEM_BYTES) != TQ_OK) return TQ_ERR_CUDA;
+  const int sms = device_sm_count();
+  for (int which = 0; which < 2; ++which) {
+    TcParams p;
+    p.bnd = which == 0 ? t->k_boundaries : t->v_boundaries;
+    p.nb = (1 << (which == 0 ? G->key_bits : G->value_bits)) - 1;
+    p.pages = c->pages;
+    p.pages_per_stream = c->pages_per_stream;
+    p.page_bytes = g.page_bytes;
+    p.row_bytes = which == 0 ? g.krow : g.vrow;
+    p.sec_off = which == 0 ? g.off_k : g.off_v;
+    p.norm_off = which == 0 ? g.off_kn : g.off_vn;
+    p.H = H; p.T = T; p.pos = pos;
+    p.nblk = nblk;
+    p.ntiles = B * H * nblk;
+    const int grid = (int)tmin<int64_t>(p.ntiles, (int64_t)sms);
+    fns[which]<<<grid, kThreads, SMEM_BYTES, st>>>(amap[which], bmap, p, which * 3 * kD);
+    if (check_launch("tq_append (tensor-core)") != TQ_OK) return TQ_ERR_CUDA;
+  }
+  return TQ_OK;
+}
+
+int read_tc_status(uint32_t* out, cudaStream_t st) {
+  void* addr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&addr, g_tc_status);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, addr, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(addr, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) {
+    set_error("tq_device_status: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return *out ? TQ_ERR_DEVICE : TQ_OK;
+}
+
+}  // namespace tq

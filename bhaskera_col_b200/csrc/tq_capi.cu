@@ -322,4 +322,15 @@ int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream) {
   return *status ? TQ_ERR_DEVICE : TQ_OK;
 }
 
+int32_t tq_append_tensor_core(const tq_geom* g, const tq_tables* t, const tq_tensor4* k,
+                              const tq_tensor4* v) {
+  if (!g || !t || !k || !v) return 0;
+  return append_tc_applies(g, t, k, v) ? 1 : 0;
+}
+
+int32_t tq_device_status(uint32_t* status, void* stream) {
+  if (!status) { set_error("tq_device_status: NULL argument"); return TQ_ERR_INVALID; }
+  return read_tc_status(status, (cudaStream_t)stream);
+}
+
 }  // extern "C"

@@ -24,6 +24,13 @@ int launch_quantize_rotated(const float* y, int64_t n, const float* b, int nb,
 int launch_append(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                   const tq_tensor4* k, const tq_tensor4* v, int64_t pos,
                   cudaStream_t st);
+// Tensor-core append (head_dim 128, bf16 inputs, no QJL): TQ_OK when it ran,
+// 1 when it does not apply (the caller uses the CUDA-core kernel), or an error.
+int launch_append_tc(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                     const tq_tensor4* k, const tq_tensor4* v, int64_t pos, cudaStream_t st);
+bool append_tc_applies(const tq_geom* g, const tq_tables* t, const tq_tensor4* k,
+                       const tq_tensor4* v);
+int read_tc_status(uint32_t* out, cudaStream_t st);
 int launch_dequant(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                    int64_t t0, int64_t t1, const tq_tensor4* ko, const tq_tensor4* vo,
                    cudaStream_t st);

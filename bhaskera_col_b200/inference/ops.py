@@ -57,10 +57,24 @@ class LayerTables:
     qjl_mat: Optional[torch.Tensor] = None
     rot_t: Optional[torch.Tensor] = None
     qjl_t: Optional[torch.Tensor] = None
+    rot_bf16x3: Optional[torch.Tensor] = None
 
     def __post_init__(self):
         self.rot = self.rot.contiguous().float()
         self.rot_t = self.rot.t().contiguous()
+        if self.head_dim == 128:
+            # R = hi + mid + lo in bf16 (24 significant bits): the tensor-core
+            # append computes x R^T as three exact bf16 products summed in fp32;
+            # rows permuted into the packed K / V orders (tq_tables.rot_bf16x3)
+            hi = self.rot.bfloat16()
+            r1 = self.rot - hi.float()
+            mid = r1.bfloat16()
+            lo = (r1 - mid.float()).bfloat16()
+            terms = torch.stack([hi, mid, lo])
+            ko, vo = row_orders(self.head_dim)
+            dev = self.rot.device
+            self.rot_bf16x3 = torch.stack([terms[:, torch.as_tensor(ko, device=dev)],
+                                           terms[:, torch.as_tensor(vo, device=dev)]]).contiguous()
         if self.qjl_mat is not None:
             self.qjl_mat = self.qjl_mat.contiguous().float()
             self.qjl_t = self.qjl_mat.t().contiguous()
@@ -78,7 +92,18 @@ class LayerTables:
         t.qjl = self.qjl_mat.data_ptr() if self.qjl_mat is not None else None
         t.rot_t = self.rot_t.data_ptr()
         t.qjl_t = self.qjl_t.data_ptr() if self.qjl_t is not None else None
+        t.rot_bf16x3 = self.rot_bf16x3.data_ptr() if self.rot_bf16x3 is not None else None
         return t
+
+
+def row_orders(head_dim: int):
+    """Coordinate stored at each position of a packed K row (quad order: quad t
+    lists 16j+2t, 16j+2t+1, 16j+2t+8, 16j+2t+9 for every 16-coordinate chunk j)
+    and of a packed V row (octet order: octet g lists g, g+8, g+16, ...)."""
+    k = [16 * j + 2 * t + e for t in range(4) for j in range(head_dim // 16)
+         for e in (0, 1, 8, 9)]
+    v = [g + 8 * c for g in range(8) for c in range(head_dim // 8)]
+    return k, v
 
 
 def page_bytes(head_dim: int, key_bits: int, value_bits: int, qjl: bool) -> int:
@@ -120,6 +145,25 @@ def append(tables: LayerTables, pages: torch.Tensor, k: torch.Tensor, v: torch.T
     _lib.check("tq_append", lib.tq_append(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c),
                                           ctypes.byref(kt), ctypes.byref(vt), int(pos),
                                           _stream(k.device)))
+
+
+def append_uses_tensor_cores(tables: LayerTables, k: torch.Tensor, v: torch.Tensor) -> bool:
+    """True when append() with these inputs runs the tcgen05 kernel."""
+    lib = _lib.load()
+    g, t = tables.geom(), tables.ctables()
+    kt, vt = tensor4(k), tensor4(v)
+    return bool(lib.tq_append_tensor_core(ctypes.byref(g), ctypes.byref(t), ctypes.byref(kt),
+                                          ctypes.byref(vt)))
+
+
+def device_status(device: torch.device) -> int:
+    """Read and clear the library's device status word (0: no kernel timed out)."""
+    lib = _lib.load()
+    st = ctypes.c_uint32(0)
+    rc = lib.tq_device_status(ctypes.byref(st), _stream(device))
+    if rc not in (_lib.TQ_OK, _lib.TQ_ERR_DEVICE):
+        _lib.check("tq_device_status", rc)
+    return int(st.value)
 
 
 def dequantize(tables: LayerTables, pages: torch.Tensor, t0: int, t1: int,

@@ -79,6 +79,13 @@ typedef struct tq_tables {
   const float* qjl;           /* S [D][D] row-major (NULL when qjl == 0)     */
   const float* rot_t;         /* R^T [D][D] row-major                        */
   const float* qjl_t;         /* S^T [D][D] row-major (NULL when qjl == 0)   */
+  /* Optional, head_dim 128 only: R as three bf16 terms (hi = bf16(R),
+   * mid = bf16(R - hi), lo = bf16(R - hi - mid)) with rows in packed order,
+   * [2][3][D][D] bf16: [0][s][p] = term s of R row k_order[p] (K quad order),
+   * [1][s][p] = term s of R row v_order[p] (V octet order).  When set,
+   * tq_append runs the rotation of bf16 inputs on the tensor cores; NULL
+   * keeps every append on the CUDA-core kernel. */
+  const uint16_t* rot_bf16x3;
 } tq_tables;
 
 /* Packed cache of one layer. */
@@ -182,6 +189,18 @@ int32_t tq_decode_attn_noalloc(const tq_geom* g, const tq_tables* t, const tq_ca
 /* Read and clear the device status word kept at the start of a decode
  * workspace (blocking copy on `stream`). */
 int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream);
+
+/* 1 when tq_append with these arguments runs the tensor-core kernel (head_dim
+ * 128, no QJL, bf16 views with 16-byte aligned rows, >= 32 tokens,
+ * rot_bf16x3 set), 0 when it runs the CUDA-core kernel.  Host-only query. */
+int32_t tq_append_tensor_core(const tq_geom* g, const tq_tables* t, const tq_tensor4* k,
+                              const tq_tensor4* v);
+
+/* Read and clear the library's own device status word, set by kernels that
+ * take no workspace (the tensor-core append: TQ_DEV_WAIT_TIMEOUT when one of
+ * its bounded waits ran out).  Blocking copy on `stream`.  No reference
+ * counterpart: the reference's append runs on the host. */
+int32_t tq_device_status(uint32_t* status, void* stream);
 
 #ifdef __cplusplus
 }
