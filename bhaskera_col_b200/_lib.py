@@ -101,6 +101,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
                                      P(DecodeArgs), VP, SZ, VP]),
             "tq_decode_attn_noalloc": (I32, [P(Geom), P(Tables), P(Cache), P(DecodeArgs), VP]),
             "tq_workspace_status": (I32, [VP, P(ctypes.c_uint32), VP]),
+            "tq_device_status": (I32, [P(ctypes.c_uint32), VP]),
+            "tq_append_tensor_core": (I32, [P(Geom), P(Tables), P(Tensor4), P(Tensor4)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)

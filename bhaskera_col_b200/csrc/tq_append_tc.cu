@@ -17,14 +17,26 @@
 //     24 per tile) into one of two TMEM accumulators; kSplit epilogue warps
 //     per TMEM lane quarter each take 128 / kSplit positions of 32 vectors.
 //
-// Bucketize: v = y / max(n, 1e-8) lies in [-1, 1].  With w = 0.4 x the
-// smallest boundary gap, cell c = round(v / w) + L (L = ceil(1.0625 / w) + 2,
-// one FFMA against 2^23 + L, whose float holds the integer in its low bits)
-// has the window [c - L - 1, c - L + 1] x w around v with at most one boundary
-// in it; the table holds {#boundaries below the window, that boundary or +inf},
-// so code = base + (v > b) = #{boundaries < v} exactly (torch.bucketize,
-// right=False).  Tables whose boundaries leave (-1, 1) or need more than
-// kMaxCells cells use a binary search instead.
+// Bucketize, almost all on the fp32 pipe (the integer pipe issues at half
+// the rate and bounded the first versions).  With w = 0.4 x the smallest
+// boundary gap and cells c = 0..2L centred at (c - L) w, L = ceil(span / w) + 3:
+//   u    = sat(y * inv / (2 L w) + 0.5)        (FFMA.SAT: clamps, NaN -> 0)
+//   cell = round(2 L u)                        (FFMA against 2^23: the float's
+//                                               low bits hold the integer)
+//   {nbK, base} = lut[cell]                    (one 8-byte load)
+//   s    = sat((y * inv K + nbK) * K)          (= [y * inv > b] exactly:
+//                                               nbK = -b K, K = 2^100, or -inf
+//                                               when the cell's window
+//                                               [c - L - 1, c - L + 1] w holds
+//                                               no boundary; it holds <= 1.
+//                                               The second scaling lifts every
+//                                               nonzero difference, denormal
+//                                               v included, to >= 2^51)
+//   code = base + s = #{boundaries < v}        (torch.bucketize, right=False)
+// Codes are packed by exact float arithmetic: acc = 2^23 + sum code_k 2^(BITS k)
+// over runs of <= 23 bits, whose low float bits are the packed field.  The
+// table is replicated for R lanes (R = 32 up to 5 bits: a warp's 32 lookups
+// are conflict-free).  Tables that do not fit use a binary search instead.
 //
 // Every wait is bounded (mbar_wait_bounded); on expiry the kernel sets
 // TQ_DEV_WAIT_TIMEOUT in a device status word (tq_device_status), drains its
@@ -44,22 +56,22 @@ constexpr int kAStages = 3;
 constexpr int kHalf = kM * 64 * 2;         // 16 KB: 128 rows x 64 bf16, 128-byte swizzle
 constexpr int kABytes = 2 * kHalf;         // one x tile
 constexpr int kBBytes = 6 * kHalf;         // 3 terms of R x 2 K-halves
-constexpr int kMaxCells = 2048;
 constexpr int kSplit = 2;                  // epilogue warps per TMEM lane quarter
 constexpr int kCW = kD / kSplit;           // positions per epilogue thread
 constexpr int kEpiWarps = 4 * kSplit;
 constexpr int kThreads = 32 * (2 + kEpiWarps);   // warp 0 TMA, warp 1 MMA, then epilogue
 constexpr uint32_t kTmemCols = 256;        // two 128-column fp32 accumulators
-constexpr float kRange = 1.0625f;          // |v| <= 1 up to rounding
+constexpr float kCmpScale = 1.2676506e30f; // K = 2^100
 
 constexpr int OFF_B = 0;
 constexpr int OFF_A = OFF_B + kBBytes;
-constexpr int OFF_LUT = OFF_A + kAStages * kABytes;
-constexpr int OFF_BND = OFF_LUT + kMaxCells * 8;
+constexpr int OFF_BND = OFF_A + kAStages * kABytes;       // [256] boundaries
 constexpr int OFF_XN = OFF_BND + 256 * 4;                 // [2][kSplit][kM] partial ||x||^2
 constexpr int OFF_BAR = OFF_XN + 2 * kSplit * kM * 4;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;          // + slack to align the base to 1 KB
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+constexpr int OFF_LUT = OFF_BAR + 256;                    // lane-replicated cell table
+constexpr int SMEM_BYTES = 227 * 1024;
+constexpr int kLutBytes = SMEM_BYTES - 1024 - OFF_LUT;    // 1 KB: slack to align the base
+static_assert(kLutBytes >= 16 * 1024, "shared memory");
 static_assert(OFF_A % 1024 == 0 && kABytes % 1024 == 0, "swizzled tiles need 1 KB alignment");
 
 struct TcParams {
@@ -86,8 +98,6 @@ __device__ __forceinline__ bool group_and(int id, int nthreads, bool pred) {
   return r != 0;
 }
 
-__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 template <int BITS>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -104,8 +114,7 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
   uint64_t* acc_empty = acc_full + 2;           // 2
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 3);
-  float* lutpar = reinterpret_cast<float*>(acc_empty + 4);   // 5 floats
-  float2* lut = reinterpret_cast<float2*>(sm + OFF_LUT);
+  float* lutpar = reinterpret_cast<float*>(acc_empty + 4);   // 4 floats
   float* bnd = reinterpret_cast<float*>(sm + OFF_BND);
   float* xn = reinterpret_cast<float*>(sm + OFF_XN);
 
@@ -128,33 +137,37 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
   }
   for (int i = tid; i < nb; i += kThreads) bnd[i] = p.bnd[i];
   __syncthreads();
+  // lookup grid (see the file comment); entries replicated for kRep lanes
+  constexpr int kRep = BITS <= 5 ? 32 : BITS == 6 ? 16 : BITS == 7 ? 8 : 4;
+  constexpr int kCellShift = kRep == 32 ? 8 : kRep == 16 ? 7 : kRep == 8 ? 6 : 5;   // log2(8 kRep)
   if (tid == 0) {
     float gap = 1.f;
     for (int i = 0; i + 1 < nb; ++i) gap = fminf(gap, bnd[i + 1] - bnd[i]);
     const float w = 0.4f * gap;
-    const float L = ceilf(kRange / w) + 2.f;
+    const float span = fmaxf(fabsf(bnd[0]), fabsf(bnd[nb - 1]));
+    const float L = ceilf(span / w) + 3.f;
     const float nc = 2.f * L + 1.f;
-    const bool ok = w > 0.f && nc <= (float)kMaxCells && bnd[0] > -1.f && bnd[nb - 1] < 1.f;
-    lutpar[0] = 1.f / w;
-    lutpar[1] = ok ? 8388608.f + L : 0.f;    // exact: L < 2^11
+    const bool ok = w > 0.f && nc * (float)(8 * kRep) <= (float)kLutBytes && span < 1.f;
+    lutpar[0] = 1.f / (2.f * L * w);          // u = sat(v * lutpar[0] + 0.5)
+    lutpar[1] = 2.f * L;                       // cell = round(u * 2L)
     lutpar[2] = ok ? nc : 0.f;
     lutpar[3] = w;
-    lutpar[4] = L;
   }
   __syncthreads();
   const int ncells = (int)lutpar[2];
   const bool use_lut = ncells > 0;
   {
-    const float w = lutpar[3], L = lutpar[4];
-    for (int c = tid; c < ncells; c += kThreads) {
+    const float w = lutpar[3], L = 0.5f * lutpar[1];
+    for (int i = tid; i < ncells * kRep; i += kThreads) {
+      const int c = i / kRep, l = i % kRep;
       const float wl = ((float)c - L - 1.f) * w, wh = ((float)c - L + 1.f) * w;
       int base = 0, hi = nb;                 // #boundaries < wl
       while (base < hi) {
         const int mid = (base + hi) >> 1;
         if (bnd[mid] < wl) base = mid + 1; else hi = mid;
       }
-      const float b = (base < nb && bnd[base] <= wh) ? bnd[base] : INFINITY;
-      lut[c] = make_float2(__int_as_float(base), b);
+      const float nbk = (base < nb && bnd[base] <= wh) ? -bnd[base] * kCmpScale : -INFINITY;
+      reinterpret_cast<float2*>(sm + OFF_LUT)[c * kRep + l] = make_float2(nbk, (float)base);
     }
   }
   tc::tc_fence_before();
@@ -236,7 +249,6 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
     const int q = warp & 3;                 // TMEM lane quarter this warp may read
     const int part = ew >> 2;               // which kCW positions of the row
     const int r = q * 32 + lane;            // tile row = vector
-    const float inv_w = lutpar[0], tofs = lutpar[1];
     int it = 0;
     for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++it) {
       const int st = it % kAStages, ac = it & 1;
@@ -245,19 +257,19 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         const unsigned char* xa = sm + OFF_A + st * kABytes;
-        float s0 = 0.f, s1 = 0.f;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
         for (int c = 0; c < kCW / 8; ++c) {
           const int chunk = part * (kCW / 8) + c;        // 16-byte chunk of the row
           const int half = chunk >> 3, c8 = chunk & 7;
           const uint4 u = *reinterpret_cast<const uint4*>(xa + half * kHalf + r * 128 +
                                                           ((c8 ^ (r & 7)) << 4));
-          s0 = fmaf(bf_lo(u.x), bf_lo(u.x), s0); s1 = fmaf(bf_hi(u.x), bf_hi(u.x), s1);
-          s0 = fmaf(bf_lo(u.y), bf_lo(u.y), s0); s1 = fmaf(bf_hi(u.y), bf_hi(u.y), s1);
-          s0 = fmaf(bf_lo(u.z), bf_lo(u.z), s0); s1 = fmaf(bf_hi(u.z), bf_hi(u.z), s1);
-          s0 = fmaf(bf_lo(u.w), bf_lo(u.w), s0); s1 = fmaf(bf_hi(u.w), bf_hi(u.w), s1);
+          tc::sq_bf16x2(u.x, s0, s1);
+          tc::sq_bf16x2(u.y, s2, s3);
+          tc::sq_bf16x2(u.z, s0, s1);
+          tc::sq_bf16x2(u.w, s2, s3);
         }
-        xn[((it & 1) * kSplit + part) * kM + r] = s0 + s1;
+        xn[((it & 1) * kSplit + part) * kM + r] = (s0 + s1) + (s2 + s3);
         __syncwarp();
         if (lane == 0) tc::mbar_arrive_cta(&a_empty[st]);
       }
@@ -291,25 +303,53 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
       uint32_t words[NW];
 #pragma unroll
       for (int x = 0; x < NW; ++x) words[x] = 0u;
+      // a run of codes packed at bit offset o, len bits, as the float
+      // acc = 2^23 + field (fields never overlap, so adding inserts them)
+      auto flush = [&](float acc, int o, int len) {
+        const uint32_t bits = __float_as_uint(acc);
+        const int wi = o >> 5, sh = o & 31;
+        if (sh + len <= 32) {
+          // for sh >= 8 the exponent bits of 2^23 shift out of the word
+          words[wi] += sh >= 8 ? (bits << sh) : ((bits & ((1u << len) - 1u)) << sh);
+        } else {
+          const uint32_t g = bits & ((1u << len) - 1u);
+          words[wi] += g << sh;
+          words[wi + 1] += g >> (32 - sh);
+        }
+      };
+      if (use_lut) {
+        const uint32_t lane_off = smem_u32(sm + OFF_LUT) + (uint32_t)(lane % kRep) * 8u -
+                                  (0x4B000000u << kCellShift);
+        const float ca = inv * lutpar[0], cK = inv * kCmpScale, c2l = lutpar[1];
+        float acc = 8388608.f;
+        int gs = 0, gl = 0;                    // run start bit / length (compile-time)
 #pragma unroll
-      for (int j = 0; j < kCW; ++j) {
-        const float v = __uint_as_float(yb[j]) * inv;
-        uint32_t code;
-        if (use_lut) {
-          const float vc = fminf(fmaxf(v, -kRange), kRange);
-          const int cell = __float_as_int(fmaf(vc, inv_w, tofs)) - 0x4B000000;
-          const float2 e = lut[cell];
-          code = (uint32_t)__float_as_int(e.x) + (v > e.y ? 1u : 0u);
-        } else {
-          code = (uint32_t)bucketize_lt(bnd, nb, v);
+        for (int j = 0; j < kCW; ++j) {
+          const int bo = j * BITS;
+          if (gl > 0 && (gl + BITS > 23 || (bo & 31) == 0)) {
+            flush(acc, gs, gl);
+            acc = 8388608.f;
+            gs = bo;
+            gl = 0;
+          }
+          const float y = __uint_as_float(yb[j]);
+          const float u = __saturatef(fmaf(y, ca, 0.5f));
+          const float tc = fmaf(u, c2l, 8388608.f);
+          const float2 e = tc::lds_f2((__float_as_uint(tc) << kCellShift) + lane_off);
+          const float sgt = __saturatef(fmaf(y, cK, e.x) * kCmpScale);
+          acc = fmaf(e.y + sgt, (float)(1u << gl), acc);
+          gl += BITS;
         }
-        const int bo = j * BITS, wi = bo >> 5, sh = bo & 31;
-        if (sh + BITS <= 32) {
-          words[wi] = tc::bfi(code, words[wi], sh, BITS);
-        } else {
-          words[wi] = tc::bfi(code, words[wi], sh, 32 - sh);
-          words[wi + 1] = tc::bfi(code >> (32 - sh), words[wi + 1], 0, BITS - (32 - sh));
-        }
+        flush(acc, gs, gl);
+      } else {
+        auto put = [&](int j, uint32_t code) {
+          const int bo = j * BITS, wi = bo >> 5, sh = bo & 31;
+          words[wi] += code << sh;
+          if (sh + BITS > 32) words[wi + 1] += code >> (32 - sh);
+        };
+#pragma unroll
+        for (int j = 0; j < kCW; ++j)
+          put(j, (uint32_t)bucketize_lt(bnd, nb, __uint_as_float(yb[j]) * inv));
       }
       const int64_t s = tile / p.nblk, tb = tile % p.nblk;
       const int64_t t = tb * kM + r;
@@ -318,15 +358,19 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
         uint8_t* page = p.pages + (s * p.pages_per_stream + tp / kPageTokens) * (int64_t)p.page_bytes;
         const int slot = (int)(tp % kPageTokens);
         uint8_t* row = page + p.sec_off + slot * p.row_bytes + part * (kCW * BITS / 8);
+        // widest store that the part's byte offset (part * NW * 4) keeps aligned
         if constexpr (NW % 4 == 0) {
 #pragma unroll
           for (int x = 0; x < NW / 4; ++x)
             reinterpret_cast<uint4*>(row)[x] =
                 make_uint4(words[4 * x], words[4 * x + 1], words[4 * x + 2], words[4 * x + 3]);
-        } else {
+        } else if constexpr (NW % 2 == 0) {
 #pragma unroll
           for (int x = 0; x < NW / 2; ++x)
             reinterpret_cast<uint2*>(row)[x] = make_uint2(words[2 * x], words[2 * x + 1]);
+        } else {
+#pragma unroll
+          for (int x = 0; x < NW; ++x) reinterpret_cast<uint32_t*>(row)[x] = words[x];
         }
         if (part == 0) reinterpret_cast<__half*>(page + p.norm_off)[slot] = __float2half_rn(n);
       }

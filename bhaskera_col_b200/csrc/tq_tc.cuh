@@ -104,6 +104,59 @@ __device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// ---- paired fp32 arithmetic (sm_100 f32x2: two lanes per instruction) --------
+struct f2 { unsigned long long r; };
+__device__ __forceinline__ f2 f2_make(float a, float b) {
+  f2 o;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(o.r) : "f"(a), "f"(b));
+  return o;
+}
+__device__ __forceinline__ void f2_split(f2 x, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x.r));
+}
+__device__ __forceinline__ f2 f2_mul(f2 a, f2 b) {
+  f2 o;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(o.r) : "l"(a.r), "l"(b.r));
+  return o;
+}
+__device__ __forceinline__ f2 f2_fma(f2 a, f2 b, f2 c) {
+  f2 o;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(o.r) : "l"(a.r), "l"(b.r), "l"(c.r));
+  return o;
+}
+
+// s0 += lo(w)^2, s1 += hi(w)^2 for the two bf16 halves of w (exact products,
+// one rounding each).
+__device__ __forceinline__ void sq_bf16x2(uint32_t w, float& s0, float& s1) {
+  asm("{\n .reg .b16 lo, hi;\n mov.b32 {lo, hi}, %2;\n"
+      " fma.rn.f32.bf16 %0, lo, lo, %0;\n fma.rn.f32.bf16 %1, hi, hi, %1;\n}"
+      : "+f"(s0), "+f"(s1) : "r"(w));
+}
+
+// 4-byte / 1-byte shared-memory loads at a 32-bit shared address.
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u8(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// 8-byte shared-memory load at a 32-bit shared address.
+__device__ __forceinline__ float2 lds_f2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+  return v;
+}
+
 // Insert the low `len` bits of a into b at bit `pos`.
 __device__ __forceinline__ uint32_t bfi(uint32_t a, uint32_t b, uint32_t pos, uint32_t len) {
   uint32_t d;
