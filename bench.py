@@ -159,11 +159,13 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
     from bhaskera_col_b200 import _lib
     from bhaskera_col_b200.inference import TurboQuantKVCache, ops
+    from bhaskera_col_b200.inference.head_parallel import HeadParallelDecoder, HeadShard
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    hkv = HKV // world
-    hq = HQ // world
+    shard = HeadShard(HQ, HKV, rank, world)
+    hkv = shard.kv_heads
+    hq = shard.q_heads
     B = B_PER_GPU * world
     S = B * hkv
     bpt = ops.page_bytes(D, KEY_BITS, VALUE_BITS, QJL) // 64
@@ -193,7 +195,7 @@ def run_ours(args, rank, world, local_rank):
     k_new = [synth((B, hkv, 1, D)) for _ in range(LAYERS)]
     v_new = [synth((B, hkv, 1, D)) for _ in range(LAYERS)]
     o_loc = [torch.empty((B, hq, 1, D), dtype=torch.bfloat16, device=dev) for _ in range(LAYERS)]
-    o_all = [torch.empty((world, B, hq, 1, D), dtype=torch.bfloat16, device=dev)
+    o_all = [torch.empty((world * B, hq, 1, D), dtype=torch.bfloat16, device=dev)
              for _ in range(LAYERS)]
     ws = ops.DecodeWorkspace()
     n_tok = T_CTX + 1
@@ -219,7 +221,7 @@ def run_ours(args, rank, world, local_rank):
                                      out=o_loc[layer], workspace=ws,
                                      phases=_lib.PHASE_MERGE)
             if world > 1:
-                dist.all_gather_into_tensor(o_all[layer], o_loc[layer])
+                shard.gather(o_loc[layer], buf=o_all[layer], layer=layer)
 
     # eager warm-up (sets kernel attributes, sizes the workspace)
     for _ in range(max(1, args.warmup)):
@@ -291,24 +293,26 @@ def run_ours(args, rank, world, local_rank):
     achieved = alg_bytes / (dec_avg / 1e3) / 1e9
 
     # ---- e2e through the public API with host buffers -----------------------
-    q_h = [q.cpu().pin_memory() for q in q_dev[:4]]
-    k_h = [k.cpu().pin_memory() for k in k_new[:4]]
-    v_h = [v.cpu().pin_memory() for v in v_new[:4]]
-    o_h = torch.empty((world if world > 1 else 1, B, hq, 1, D), dtype=torch.bfloat16).pin_memory()
+    # each rank receives the full step inputs (all heads) from the host, keeps
+    # its own heads, and reads back the gathered (B, Hq, 1, D) output
+    full_q = [torch.cat([q] * world, 1) for q in q_dev[:4]]
+    full_k = [torch.cat([k] * world, 1) for k in k_new[:4]]
+    full_v = [torch.cat([v] * world, 1) for v in v_new[:4]]
+    q_h = [q.cpu().pin_memory() for q in full_q]
+    k_h = [k.cpu().pin_memory() for k in full_k]
+    v_h = [v.cpu().pin_memory() for v in full_v]
+    o_h = torch.empty((B, HQ, 1, D), dtype=torch.bfloat16).pin_memory()
     h2d = (q_h[0].numel() + k_h[0].numel() + v_h[0].numel()) * 2 * LAYERS
     d2h = o_h.numel() * 2 * LAYERS
+    decoder = HeadParallelDecoder(cache, shard)
 
     def e2e_step():
         for layer in range(LAYERS):
             qd = q_h[layer % 4].to(dev, non_blocking=True)
             kd = k_h[layer % 4].to(dev, non_blocking=True)
             vd = v_h[layer % 4].to(dev, non_blocking=True)
-            o = cache.decode(qd, kd, vd, layer)
-            if world > 1:
-                dist.all_gather_into_tensor(o_all[layer], o)
-                o_h.copy_(o_all[layer], non_blocking=True)
-            else:
-                o_h[0].copy_(o, non_blocking=True)
+            o = decoder.decode(qd, kd, vd, layer, buf=o_all[layer])
+            o_h.copy_(o, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
 
     for st in stores:      # the e2e leg appends for real: start from T_CTX tokens
