@@ -27,7 +27,7 @@ EXPORTED = (
     "tq_last_error", "tq_version", "tq_page_bytes", "tq_quantize_rotated",
     "tq_append", "tq_dequantize", "tq_decode_workspace_bytes", "tq_decode_attn",
     "tq_decode_step", "tq_decode_attn_noalloc", "tq_workspace_status", "tq_device_status",
-    "tq_append_tensor_core",
+    "tq_append_tensor_core", "tq_prefill_attn",
 )
 
 
@@ -49,7 +49,7 @@ class Tables(ctypes.Structure):
                 ("v_centroids", ctypes.c_void_p), ("v_boundaries", ctypes.c_void_p),
                 ("rot", ctypes.c_void_p), ("qjl", ctypes.c_void_p),
                 ("rot_t", ctypes.c_void_p), ("qjl_t", ctypes.c_void_p),
-                ("rot_bf16x3", ctypes.c_void_p)]
+                ("rot_bf16x3", ctypes.c_void_p), ("rot_f16", ctypes.c_void_p)]
 
 
 class Cache(ctypes.Structure):
@@ -68,6 +68,12 @@ class DecodeArgs(ctypes.Structure):
                 ("n_tokens", ctypes.c_int64), ("num_q_heads", ctypes.c_int64),
                 ("scale", ctypes.c_float), ("num_ctas", ctypes.c_int32),
                 ("phases", ctypes.c_int32)]
+
+
+class PrefillArgs(ctypes.Structure):
+    _fields_ = [("q", ctypes.POINTER(Tensor4)), ("out", ctypes.POINTER(Tensor4)),
+                ("n_tokens", ctypes.c_int64), ("scale", ctypes.c_float),
+                ("causal", ctypes.c_int32)]
 
 
 _lock = threading.Lock()
@@ -103,6 +109,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             "tq_workspace_status": (I32, [VP, P(ctypes.c_uint32), VP]),
             "tq_device_status": (I32, [P(ctypes.c_uint32), VP]),
             "tq_append_tensor_core": (I32, [P(Geom), P(Tables), P(Tensor4), P(Tensor4)]),
+            "tq_prefill_attn": (I32, [P(Geom), P(Tables), P(Cache), P(PrefillArgs), VP]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)

@@ -501,6 +501,15 @@ int launch_append_tc(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   return TQ_OK;
 }
 
+uint32_t* device_status_word() {
+  void* addr = nullptr;
+  if (cudaGetSymbolAddress(&addr, g_tc_status) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return static_cast<uint32_t*>(addr);
+}
+
 int read_tc_status(uint32_t* out, cudaStream_t st) {
   void* addr = nullptr;
   cudaError_t e = cudaGetSymbolAddress(&addr, g_tc_status);

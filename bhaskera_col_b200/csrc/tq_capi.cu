@@ -309,6 +309,52 @@ int32_t tq_decode_step(const tq_geom* g, const tq_tables* t, const tq_cache* c,
   return launch_decode(g, t, c, a, workspace, workspace_bytes, (cudaStream_t)stream, &step);
 }
 
+int32_t tq_prefill_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                        const tq_prefill_args* a, void* stream) {
+  const char* fn = "tq_prefill_attn";
+  int rc;
+  if ((rc = check_geom(g, fn)) || (rc = check_tables(g, t, fn)) || (rc = check_cache(c, fn)))
+    return rc;
+  if (!a) { set_error("%s: args are NULL", fn); return TQ_ERR_INVALID; }
+  if ((rc = check_t4(a->q, "q", fn)) || (rc = check_t4(a->out, "out", fn))) return rc;
+  if (!t->rot_f16 || reinterpret_cast<uintptr_t>(t->rot_f16) % 16) {
+    set_error("%s: tables.rot_f16 (R as fp16, 16-byte aligned) is required", fn);
+    return TQ_ERR_INVALID;
+  }
+  if (!prefill_supported(g->head_dim, g->key_bits, g->value_bits)) {
+    set_error("%s: no kernel for head_dim %d, key_bits %d, value_bits %d", fn, g->head_dim,
+              g->key_bits, g->value_bits);
+    return TQ_ERR_INVALID;
+  }
+  const tq_tensor4 *q = a->q, *o = a->out;
+  for (int i = 0; i < 4; ++i)
+    if (q->shape[i] != o->shape[i]) { set_error("%s: q and out shapes differ", fn); return TQ_ERR_INVALID; }
+  if (q->shape[3] != g->head_dim) {
+    set_error("%s: last dim %lld != head_dim %d", fn, (long long)q->shape[3], g->head_dim);
+    return TQ_ERR_INVALID;
+  }
+  const int64_t B = q->shape[0], Hq = q->shape[1], Tq = q->shape[2];
+  if (B <= 0 || c->streams % B || Hq % (c->streams / B)) {
+    set_error("%s: q (B=%lld, Hq=%lld) does not match %lld streams (B * Hkv, Hq a multiple of Hkv)",
+              fn, (long long)B, (long long)Hq, (long long)c->streams);
+    return TQ_ERR_INVALID;
+  }
+  if (B * Hq > 65535) {
+    set_error("%s: B * Hq = %lld exceeds the grid limit 65535", fn, (long long)(B * Hq));
+    return TQ_ERR_INVALID;
+  }
+  if (a->n_tokens < Tq || a->n_tokens > c->pages_per_stream * TQ_PAGE_TOKENS) {
+    set_error("%s: n_tokens %lld must lie in [Tq = %lld, capacity %lld]", fn,
+              (long long)a->n_tokens, (long long)Tq,
+              (long long)(c->pages_per_stream * TQ_PAGE_TOKENS));
+    return TQ_ERR_INVALID;
+  }
+  if (!(a->scale > 0.f)) { set_error("%s: scale must be positive", fn); return TQ_ERR_INVALID; }
+  uint32_t* status = device_status_word();
+  if (!status) { set_error("%s: device status word unavailable", fn); return TQ_ERR_CUDA; }
+  return launch_prefill(g, t, c, a, status, (cudaStream_t)stream);
+}
+
 int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream) {
   if (!workspace || !status) { set_error("tq_workspace_status: NULL argument"); return TQ_ERR_INVALID; }
   cudaStream_t st = (cudaStream_t)stream;

@@ -31,6 +31,11 @@ int launch_append_tc(const tq_geom* g, const tq_tables* t, const tq_cache* c,
 bool append_tc_applies(const tq_geom* g, const tq_tables* t, const tq_tensor4* k,
                        const tq_tensor4* v);
 int read_tc_status(uint32_t* out, cudaStream_t st);
+// Device address of the library status word read by tq_device_status.
+uint32_t* device_status_word();
+bool prefill_supported(int D, int kb, int vb);
+int launch_prefill(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                   const tq_prefill_args* a, uint32_t* status, cudaStream_t st);
 int launch_dequant(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                    int64_t t0, int64_t t1, const tq_tensor4* ko, const tq_tensor4* vo,
                    cudaStream_t st);

@@ -370,6 +370,18 @@ class _LayerKVStore:
         self.store(k, v, residual_window)
         return self.attend(q, scale=scale, out=out)
 
+    def prefill(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, residual_window: int,
+                scale: Optional[float] = None, causal: bool = True,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Store T new tokens and return the attention of q (B, Hq, T, D) at
+        their positions over everything stored, straight off the pages."""
+        if residual_window > 0 or self._win_k is not None:
+            raise ValueError("fused prefill attention needs residual_window == 0 "
+                             "(window tokens stay dense; use update() instead)")
+        self.store(k, v, residual_window)
+        return ops.prefill_attention(self.tables, self._pages, q, self._comp_ptr, scale=scale,
+                                     causal=causal, out=out)
+
     def reset(self) -> None:
         self._comp_ptr = 0
         self._win_k = self._win_v = None
@@ -464,12 +476,24 @@ class TurboQuantKVCache(BaseKVCache):
         return self._stores[layer_idx].decode(query_states, key_states, value_states,
                                               self.residual_window, scale=scale, out=out)
 
+    def prefill(self, query_states: torch.Tensor, key_states: torch.Tensor,
+                value_states: torch.Tensor, layer_idx: int, scale: Optional[float] = None,
+                causal: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """A prefill forward of one layer: store the T new tokens and return the
+        causal attention of query_states (B, Hq, T, D) over the whole cache
+        (the SDPA that follows update() in the reference), without dense K/V.
+        Needs residual_window == 0."""
+        return self._stores[layer_idx].prefill(query_states, key_states, value_states,
+                                               self.residual_window, scale=scale,
+                                               causal=causal, out=out)
+
     def device_status(self) -> int:
-        """OR of the device status words of all layers (synchronises)."""
+        """OR of the device status words of all layers and of the library's
+        own status word (synchronises)."""
         st = 0
         for s in self._stores:
             st |= s.workspace.status()
-        return st
+        return st | ops.device_status(self.device)
 
     # -- bookkeeping -------------------------------------------------------------
     def advance(self, n: int = 1) -> None:

@@ -58,10 +58,12 @@ class LayerTables:
     rot_t: Optional[torch.Tensor] = None
     qjl_t: Optional[torch.Tensor] = None
     rot_bf16x3: Optional[torch.Tensor] = None
+    rot_f16: Optional[torch.Tensor] = None
 
     def __post_init__(self):
         self.rot = self.rot.contiguous().float()
         self.rot_t = self.rot.t().contiguous()
+        self.rot_f16 = self.rot.half().contiguous()      # prefill attention
         if self.head_dim == 128:
             # R = hi + mid + lo in bf16 (24 significant bits): the tensor-core
             # append computes x R^T as three exact bf16 products summed in fp32;
@@ -93,6 +95,7 @@ class LayerTables:
         t.rot_t = self.rot_t.data_ptr()
         t.qjl_t = self.qjl_t.data_ptr() if self.qjl_t is not None else None
         t.rot_bf16x3 = self.rot_bf16x3.data_ptr() if self.rot_bf16x3 is not None else None
+        t.rot_f16 = self.rot_f16.data_ptr() if self.rot_f16 is not None else None
         return t
 
 
@@ -243,6 +246,26 @@ def decode_step(tables: LayerTables, pages: torch.Tensor, k_new: torch.Tensor,
     _lib.check("tq_decode_step", lib.tq_decode_step(
         ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(kt), ctypes.byref(vt),
         int(pos), ctypes.byref(a), ws.data_ptr(), ws.numel(), _stream(q.device)))
+    return out
+
+
+def prefill_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
+                      n_tokens: int, scale: Optional[float] = None, causal: bool = True,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention of queries q (B, Hq, Tq, D) at positions n_tokens - Tq ..
+    n_tokens - 1 over the packed tokens [0, n_tokens) of every stream (causal:
+    a query sees keys at or before its position)."""
+    _require_cuda(pages, q)
+    lib = _lib.load()
+    if out is None:
+        out = torch.empty_like(q)
+    g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
+    qt, ot = tensor4(q), tensor4(out)
+    a = _lib.PrefillArgs(ctypes.pointer(qt), ctypes.pointer(ot), int(n_tokens),
+                         float(scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])),
+                         1 if causal else 0)
+    _lib.check("tq_prefill_attn", lib.tq_prefill_attn(
+        ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(a), _stream(q.device)))
     return out
 
 

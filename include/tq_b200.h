@@ -86,6 +86,8 @@ typedef struct tq_tables {
    * tq_append runs the rotation of bf16 inputs on the tensor cores; NULL
    * keeps every append on the CUDA-core kernel. */
   const uint16_t* rot_bf16x3;
+  /* R [D][D] fp16, row-major: required by tq_prefill_attn, unused elsewhere. */
+  const uint16_t* rot_f16;
 } tq_tables;
 
 /* Packed cache of one layer. */
@@ -172,6 +174,27 @@ int32_t tq_decode_step(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                        const tq_tensor4* k_new, const tq_tensor4* v_new, int64_t pos,
                        const tq_decode_args* a, void* workspace, size_t workspace_bytes,
                        void* stream);
+
+/* Prefill attention straight off the packed cache: queries q (B, Hq, Tq, D)
+ * at positions n_tokens - Tq .. n_tokens - 1 of every stream attend the
+ * stream's tokens [0, n_tokens) (causal: a query at position p attends keys
+ * <= p), GQA with Hq a multiple of Hkv; out (B, Hq, Tq, D).  Keys and values
+ * are the dequantised ones, n (c[idx] R) (MSE codes; a QJL sketch is not
+ * used), so the result is SDPA over what update() returns at
+ * residual_window 0.  head_dim 64 or 128; t->rot_f16 is required.  No
+ * workspace; device-side wait timeouts go to the library status word
+ * (tq_device_status).  Replaces HF attention over update()'s output in a
+ * prefill forward (kv_cache.py:483-488, engine.py:389). */
+typedef struct tq_prefill_args {
+  const tq_tensor4* q;
+  const tq_tensor4* out;
+  int64_t n_tokens;            /* tokens per stream, the Tq new ones included */
+  float scale;                 /* softmax scale                               */
+  int32_t causal;              /* 1: causal; 0: every query sees all tokens   */
+} tq_prefill_args;
+
+int32_t tq_prefill_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                        const tq_prefill_args* a, void* stream);
 
 /* tq_decode_attn for callers that cannot allocate device memory (a runtime
  * that owns all device memory through its own pool, or code that must not

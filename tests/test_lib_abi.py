@@ -52,7 +52,7 @@ def test_append_argument_validation():
     assert rc == _lib.TQ_ERR_INVALID
     assert "NULL" in _lib.last_error()
     # all pointers non-null, but k/v disagree with the cache's stream count
-    t = _lib.Tables(*([16] * 9))
+    t = _lib.Tables(*([16] * 10))
     c = _lib.Cache(1024, 3, 4)
     k = _lib.Tensor4(16, _lib.TQ_BF16, (ctypes.c_int64 * 4)(1, 2, 5, 128),
                      (ctypes.c_int64 * 4)(1280, 640, 128, 1))
@@ -69,7 +69,7 @@ def test_append_argument_validation():
 def test_decode_argument_validation():
     lib = _lib.load()
     g = _geom()
-    t = _lib.Tables(*([16] * 9))
+    t = _lib.Tables(*([16] * 10))
     c = _lib.Cache(1024, 8, 4)
     q = _lib.Tensor4(16, _lib.TQ_BF16, (ctypes.c_int64 * 4)(2, 6, 1, 128),
                      (ctypes.c_int64 * 4)(768, 128, 128, 1))
