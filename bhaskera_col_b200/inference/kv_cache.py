@@ -131,6 +131,12 @@ class BaseKVCache(_HFCache):
     def get_seq_length(self, layer_idx: Optional[int] = 0) -> int:
         return self.seq_len
 
+    def get_mask_sizes(self, query_length: int, layer_idx: int = 0) -> Tuple[int, int]:
+        """(kv_length, kv_offset) for transformers' mask builders: the stored
+        tokens plus the query's.  transformers 5's default assumes per-layer
+        cache objects and fails on this cache otherwise."""
+        return self.get_seq_length(layer_idx) + query_length, 0
+
     @property
     @abstractmethod
     def seq_len(self) -> int: ...
@@ -407,16 +413,19 @@ class _LayerKVStore:
 class TurboQuantKVCache(BaseKVCache):
     """TurboQuant V3 (MSE) KV cache with bit-packed GPU storage.
 
-    Extra (build-only) keyword: ``qjl`` — also store a 1-bit QJL sketch of
+    Extra (build-only) keywords: ``qjl`` — also store a 1-bit QJL sketch of
     each key's quantisation residual; ``attend()`` then adds the unbiased
-    residual inner-product estimate to every score.
+    residual inner-product estimate to every score.  ``fused_attention`` —
+    ``update()`` stores nothing and returns the new K/V, for models whose
+    attention is the registered "turboquant" function (hf_attention.py),
+    which stores and attends straight off the packed pages.
     """
 
     def __init__(self, num_layers: int, batch_size: int, num_heads: int, head_dim: int,
                  key_bits: int = 4, value_bits: int = 2, residual_window: int = 128,
                  protected_layers: int = 2, dtype: torch.dtype = torch.bfloat16,
                  device: torch.device = torch.device("cpu"), max_seq_len: int = 2048,
-                 qjl: bool = False):
+                 qjl: bool = False, fused_attention: bool = False):
         device = torch.device(device)
         if device.type != "cuda":
             raise RuntimeError("TurboQuantKVCache stores its pages on a CUDA device; "
@@ -432,6 +441,7 @@ class TurboQuantKVCache(BaseKVCache):
         self.dtype = dtype
         self.device = device
         self.qjl = qjl
+        self.fused_attention = fused_attention
         self._seq_len = 0
         self._stores: List[_LayerKVStore] = []
         for i in range(num_layers):
@@ -450,6 +460,12 @@ class TurboQuantKVCache(BaseKVCache):
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
                cache_kwargs: Optional[Dict[str, Any]] = None
                ) -> Tuple[torch.Tensor, torch.Tensor]:
+        if self.fused_attention:
+            # the registered "turboquant" attention function stores and
+            # attends in one call (hf_attention.py)
+            from . import hf_attention
+            hf_attention.set_current(self)
+            return key_states, value_states
         return self._stores[layer_idx].store_and_get(key_states, value_states,
                                                      self.residual_window)
 
