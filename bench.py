@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import argparse
 import datetime
+from dataclasses import dataclass, replace
 import json
 import math
 import os
@@ -37,6 +38,49 @@ sys.path.insert(0, ROOT)
 LAYERS, HQ, HKV, D, T_CTX, B_PER_GPU = 32, 32, 8, 128, 8192, 16
 KEY_BITS, VALUE_BITS, QJL = 4, 2, True
 APPEND_CFG = dict(layers=48, B=8, H=8, T=4096, D=128, bits=4)
+
+
+@dataclass(frozen=True)
+class Workload:
+    """A decode-step workload: `batch` sequences per GPU (weak scaling) or in
+    total (strong scaling, KV heads split over the GPUs)."""
+    title: str
+    layers: int
+    hq: int
+    hkv: int
+    d: int
+    t_ctx: int
+    batch: int
+    kb: int
+    vb: int
+    qjl: bool
+    scaling: str
+    data: str           # "outlier": N(0,1), 2 of 128 channels x8; "student-t": t(4)/sqrt(2)
+
+
+WORKLOADS = {
+    # the headline: Mixtral-8x7B attention shapes, B16 x 8192 context per GPU
+    "mixtral": Workload("Mixtral-8x7B attention decode step", LAYERS, HQ, HKV, D, T_CTX,
+                        B_PER_GPU, KEY_BITS, VALUE_BITS, QJL, "weak", "outlier"),
+    # Qwen2.5-14B long context (GQA 5); --batch 1|4, --context 32768|131072, --bits 2|3|4
+    "qwen-long": Workload("Qwen2.5-14B long-context decode step", 48, 40, 8, 128, 32768, 1,
+                          3, 3, False, "weak", "student-t"),
+    # 256 sequences x 4096 context of Mixtral, KV heads split over the GPUs
+    "serving": Workload("Mixtral-8x7B head-sharded serving decode step", 32, 32, 8, 128, 4096,
+                        256, 3, 3, True, "strong", "outlier"),
+}
+
+
+def _workload(args) -> Workload:
+    w = WORKLOADS[args.workload]
+    ch = {}
+    if args.batch:
+        ch["batch"] = args.batch
+    if args.context:
+        ch["t_ctx"] = args.context
+    if args.bits:
+        ch["kb"] = ch["vb"] = args.bits
+    return replace(w, **ch) if ch else w
 
 
 def _peaks():
@@ -108,7 +152,10 @@ def run_reference(args, rank, world):
         return
     import torch
     from oracle import cpu_baseline as C
-    B = B_PER_GPU * world
+    W = _workload(args)
+    LAYERS, HQ, HKV, D, T_CTX, KEY_BITS, VALUE_BITS = (W.layers, W.hq, W.hkv, W.d, W.t_ctx,
+                                                       W.kb, W.vb)
+    B = W.batch * world if W.scaling == "weak" else W.batch
     kc, kb = C.codebook(D, KEY_BITS)
     vc, vb = C.codebook(D, VALUE_BITS)
     layer = C.RefLayer(B, HKV, D, T_CTX, KEY_BITS, VALUE_BITS, kc, kb, vc, vb)
@@ -128,9 +175,9 @@ def run_reference(args, rank, world):
     line = {
         "impl": "reference", "metric": "decode-attn tokens/s", "value": value,
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": W.scaling,
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": _config(world),
+        "config": _config(W, world),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": C.host_threads(),
                          "kind": "port",
                          "sample": f"1 of {LAYERS} layers per step timed, x{LAYERS}; "
@@ -142,15 +189,24 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def _config(world):
-    return {"workload": f"Mixtral-8x7B attention decode step: {LAYERS} layers x (append 1 "
-                        f"token + GQA decode), Hq{HQ}/Hkv{HKV}, D{D}, context {T_CTX}, "
-                        f"K{KEY_BITS}+QJL/V{VALUE_BITS}",
-            "global_batch": B_PER_GPU * world, "seq_len": T_CTX, "layers": LAYERS,
-            "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "key_bits": KEY_BITS,
-            "value_bits": VALUE_BITS, "qjl": QJL,
+def _config(W, world):
+    import math as _m
+    B = W.batch * world if W.scaling == "weak" else W.batch
+    bpt = W.d * (W.kb + W.vb) // 8 + 4 + ((W.d // 8 + 2) if W.qjl else 0)
+    per_gpu = W.layers * B * (W.hkv // world) * W.t_ctx * bpt
+    return {"workload": f"{W.title}: {W.layers} layers x (append 1 token + GQA decode), "
+                        f"Hq{W.hq}/Hkv{W.hkv}, D{W.d}, context {W.t_ctx}, "
+                        f"K{W.kb}{'+QJL' if W.qjl else ''}/V{W.vb}",
+            "global_batch": B, "seq_len": W.t_ctx, "layers": W.layers,
+            "q_heads": W.hq, "kv_heads": W.hkv, "head_dim": W.d, "key_bits": W.kb,
+            "value_bits": W.vb, "qjl": W.qjl,
+            "kv_data": ("N(0,1), 2 of 128 channels x8" if W.data == "outlier"
+                        else "Student-t(4) / sqrt(2)"),
             "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
-            "l2": "no flush: 3.96 GB packed KV per step per GPU > 126 MB L2"}
+            "l2": (f"no flush: {per_gpu / 1e9:.2f} GB packed KV per step per GPU > 126 MB L2"
+                   if per_gpu > 4 * 126e6 else
+                   f"{per_gpu / 1e6:.0f} MB packed KV per step per GPU over {W.layers} "
+                   "layers read in order (each layer's pages evicted before reuse)")}
 
 
 # ---------------------------------------------------------------------------
@@ -161,12 +217,15 @@ def run_ours(args, rank, world, local_rank):
     from bhaskera_col_b200.inference import TurboQuantKVCache, ops
     from bhaskera_col_b200.inference.head_parallel import HeadParallelDecoder, HeadShard
 
+    W = _workload(args)
+    LAYERS, HQ, HKV, D, T_CTX, KEY_BITS, VALUE_BITS, QJL = (W.layers, W.hq, W.hkv, W.d, W.t_ctx,
+                                                            W.kb, W.vb, W.qjl)
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     shard = HeadShard(HQ, HKV, rank, world)
     hkv = shard.kv_heads
     hq = shard.q_heads
-    B = B_PER_GPU * world
+    B = W.batch * world if W.scaling == "weak" else W.batch
     S = B * hkv
     bpt = ops.page_bytes(D, KEY_BITS, VALUE_BITS, QJL) // 64
 
@@ -181,7 +240,12 @@ def run_ours(args, rank, world, local_rank):
     scale = torch.ones(D, device=dev)
     scale[out_ch] = 8.0
 
+    student = torch.distributions.StudentT(torch.tensor(4.0, device=dev))
+    torch.cuda.manual_seed(1234 + rank)
+
     def synth(shape):
+        if W.data == "student-t":
+            return (student.sample(shape) * (0.5 ** 0.5)).to(torch.bfloat16)
         return (torch.randn(shape, device=dev, generator=gen) * scale).to(torch.bfloat16)
 
     CH = 2048
@@ -341,11 +405,13 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- prefill append throughput (48 layers x B8 x Hkv8 x 4096, 4-bit) ----
     append_line = None
-    if rank == 0 and not args.skip_append:
+    prefill_line = None
+    if rank == 0 and not args.skip_append and args.workload == "mixtral":
         append_line = bench_append(dev, args)
+        prefill_line = bench_prefill(dev, args)
 
     cpu_line = None
-    if rank == 0 and world == 1 and not args.skip_cpu:
+    if rank == 0 and world == 1 and not args.skip_cpu and args.workload == "mixtral":
         from oracle import cpu_baseline as C
         t_layer = C.time_decode(B, HQ, HKV, D, T_CTX, KEY_BITS, VALUE_BITS, steps=2)
         cpu_line = {"value": B / (t_layer * LAYERS), "unit": "tokens/s",
@@ -357,14 +423,15 @@ def run_ours(args, rank, world, local_rank):
         line = {
             "metric": "decode-attn tokens/s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": W.scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": _config(world),
+            "config": _config(W, world),
             "packed_kv_gbs_per_gpu": LAYERS * alg_bytes / (ms_step / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "traffic": _traffic_per_launch(),
-                         "kernel": "decode_kernel<128,4,2,qjl>",
+                         "traffic": _traffic_per_launch() if args.workload == "mixtral" else None,
+                         "kernel": f"decode_kernel<{D},{KEY_BITS},{VALUE_BITS},"
+                                   f"{'qjl' if QJL else 'mse'}>",
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "avg_launch_ms": dec_avg, "peak_kind": peak_kind},
             "cpu_baseline": cpu_line,
@@ -375,6 +442,7 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": args.steps * LAYERS * 3,
             "clocks": clocks,
             "append": append_line,
+            "prefill_attention": prefill_line,
             "device_status": status,
         }
         print(json.dumps(line), flush=True)
@@ -426,6 +494,49 @@ def bench_append(dev, args):
             "token_heads_per_s": th / (ms / 1e3), "algorithmic_bytes": alg}
 
 
+def bench_prefill(dev, args):
+    """Prefill attention over the packed cache: one layer of B8 x Hq32/Hkv8 x
+    4096 tokens, D128, K4/V4, causal (4 * B * Hq * T^2/2 * D flops)."""
+    import torch
+    from bhaskera_col_b200.inference import ops
+    from bhaskera_col_b200.inference.kv_cache import (FastLloydMaxCodebook,
+                                                      _generate_rotation_matrix)
+    c = APPEND_CFG
+    B, H, T, Dd, bits, g = c["B"], c["H"], c["T"], c["D"], c["bits"], 4
+    cb = FastLloydMaxCodebook.get(Dd, bits, dev)
+    t = ops.LayerTables(Dd, bits, bits, False, cb.centroids, cb.boundaries, cb.centroids,
+                        cb.boundaries, _generate_rotation_matrix(Dd, 42, dev).contiguous())
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+    pages = torch.zeros((B * H, T // 64, ops.page_bytes(Dd, bits, bits, False)),
+                        dtype=torch.uint8, device=dev)
+    k = torch.randn((B, H, T, Dd), device=dev, generator=gen).to(torch.bfloat16)
+    ops.append(t, pages, k, k, 0)
+    q = torch.randn((B, H * g, T, Dd), device=dev, generator=gen).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    for _ in range(2):
+        ops.prefill_attention(t, pages, q, T, out=out)
+    torch.cuda.synchronize()
+    reps = max(2, min(args.steps, 5))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        ops.prefill_attention(t, pages, q, T, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = 4.0 * B * H * g * (T * T / 2) * Dd
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        peak = 1590.0
+    return {"workload": f"prefill attention over the packed cache, 1 layer: B{B} x Hq{H * g}/Hkv{H} "
+                        f"x {T} tokens causal, D{Dd}, K{bits}/V{bits}", "ms": ms,
+            "tflops": flops / (ms / 1e3) / 1e12, "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peak,
+            "kernel": "prefill_kernel (mma.sync m16n8k16 fp16)"}
+
+
 def run_profile(args):
     """Small single-GPU cases for ncu captures (no JSON line):
     --profile decode : one Mixtral layer (B16 Hkv8 T8192, K4+QJL/V2), 4 decode calls
@@ -437,6 +548,24 @@ def run_profile(args):
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev)
     gen.manual_seed(5)
+    if args.profile == "prefill":
+        c = APPEND_CFG
+        from bhaskera_col_b200.inference.kv_cache import FastLloydMaxCodebook
+        cb = FastLloydMaxCodebook.get(c["D"], c["bits"], dev)
+        from bhaskera_col_b200.inference.kv_cache import _generate_rotation_matrix
+        t = ops.LayerTables(c["D"], c["bits"], c["bits"], False, cb.centroids, cb.boundaries,
+                            cb.centroids, cb.boundaries,
+                            _generate_rotation_matrix(c["D"], 42, dev).contiguous())
+        Bp, Tp = 2, 2048          # a smaller case of the same kernel for ncu
+        pages = torch.zeros((Bp * c["H"], Tp // 64, ops.page_bytes(c["D"], c["bits"], c["bits"], False)),
+                            dtype=torch.uint8, device=dev)
+        k = torch.randn((Bp, c["H"], Tp, c["D"]), device=dev, generator=gen).to(torch.bfloat16)
+        ops.append(t, pages, k, k, 0)
+        q = torch.randn((Bp, 4 * c["H"], Tp, c["D"]), device=dev, generator=gen).to(torch.bfloat16)
+        for _ in range(3):
+            ops.prefill_attention(t, pages, q, Tp)
+        torch.cuda.synchronize()
+        return
     if args.profile == "append":
         c = APPEND_CFG
         cache = TurboQuantKVCache(num_layers=1, batch_size=c["B"], num_heads=c["H"],
@@ -478,8 +607,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-append", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--profile", choices=["decode", "append", "step"], default=None,
+    ap.add_argument("--profile", choices=["decode", "append", "step", "prefill"], default=None,
                     help="run a small single-layer case for ncu and exit")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mixtral",
+                    help="decode-step workload (default: the Mixtral headline)")
+    ap.add_argument("--batch", type=int, default=0, help="override the workload's batch")
+    ap.add_argument("--context", type=int, default=0, help="override the context length")
+    ap.add_argument("--bits", type=int, default=0, help="override K and V bit widths")
     args = ap.parse_args()
     if args.profile:
         run_profile(args)

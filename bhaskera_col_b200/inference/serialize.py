@@ -126,9 +126,10 @@ def write(f: BinaryIO, cache_meta: dict, layers: List[dict]) -> None:
 
 
 def read(f: BinaryIO) -> Tuple[dict, List[dict]]:
-    """Read a file into (header, layers); each layer dict carries `pages`
-    (uint8 CPU tensor) and `window_k`/`window_v` (or None).  Checks magic,
-    version, bounds and CRCs."""
+    """Read a file into (header, layers); each layer dict carries the header
+    entry's fields, with `pages` replaced by the page data (uint8 CPU tensor
+    [streams][pages][page_bytes]), and `window_k`/`window_v` (or None).
+    Checks magic, version, bounds and CRCs."""
     head = f.read(12)
     if len(head) < 12 or head[:4] != MAGIC:
         raise FormatError("not a TurboQuant cache file (bad magic)")
@@ -223,7 +224,7 @@ def load(path_or_file: Union[str, BinaryIO], device, max_seq_len: Optional[int] 
         if L["streams"] != st._pages.shape[0]:
             raise FormatError("stream count does not match batch_size * num_heads")
         st._ensure_capacity(L["tokens"])
-        st._pages[:, :L["pages"]] = L["pages"].to(st.device)
+        st._pages[:, :L["pages"].shape[1]] = L["pages"].to(st.device)
         st._comp_ptr = L["tokens"]
         if L["window_k"] is not None:
             st._win_k = L["window_k"].to(st.device)
