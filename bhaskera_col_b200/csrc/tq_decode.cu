@@ -34,9 +34,7 @@
 
 namespace tq {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kDecThreads = 32 * (kConsumerWarps + 1);   // + one producer warp
-constexpr int kStages = 5;
+constexpr int kTileWarps = 4;     // warps sharing one 64-token page (16 tokens each)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegInf = -INFINITY;
 
@@ -178,18 +176,72 @@ struct Dec {
   static constexpr int PB = align128(PAGE);
   // static shared memory: the K table (aliased by the combine scratch) and,
   // when both fit, the V table.  Dynamic: [V table] [stages] [barriers].
-  static constexpr int COMB = kConsumerWarps * (16 + 8 * D) * 4;
-  static constexpr int REGION0 = align128(cmax(Lut<KB>::kBytes, COMB));
-  static constexpr bool VSTATIC = REGION0 + Lut<VB>::kBytes <= 45 * 1024;
-  static constexpr int LUTV_STATIC = VSTATIC ? Lut<VB>::kBytes : 16;
+  // K4 with V2 / V4 at D128: one 64 KB dynamic table region, 256 rows of
+  // 256 B (one row per code byte): bytes 0-127 the K pair entry for each of
+  // 32 lanes, bytes 128-255 the V entry (V4: pair for 32 lanes; V2: quad of
+  // 8 B for 16 lanes).  A lookup address is (byte << 8) | lane offset: one
+  // byte permute.  The combine scratch aliases its first rows.  Such a CTA
+  // owns its SM: 12 consumer warps in three groups of four take every third
+  // page, so one table serves as many warps as three CTAs of the other
+  // variants do.
+  static constexpr bool FAST = D == 128 && KB == 4 && (VB == 2 || VB == 4);
+  static constexpr int NCW = FAST ? 12 : 4;            // consumer warps
+  static constexpr int NG = NCW / kTileWarps;          // page groups
+  static constexpr int THREADS = 32 * (NCW + 1);       // + one producer warp
+  static constexpr int MINB = FAST ? 1 : 3;            // CTAs per SM
+  static constexpr int SG = FAST ? 3 : 5;               // stages per page group
+  static constexpr int STAGES = NG * SG;
+  static constexpr int COMB = NCW * (16 + 8 * D) * 4;
+  static constexpr int FLUT = 65536;
+  static_assert(!FAST || COMB <= FLUT, "combine scratch");
+  static constexpr int REGION0 = FAST ? 128 : align128(cmax(Lut<KB>::kBytes, COMB));
+  static constexpr bool VSTATIC = FAST || REGION0 + Lut<VB>::kBytes <= 45 * 1024;
+  static constexpr int LUTV_STATIC = (VSTATIC && !FAST) ? Lut<VB>::kBytes : 16;
   static constexpr int LUTV = 0;   // offset of the V table in the dynamic region
-  static constexpr int STAGE0 = VSTATIC ? 0 : align128(Lut<VB>::kBytes);
-  static constexpr int BARS = STAGE0 + kStages * PB;
-  static constexpr int SMEM = BARS + 2 * kStages * 8;
+  static constexpr int STAGE0 = FAST ? FLUT : VSTATIC ? 0 : align128(Lut<VB>::kBytes);
+  static constexpr int BARS = STAGE0 + STAGES * PB;
+  static constexpr int SMEM = BARS + 2 * STAGES * 8;
 };
 
+// The K4 / V2|V4 table region (see Dec::FAST): rows [r0, r1) of 256 B, one
+// 16-byte chunk per thread and step (consecutive threads, consecutive chunks).
+template <int VB>
+__device__ __forceinline__ void build_fast_lut(unsigned char* base, const float* kc,
+                                               const float* vc, int r0, int r1, int tid,
+                                               int nthreads) {
+  uint4* L = reinterpret_cast<uint4*>(base);
+  for (int i = r0 * 16 + tid; i < r1 * 16; i += nthreads) {
+    const int e = i >> 4, c = i & 15;
+    uint4 val;
+    if (c < 8) {
+      const uint32_t k = pack_half2(__ldg(kc + (e & 15)), __ldg(kc + (e >> 4)));
+      val = make_uint4(k, k, k, k);
+    } else if constexpr (VB == 4) {
+      const uint32_t v = pack_half2(__ldg(vc + (e & 15)), __ldg(vc + (e >> 4)));
+      val = make_uint4(v, v, v, v);
+    } else {
+      // byte e = a0 | a1 << 2 | b0 << 4 | b1 << 6 (codes of tokens a, b at
+      // two positions): half2(c[a0], c[b0]) then half2(c[a1], c[b1])
+      const uint32_t v0 = pack_half2(__ldg(vc + (e & 3)), __ldg(vc + ((e >> 4) & 3)));
+      const uint32_t v1 = pack_half2(__ldg(vc + ((e >> 2) & 3)), __ldg(vc + (e >> 6)));
+      val = make_uint4(v0, v1, v0, v1);
+    }
+    L[i] = val;
+  }
+}
+
+// (byte b of x) << 8 | low byte of lane_off: the address of a fast-table
+// lookup, in one byte permute (the other bytes of lane_off are zero).
+__device__ __forceinline__ uint32_t fast_addr(uint32_t x, uint32_t lane_off, int b) {
+  return __byte_perm(x, lane_off, 0x5504u | ((uint32_t)b << 4));
+}
+
+__device__ __forceinline__ uint2 lds64(const unsigned char* base, uint32_t byte_off) {
+  return *reinterpret_cast<const uint2*>(base + byte_off);
+}
+
 template <int D, int KB, int VB, bool QJL>
-__global__ void __launch_bounds__(kDecThreads, 3)
+__global__ void __launch_bounds__(Dec<D, KB, VB, QJL>::THREADS, Dec<D, KB, VB, QJL>::MINB)
 decode_kernel(DecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   using G = Dec<D, KB, VB, QJL>;
@@ -207,9 +259,11 @@ decode_kernel(DecodeParams p) {
 
   __shared__ __align__(128) unsigned char s_lut0[G::REGION0];
   __shared__ __align__(128) unsigned char s_lutv_static[G::LUTV_STATIC];
-  unsigned char* lutk = s_lut0;
-  unsigned char* lutv = G::VSTATIC ? s_lutv_static : smem + G::LUTV;
+  unsigned char* lutk = G::FAST ? smem : s_lut0;
+  unsigned char* lutv = G::FAST ? smem : G::VSTATIC ? s_lutv_static : smem + G::LUTV;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::BARS);
+  constexpr int kStages = G::STAGES;
+  constexpr int kConsumerWarps = G::NCW;
   uint64_t* empty = full + kStages;
   __shared__ int s_abort;
 
@@ -226,39 +280,48 @@ decode_kernel(DecodeParams p) {
     s_abort = 0;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], kTileWarps);
     }
     fence_mbar_init();
   }
   pdl_launch_dependents();
   if (warp < kConsumerWarps) {
-    build_lut<KB>(lutk, p.kc, tid, NCT);
-    build_lut<VB>(lutv, p.vc, tid, NCT);
+    if constexpr (G::FAST) {
+      build_fast_lut<VB>(smem, p.kc, p.vc, 0, 256, tid, NCT);
+    } else {
+      build_lut<KB>(lutk, p.kc, tid, NCT);
+      build_lut<VB>(lutv, p.vc, tid, NCT);
+    }
   }
   __syncthreads();
   pdl_wait();   // pages and query fragments come from the preceding kernels
 
   // ------------------------------------------------------------ producer
+  // Lane g feeds page group g (pages i = g, g + NG, ...) through its own ring
+  // of SG stages, so a slow group never holds back the others' pages.
   if (warp == kConsumerWarps) {
-    if (lane == 0) {
-      int64_t s = gp0 / p.Pv, pg = gp0 - s * p.Pv;
-      for (int i = 0; i < npages; ++i) {
-        const int st = i % kStages;
-        if (i >= kStages && !s_abort) {
-          if (!mbar_wait_bounded(&empty[st], (uint32_t)(((i / kStages) - 1) & 1))) {
+    if (lane < G::NG) {
+      const int gr = lane;
+      int issued = 0;
+      for (int i = gr, k = 0; i < npages; i += G::NG, ++k) {
+        const int st = gr * G::SG + k % G::SG;
+        if (k >= G::SG && !s_abort) {
+          if (!mbar_wait_bounded(&empty[st], (uint32_t)(((k / G::SG) - 1) & 1))) {
             atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
             s_abort = 1;
           }
         }
         if (s_abort) break;
+        const int64_t gpi = gp0 + i;
+        const int64_t s = gpi / p.Pv, pg = gpi - s * p.Pv;
         const uint8_t* src = p.pages + (s * p.pages_per_stream + pg) * (int64_t)G::PAGE;
-        if (++pg == p.Pv) { pg = 0; ++s; }
         mbar_expect_tx(&full[st], (uint32_t)G::PAGE);
         bulk_g2s(smem + G::STAGE0 + st * G::PB, src, (uint32_t)G::PAGE, &full[st]);
+        issued = k + 1;
       }
       if (s_abort) {   // never leave with a copy still writing shared memory
-        for (int i = tmax(0, npages - kStages); i < npages; ++i)
-          mbar_wait_bounded(&full[i % kStages], (uint32_t)((i / kStages) & 1), 16u);
+        for (int k = tmax(0, issued - G::SG); k < issued; ++k)
+          mbar_wait_bounded(&full[gr * G::SG + k % G::SG], (uint32_t)((k / G::SG) & 1), 16u);
       }
     }
     return;
@@ -270,7 +333,6 @@ decode_kernel(DecodeParams p) {
   uint32_t qf[NJ][2], sqf[NJ][2];
   float O[NJ][4];
   float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
-  int64_t cur_s = -1;
 
   auto reset_state = [&]() {
 #pragma unroll
@@ -292,164 +354,222 @@ decode_kernel(DecodeParams p) {
   };
   reset_state();
 
-  int64_t s = gp0 / p.Pv;                       // advanced incrementally below
-  int pg = (int)(gp0 - s * p.Pv);
-  for (int i = 0; i < npages; ++i, ++pg) {
-    if (pg == Pv32) { pg = 0; ++s; }
-    const int st = i % kStages;
-    if (s != cur_s) { load_q(s); cur_s = s; }
-    if (!s_abort && !mbar_wait_bounded(&full[st], (uint32_t)((i / kStages) & 1))) {
-      atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
-      s_abort = 1;
-    }
-    const uint8_t* pgb = smem + G::STAGE0 + st * G::PB;
-    const int tok0 = pg * kPageTokens + warp * 16;
-
-    if (tok0 < T32) {
-      // ---------------- scores: S^T tile (16 tokens x 8 heads) --------------
-      const int r0 = warp * 16 + gq, r1 = r0 + 8;
-      uint32_t wk0[KQW], wk1[KQW];
-      load_bits<KQB, KQA>(pgb + r0 * G::KROW, tq * KQB, wk0);
-      load_bits<KQB, KQA>(pgb + r1 * G::KROW, tq * KQB, wk1);
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      float acc2[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t wq0[QQW], wq1[QQW];
-      if constexpr (QJL) {
-        load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r0 * G::QROW, tq * QQB, wq0);
-        load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r1 * G::QROW, tq * QQB, wq1);
+  const int tw = warp % kTileWarps;             // 16-token tile of a page
+  const int grp = warp / kTileWarps;             // pages i with i % NG == grp
+  // Segments are the runs of one stream's pages in this CTA's range; each
+  // warp takes its group's pages of a segment, then all consumer warps
+  // combine their partial results for the segment.
+  int64_t s = gp0 / p.Pv;                       // stream of the segment
+  int pg0 = (int)(gp0 - s * p.Pv);              // its first page
+  int i0 = 0;                                   // CTA-relative index of that page
+  int inext = grp;                              // next page of this warp's group
+  int ring = 0;                                 // position in the group's stage ring
+  uint32_t phase = 0;
+  while (i0 < npages) {
+    const int i1 = tmin(npages, i0 + (Pv32 - pg0));   // the segment: pages [i0, i1)
+    if (inext < i1) load_q(s);
+    for (; inext < i1; inext += G::NG) {
+      const int st = grp * G::SG + ring;
+      const int pg = pg0 + (inext - i0);
+      if (!s_abort && !mbar_wait_bounded(&full[st], phase)) {
+        atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
+        s_abort = 1;
       }
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        uint32_t a[4];
-        const int o0 = (4 * j) * KB, o1 = (4 * j + 2) * KB;   // quad entries 4j.., 4j+2..
-        if constexpr (Lut<KB>::kPair) {
-          a[0] = lds32(lutk, field_addr<2 * KB>(wk0, o0, lane4));
-          a[1] = lds32(lutk, field_addr<2 * KB>(wk1, o0, lane4));
-          a[2] = lds32(lutk, field_addr<2 * KB>(wk0, o1, lane4));
-          a[3] = lds32(lutk, field_addr<2 * KB>(wk1, o1, lane4));
-        } else {
-          a[0] = lds16(lutk, getbits(wk0, o0, KB) << 1) | (lds16(lutk, getbits(wk0, o0 + KB, KB) << 1) << 16);
-          a[1] = lds16(lutk, getbits(wk1, o0, KB) << 1) | (lds16(lutk, getbits(wk1, o0 + KB, KB) << 1) << 16);
-          a[2] = lds16(lutk, getbits(wk0, o1, KB) << 1) | (lds16(lutk, getbits(wk0, o1 + KB, KB) << 1) << 16);
-          a[3] = lds16(lutk, getbits(wk1, o1, KB) << 1) | (lds16(lutk, getbits(wk1, o1 + KB, KB) << 1) << 16);
-        }
-        mma_f16_16816(acc, a, qf[j][0], qf[j][1]);
+      const uint8_t* pgb = smem + G::STAGE0 + st * G::PB;
+      const int tok0 = pg * kPageTokens + tw * 16;
+
+      if (tok0 < T32) {
+        // ---------------- scores: S^T tile (16 tokens x 8 heads) --------------
+        const int r0 = tw * 16 + gq, r1 = r0 + 8;
+        uint32_t wk0[KQW], wk1[KQW];
+        load_bits<KQB, KQA>(pgb + r0 * G::KROW, tq * KQB, wk0);
+        load_bits<KQB, KQA>(pgb + r1 * G::KROW, tq * KQB, wk1);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t wq0[QQW], wq1[QQW];
         if constexpr (QJL) {
-          uint32_t b[4];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int pr = 2 * j + h;                 // pair index in the quad
-            const int ch = pr / SP, pin = pr % SP;
-            const int pe = ch * 2 * SP + pin, po = pe + SP;
-            const int wi = pe >> 5;
-            b[2 * h + 0] = sign_pair(wq0[wi], pe & 31, po - (wi << 5));
-            b[2 * h + 1] = sign_pair(wq1[wi], pe & 31, po - (wi << 5));
-          }
-          mma_f16_16816(acc2, b, sqf[j][0], sqf[j][1]);
+          load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r0 * G::QROW, tq * QQB, wq0);
+          load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r1 * G::QROW, tq * QQB, wq1);
         }
-      }
-      const __half* kn = reinterpret_cast<const __half*>(pgb + G::OFF_KN);
-      const __half* vn = reinterpret_cast<const __half*>(pgb + G::OFF_VN);
-      const bool ok0 = tok0 + gq < T32, ok1 = tok0 + gq + 8 < T32;
-      const float n0 = __half2float(kn[r0]), n1 = __half2float(kn[r1]);
-      float s00 = acc[0] * n0, s01 = acc[1] * n0, s10 = acc[2] * n1, s11 = acc[3] * n1;
-      if constexpr (QJL) {
-        const __half* kr = reinterpret_cast<const __half*>(pgb + G::OFF_KR);
-        const float g0 = __half2float(kr[r0]), g1 = __half2float(kr[r1]);
-        s00 = fmaf(acc2[0], g0, s00); s01 = fmaf(acc2[1], g0, s01);
-        s10 = fmaf(acc2[2], g1, s10); s11 = fmaf(acc2[3], g1, s11);
-      }
-      if (!ok0) { s00 = kNegInf; s01 = kNegInf; }
-      if (!ok1) { s10 = kNegInf; s11 = kNegInf; }
-
-      // ---------------- online softmax (columns = heads 2tq, 2tq+1) ---------
-      float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-      }
-      if (mx0 > m0) {            // rescale only when the running max grows
-        const float c = fast_exp2(m0 - mx0);
-        l0 *= c;
-#pragma unroll
-        for (int i2 = 0; i2 < NJ; ++i2) { O[i2][0] *= c; O[i2][2] *= c; }
-        m0 = mx0;
-      }
-      if (mx1 > m1) {
-        const float c = fast_exp2(m1 - mx1);
-        l1 *= c;
-#pragma unroll
-        for (int i2 = 0; i2 < NJ; ++i2) { O[i2][1] *= c; O[i2][3] *= c; }
-        m1 = mx1;
-      }
-      const float b0s = m0 == kNegInf ? 0.f : m0, b1s = m1 == kNegInf ? 0.f : m1;
-      const float p00 = fast_exp2(s00 - b0s), p01 = fast_exp2(s01 - b1s);
-      const float p10 = fast_exp2(s10 - b0s), p11 = fast_exp2(s11 - b1s);
-      l0 += p00 + p10;
-      l1 += p01 + p11;
-
-      // ---------------- P' = p * ||v|| -> B fragments -----------------------
-      const float v0 = ok0 ? __half2float(vn[r0]) : 0.f;
-      const float v1 = ok1 ? __half2float(vn[r1]) : 0.f;
-      const uint32_t pb0 = movmatrix_trans(pack_half2(p00 * v0, p01 * v0));
-      const uint32_t pb1 = movmatrix_trans(pack_half2(p10 * v1, p11 * v1));
-
-      // ---------------- O^T += V^T P ----------------------------------------
-      const int t0r = warp * 16 + 2 * tq;
-      uint32_t wa[VOW], wb[VOW], wc[VOW], wd[VOW];
-      load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 0) * G::VROW, gq * VOB, wa);
-      load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 1) * G::VROW, gq * VOB, wb);
-      load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 8) * G::VROW, gq * VOB, wc);
-      load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 9) * G::VROW, gq * VOB, wd);
-      if constexpr (VINTER) {
-        // combine the two tokens of each pair word-wise: field c of lo/hi is
-        // (code of token a) | (code of token b) << VB
-        constexpr uint32_t M = VB == 1 ? 0x55555555u : VB == 2 ? 0x33333333u : 0x0F0F0F0Fu;
-        uint32_t lab[VOW], hab[VOW], lcd[VOW], hcd[VOW];
-#pragma unroll
-        for (int x = 0; x < VOW; ++x) {
-          lab[x] = (wa[x] & M) | ((wb[x] << VB) & ~M);
-          hab[x] = ((wa[x] >> VB) & M) | (wb[x] & ~M);
-          lcd[x] = (wc[x] & M) | ((wd[x] << VB) & ~M);
-          hcd[x] = ((wc[x] >> VB) & M) | (wd[x] & ~M);
-        }
-        constexpr int PER = 32 / VB;                 // codes per word
-#pragma unroll
-        for (int i2 = 0; i2 < NJ; ++i2) {
-          const int c0 = 2 * i2;                     // even position -> lo, odd -> hi
-          const int o = ((c0 % PER) & ~1) * VB + (c0 / PER) * 32;
+  #pragma unroll
+        for (int j = 0; j < NJ; ++j) {
           uint32_t a[4];
-          a[0] = lds32(lutv, field_addr<2 * VB>(lab, o, lane4));
-          a[1] = lds32(lutv, field_addr<2 * VB>(hab, o, lane4));
-          a[2] = lds32(lutv, field_addr<2 * VB>(lcd, o, lane4));
-          a[3] = lds32(lutv, field_addr<2 * VB>(hcd, o, lane4));
-          mma_f16_16816(O[i2], a, pb0, pb1);
-        }
-      } else {
-#pragma unroll
-        for (int i2 = 0; i2 < NJ; ++i2) {
-          const int c0p = (2 * i2) * VB, c1p = (2 * i2 + 1) * VB;
-          uint32_t a[4];
-          if constexpr (Lut<VB>::kPair) {
-            a[0] = lds32(lutv, (((getbits(wb, c0p, VB) << VB) | getbits(wa, c0p, VB)) << 7 | lane4));
-            a[1] = lds32(lutv, (((getbits(wb, c1p, VB) << VB) | getbits(wa, c1p, VB)) << 7 | lane4));
-            a[2] = lds32(lutv, (((getbits(wd, c0p, VB) << VB) | getbits(wc, c0p, VB)) << 7 | lane4));
-            a[3] = lds32(lutv, (((getbits(wd, c1p, VB) << VB) | getbits(wc, c1p, VB)) << 7 | lane4));
+          const int o0 = (4 * j) * KB, o1 = (4 * j + 2) * KB;   // quad entries 4j.., 4j+2..
+          if constexpr (G::FAST) {
+            // pair bytes 2j and 2j + 1 of the quad
+            const int wi = j >> 1, b0 = 2 * (j & 1);
+            a[0] = lds32(smem, fast_addr(wk0[wi], lane4, b0));
+            a[1] = lds32(smem, fast_addr(wk1[wi], lane4, b0));
+            a[2] = lds32(smem, fast_addr(wk0[wi], lane4, b0 + 1));
+            a[3] = lds32(smem, fast_addr(wk1[wi], lane4, b0 + 1));
+          } else if constexpr (Lut<KB>::kPair) {
+            a[0] = lds32(lutk, field_addr<2 * KB>(wk0, o0, lane4));
+            a[1] = lds32(lutk, field_addr<2 * KB>(wk1, o0, lane4));
+            a[2] = lds32(lutk, field_addr<2 * KB>(wk0, o1, lane4));
+            a[3] = lds32(lutk, field_addr<2 * KB>(wk1, o1, lane4));
           } else {
-            a[0] = lds16(lutv, (getbits(wa, c0p, VB) << 1)) | (lds16(lutv, (getbits(wb, c0p, VB) << 1)) << 16);
-            a[1] = lds16(lutv, (getbits(wa, c1p, VB) << 1)) | (lds16(lutv, (getbits(wb, c1p, VB) << 1)) << 16);
-            a[2] = lds16(lutv, (getbits(wc, c0p, VB) << 1)) | (lds16(lutv, (getbits(wd, c0p, VB) << 1)) << 16);
-            a[3] = lds16(lutv, (getbits(wc, c1p, VB) << 1)) | (lds16(lutv, (getbits(wd, c1p, VB) << 1)) << 16);
+            a[0] = lds16(lutk, getbits(wk0, o0, KB) << 1) | (lds16(lutk, getbits(wk0, o0 + KB, KB) << 1) << 16);
+            a[1] = lds16(lutk, getbits(wk1, o0, KB) << 1) | (lds16(lutk, getbits(wk1, o0 + KB, KB) << 1) << 16);
+            a[2] = lds16(lutk, getbits(wk0, o1, KB) << 1) | (lds16(lutk, getbits(wk0, o1 + KB, KB) << 1) << 16);
+            a[3] = lds16(lutk, getbits(wk1, o1, KB) << 1) | (lds16(lutk, getbits(wk1, o1 + KB, KB) << 1) << 16);
           }
-          mma_f16_16816(O[i2], a, pb0, pb1);
+          mma_f16_16816(acc, a, qf[j][0], qf[j][1]);
+          if constexpr (QJL) {
+            uint32_t b[4];
+  #pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int pr = 2 * j + h;                 // pair index in the quad
+              const int ch = pr / SP, pin = pr % SP;
+              const int pe = ch * 2 * SP + pin, po = pe + SP;
+              const int wi = pe >> 5;
+              b[2 * h + 0] = sign_pair(wq0[wi], pe & 31, po - (wi << 5));
+              b[2 * h + 1] = sign_pair(wq1[wi], pe & 31, po - (wi << 5));
+            }
+            mma_f16_16816(acc2, b, sqf[j][0], sqf[j][1]);
+          }
+        }
+        const __half* kn = reinterpret_cast<const __half*>(pgb + G::OFF_KN);
+        const __half* vn = reinterpret_cast<const __half*>(pgb + G::OFF_VN);
+        const bool ok0 = tok0 + gq < T32, ok1 = tok0 + gq + 8 < T32;
+        const float n0 = __half2float(kn[r0]), n1 = __half2float(kn[r1]);
+        float s00 = acc[0] * n0, s01 = acc[1] * n0, s10 = acc[2] * n1, s11 = acc[3] * n1;
+        if constexpr (QJL) {
+          const __half* kr = reinterpret_cast<const __half*>(pgb + G::OFF_KR);
+          const float g0 = __half2float(kr[r0]), g1 = __half2float(kr[r1]);
+          s00 = fmaf(acc2[0], g0, s00); s01 = fmaf(acc2[1], g0, s01);
+          s10 = fmaf(acc2[2], g1, s10); s11 = fmaf(acc2[3], g1, s11);
+        }
+        if (!ok0) { s00 = kNegInf; s01 = kNegInf; }
+        if (!ok1) { s10 = kNegInf; s11 = kNegInf; }
+
+        // ---------------- online softmax (columns = heads 2tq, 2tq+1) ---------
+        float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
+  #pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        if (mx0 > m0) {            // rescale only when the running max grows
+          const float c = fast_exp2(m0 - mx0);
+          l0 *= c;
+  #pragma unroll
+          for (int i2 = 0; i2 < NJ; ++i2) { O[i2][0] *= c; O[i2][2] *= c; }
+          m0 = mx0;
+        }
+        if (mx1 > m1) {
+          const float c = fast_exp2(m1 - mx1);
+          l1 *= c;
+  #pragma unroll
+          for (int i2 = 0; i2 < NJ; ++i2) { O[i2][1] *= c; O[i2][3] *= c; }
+          m1 = mx1;
+        }
+        const float b0s = m0 == kNegInf ? 0.f : m0, b1s = m1 == kNegInf ? 0.f : m1;
+        const float p00 = fast_exp2(s00 - b0s), p01 = fast_exp2(s01 - b1s);
+        const float p10 = fast_exp2(s10 - b0s), p11 = fast_exp2(s11 - b1s);
+        l0 += p00 + p10;
+        l1 += p01 + p11;
+
+        // ---------------- P' = p * ||v|| -> B fragments -----------------------
+        const float v0 = ok0 ? __half2float(vn[r0]) : 0.f;
+        const float v1 = ok1 ? __half2float(vn[r1]) : 0.f;
+        const uint32_t pb0 = movmatrix_trans(pack_half2(p00 * v0, p01 * v0));
+        const uint32_t pb1 = movmatrix_trans(pack_half2(p10 * v1, p11 * v1));
+
+        // ---------------- O^T += V^T P ----------------------------------------
+        const int t0r = tw * 16 + 2 * tq;
+        uint32_t wa[VOW], wb[VOW], wc[VOW], wd[VOW];
+        load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 0) * G::VROW, gq * VOB, wa);
+        load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 1) * G::VROW, gq * VOB, wb);
+        load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 8) * G::VROW, gq * VOB, wc);
+        load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 9) * G::VROW, gq * VOB, wd);
+        if constexpr (G::FAST && VB == 2) {
+          // bytes of lo (hi): codes at positions 4k, 4k+1 (4k+2, 4k+3) of token
+          // a in the low nibble and of token b in the high nibble
+          const uint32_t lab = (wa[0] & 0x0F0F0F0Fu) | ((wb[0] << 4) & 0xF0F0F0F0u);
+          const uint32_t hab = ((wa[0] >> 4) & 0x0F0F0F0Fu) | (wb[0] & 0xF0F0F0F0u);
+          const uint32_t lcd = (wc[0] & 0x0F0F0F0Fu) | ((wd[0] << 4) & 0xF0F0F0F0u);
+          const uint32_t hcd = ((wc[0] >> 4) & 0x0F0F0F0Fu) | (wd[0] & 0xF0F0F0F0u);
+          const uint32_t lane_v = 128u + ((uint32_t)(lane & 15) << 3);
+  #pragma unroll
+          for (int i2 = 0; i2 < NJ; ++i2) {
+            const uint2 eab = lds64(smem, fast_addr((i2 & 1) ? hab : lab, lane_v, i2 >> 1));
+            const uint2 ecd = lds64(smem, fast_addr((i2 & 1) ? hcd : lcd, lane_v, i2 >> 1));
+            const uint32_t a[4] = {eab.x, eab.y, ecd.x, ecd.y};
+            mma_f16_16816(O[i2], a, pb0, pb1);
+          }
+        } else if constexpr (G::FAST && VB == 4) {
+          // per word: byte k of lo (hi) = code at position 2k (2k+1) of token a,
+          // and of token b in the high nibble
+          uint32_t lab[2], hab[2], lcd[2], hcd[2];
+  #pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            lab[x] = (wa[x] & 0x0F0F0F0Fu) | ((wb[x] << 4) & 0xF0F0F0F0u);
+            hab[x] = ((wa[x] >> 4) & 0x0F0F0F0Fu) | (wb[x] & 0xF0F0F0F0u);
+            lcd[x] = (wc[x] & 0x0F0F0F0Fu) | ((wd[x] << 4) & 0xF0F0F0F0u);
+            hcd[x] = ((wc[x] >> 4) & 0x0F0F0F0Fu) | (wd[x] & 0xF0F0F0F0u);
+          }
+          const uint32_t lane_v = 128u + lane4;
+  #pragma unroll
+          for (int i2 = 0; i2 < NJ; ++i2) {
+            const int x = i2 >> 2, k = i2 & 3;
+            const uint32_t a[4] = {lds32(smem, fast_addr(lab[x], lane_v, k)),
+                                   lds32(smem, fast_addr(hab[x], lane_v, k)),
+                                   lds32(smem, fast_addr(lcd[x], lane_v, k)),
+                                   lds32(smem, fast_addr(hcd[x], lane_v, k))};
+            mma_f16_16816(O[i2], a, pb0, pb1);
+          }
+        } else if constexpr (VINTER) {
+          // combine the two tokens of each pair word-wise: field c of lo/hi is
+          // (code of token a) | (code of token b) << VB
+          constexpr uint32_t M = VB == 1 ? 0x55555555u : VB == 2 ? 0x33333333u : 0x0F0F0F0Fu;
+          uint32_t lab[VOW], hab[VOW], lcd[VOW], hcd[VOW];
+  #pragma unroll
+          for (int x = 0; x < VOW; ++x) {
+            lab[x] = (wa[x] & M) | ((wb[x] << VB) & ~M);
+            hab[x] = ((wa[x] >> VB) & M) | (wb[x] & ~M);
+            lcd[x] = (wc[x] & M) | ((wd[x] << VB) & ~M);
+            hcd[x] = ((wc[x] >> VB) & M) | (wd[x] & ~M);
+          }
+          constexpr int PER = 32 / VB;                 // codes per word
+  #pragma unroll
+          for (int i2 = 0; i2 < NJ; ++i2) {
+            const int c0 = 2 * i2;                     // even position -> lo, odd -> hi
+            const int o = ((c0 % PER) & ~1) * VB + (c0 / PER) * 32;
+            uint32_t a[4];
+            a[0] = lds32(lutv, field_addr<2 * VB>(lab, o, lane4));
+            a[1] = lds32(lutv, field_addr<2 * VB>(hab, o, lane4));
+            a[2] = lds32(lutv, field_addr<2 * VB>(lcd, o, lane4));
+            a[3] = lds32(lutv, field_addr<2 * VB>(hcd, o, lane4));
+            mma_f16_16816(O[i2], a, pb0, pb1);
+          }
+        } else {
+  #pragma unroll
+          for (int i2 = 0; i2 < NJ; ++i2) {
+            const int c0p = (2 * i2) * VB, c1p = (2 * i2 + 1) * VB;
+            uint32_t a[4];
+            if constexpr (Lut<VB>::kPair) {
+              a[0] = lds32(lutv, (((getbits(wb, c0p, VB) << VB) | getbits(wa, c0p, VB)) << 7 | lane4));
+              a[1] = lds32(lutv, (((getbits(wb, c1p, VB) << VB) | getbits(wa, c1p, VB)) << 7 | lane4));
+              a[2] = lds32(lutv, (((getbits(wd, c0p, VB) << VB) | getbits(wc, c0p, VB)) << 7 | lane4));
+              a[3] = lds32(lutv, (((getbits(wd, c1p, VB) << VB) | getbits(wc, c1p, VB)) << 7 | lane4));
+            } else {
+              a[0] = lds16(lutv, (getbits(wa, c0p, VB) << 1)) | (lds16(lutv, (getbits(wb, c0p, VB) << 1)) << 16);
+              a[1] = lds16(lutv, (getbits(wa, c1p, VB) << 1)) | (lds16(lutv, (getbits(wb, c1p, VB) << 1)) << 16);
+              a[2] = lds16(lutv, (getbits(wc, c0p, VB) << 1)) | (lds16(lutv, (getbits(wd, c0p, VB) << 1)) << 16);
+              a[3] = lds16(lutv, (getbits(wc, c1p, VB) << 1)) | (lds16(lutv, (getbits(wd, c1p, VB) << 1)) << 16);
+            }
+            mma_f16_16816(O[i2], a, pb0, pb1);
+          }
         }
       }
+
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (++ring == G::SG) { ring = 0; phase ^= 1u; }
     }
 
     // ---------------- segment end: combine warps, emit partial ---------------
-    const bool seg_end = (pg == Pv32 - 1) || (i == npages - 1);
-    if (seg_end) {
+    {
       float L0 = l0, L1 = l1;
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) {
@@ -498,14 +618,18 @@ decode_kernel(DecodeParams p) {
         }
       }
       named_bar(1, NCT);
-      if (i != npages - 1) {                   // restore the K table
-        build_lut<KB>(lutk, p.kc, tid, NCT);
+      if (i1 != npages) {                      // restore the table rows the scratch used
+        if constexpr (G::FAST)
+          build_fast_lut<VB>(smem, p.kc, p.vc, 0, (G::COMB + 255) / 256, tid, NCT);
+        else
+          build_lut<KB>(lutk, p.kc, tid, NCT);
         named_bar(1, NCT);
       }
       reset_state();
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
+    i0 = i1;
+    ++s;
+    pg0 = 0;
   }
 }
 
@@ -866,10 +990,12 @@ struct Variant {
   int D, kb, vb, qjl;
   DecodeFn fn;
   size_t (*smem)();
+  int threads;
 };
 
 #define TQ_VARIANT(D_, KB_, VB_, Q_) \
-  {D_, KB_, VB_, Q_, decode_kernel<D_, KB_, VB_, (Q_ != 0)>, dec_smem_bytes<D_, KB_, VB_, (Q_ != 0)>}
+  {D_, KB_, VB_, Q_, decode_kernel<D_, KB_, VB_, (Q_ != 0)>, dec_smem_bytes<D_, KB_, VB_, (Q_ != 0)>, \
+   Dec<D_, KB_, VB_, (Q_ != 0)>::THREADS}
 #define TQ_VARIANT2(D_, KB_, VB_) TQ_VARIANT(D_, KB_, VB_, 0), TQ_VARIANT(D_, KB_, VB_, 1)
 
 const Variant kVariants[] = {
@@ -920,7 +1046,7 @@ Plan make_plan(const tq_geom* G, const tq_cache* c, const tq_decode_args* a, int
 }
 
 int occupancy_of(const Variant* v, size_t smem) {
-  return occupancy((const void*)v->fn, kDecThreads, smem);
+  return occupancy((const void*)v->fn, v->threads, smem);
 }
 
 }  // namespace
@@ -1013,7 +1139,7 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   dp.part_o = reinterpret_cast<float*>(w + pl.off_o);
   dp.status = reinterpret_cast<uint32_t*>(w);
   if (pl.ctas > 0 && (phases & TQ_PHASE_DECODE)) {
-    if (launch_result(launch_pdl(v->fn, dim3(pl.ctas, pl.nch), dim3(kDecThreads), smem, st, dp),
+    if (launch_result(launch_pdl(v->fn, dim3(pl.ctas, pl.nch), dim3(v->threads), smem, st, dp),
                       "tq_decode_attn/decode") != TQ_OK)
       return TQ_ERR_CUDA;
   }

@@ -36,9 +36,8 @@ def tensor4(x: torch.Tensor) -> _lib.Tensor4:
     t = _lib.Tensor4()
     t.data = x.data_ptr()
     t.dtype = _DT[x.dtype]
-    for i in range(4):
-        t.shape[i] = x.shape[i]
-        t.stride[i] = x.stride(i)
+    t.shape[:] = x.shape
+    t.stride[:] = x.stride()
     return t
 
 
@@ -81,10 +80,28 @@ class LayerTables:
             self.qjl_mat = self.qjl_mat.contiguous().float()
             self.qjl_t = self.qjl_mat.t().contiguous()
 
+    def __setattr__(self, name, value):
+        # a changed table invalidates the cached C descriptors
+        self.__dict__.pop("_geom", None)
+        self.__dict__.pop("_ctab", None)
+        super().__setattr__(name, value)
+
     def geom(self) -> _lib.Geom:
-        return _lib.Geom(self.head_dim, self.key_bits, self.value_bits, 1 if self.qjl else 0)
+        g = self.__dict__.get("_geom")
+        if g is None:
+            g = _lib.Geom(self.head_dim, self.key_bits, self.value_bits, 1 if self.qjl else 0)
+            self.__dict__["_geom"] = g
+        return g
 
     def ctables(self) -> _lib.Tables:
+        """The C table descriptor (built once: the tables never move)."""
+        t = self.__dict__.get("_ctab")
+        if t is None:
+            t = self._build_ctables()
+            self.__dict__["_ctab"] = t
+        return t
+
+    def _build_ctables(self) -> _lib.Tables:
         t = _lib.Tables()
         t.k_centroids = self.k_centroids.data_ptr()
         t.k_boundaries = self.k_boundaries.data_ptr()
@@ -117,11 +134,7 @@ def page_bytes(head_dim: int, key_bits: int, value_bits: int, qjl: bool) -> int:
 
 
 def _cache_desc(pages: torch.Tensor) -> _lib.Cache:
-    c = _lib.Cache()
-    c.pages = pages.data_ptr()
-    c.streams = pages.shape[0]
-    c.pages_per_stream = pages.shape[1]
-    return c
+    return _lib.Cache(pages.data_ptr(), pages.shape[0], pages.shape[1])
 
 
 # ---------------------------------------------------------------------------

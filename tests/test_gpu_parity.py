@@ -179,6 +179,7 @@ DECODE_CASES = [
     (128, 3, 3, True, 1, 1, 5, 64, 0),
     (128, 2, 2, False, 3, 1, 1, 65, 0),
     (128, 4, 4, False, 1, 2, 16, 130, 0),
+    (128, 4, 4, True, 2, 2, 4, 200, 5),
     (128, 6, 4, True, 1, 2, 8, 200, 7),
     (128, 5, 5, False, 2, 1, 3, 17, 16),
     (128, 8, 8, False, 1, 1, 2, 90, 0),
