@@ -13,8 +13,9 @@
 // queries once, attends centroid values decoded from the codes, and
 // un-rotates its output once.
 //
-// One CTA = 128 consecutive query positions of one query head, 8 warps of 16
-// positions.  Per 64-token page (one key tile): a bulk async copy brings the
+// One CTA = 128 query rows of one KV head's GQA group: hc heads (the largest
+// of 8, 4, 2, 1 dividing the group) x 128 / hc consecutive positions, 8 warps
+// of 16 rows, so each decoded page serves hc heads.  Per 64-token page (one key tile): a bulk async copy brings the
 // page into shared memory (double-buffered, mbarrier), all threads decode the
 // K and V codes into fp16 tiles in coordinate order, then every warp runs
 // S = Q' K^T and O += P' V with mma.sync m16n8k16 (fp16 in, fp32 accumulate)
@@ -29,7 +30,6 @@ namespace {
 
 constexpr int kPfWarps = 8;
 constexpr int kPfThreads = 32 * kPfWarps;
-constexpr int kPfRows = 16 * kPfWarps;      // query positions per CTA
 constexpr float kLog2eP = 1.4426950408889634f;
 
 struct PrefillParams {
@@ -41,7 +41,8 @@ struct PrefillParams {
   const float* vc;
   const void* q; int q_dtype; int64_t qs[4];     // (B, Hq, Tq, D)
   void* out; int o_dtype; int64_t os[4];
-  int64_t Hq, g, Tq, n_tokens;
+  int64_t Hq, Hkv, g, Tq, n_tokens;
+  int hc;                       // query heads per CTA
   float scale;                  // softmax scale
   int causal;
   int nqb;                      // query blocks per head
@@ -105,13 +106,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(PrefillParams p)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = lane >> 2, tq = lane & 3;
+  const int wph = kPfWarps / p.hc;                     // warps per head
+  const int P = 16 * wph;                              // query positions per CTA
   const int qb = p.nqb - 1 - (int)blockIdx.x;          // long rows first
-  const int64_t bh = blockIdx.y;                       // b * Hq + h
-  const int64_t b = bh / p.Hq, h = bh % p.Hq;
-  const int64_t stream = b * (p.Hq / p.g) + h / p.g;
+  const int nchunk = (int)(p.g / p.hc);
+  const int64_t stream = (int64_t)blockIdx.y / nchunk;  // b * Hkv + kv head
+  const int chunk = (int)((int64_t)blockIdx.y % nchunk);
+  const int64_t b = stream / p.Hkv, kvh = stream % p.Hkv;
+  const int64_t h = kvh * p.g + (int64_t)chunk * p.hc + warp / wph;   // this warp's head
   const int64_t t_base = p.n_tokens - p.Tq;            // position of query 0
-  const int t0 = qb * kPfRows + warp * 16;             // this warp's first query
-  const int64_t qpos_max = t_base + tmin<int64_t>((int64_t)(qb + 1) * kPfRows, p.Tq) - 1;
+  const int t0 = qb * P + (warp % wph) * 16;           // this warp's first query
+  const int64_t qpos_max = t_base + tmin<int64_t>((int64_t)(qb + 1) * P, p.Tq) - 1;
   const int64_t kend = p.causal ? qpos_max + 1 : p.n_tokens;   // keys this CTA needs
   const int ntiles = (int)((kend + 63) / 64);
 
@@ -423,12 +428,14 @@ int launch_prefill(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   p.out = a->out->data; p.o_dtype = a->out->dtype;
   for (int i = 0; i < 4; ++i) { p.qs[i] = a->q->stride[i]; p.os[i] = a->out->stride[i]; }
   p.Hq = a->q->shape[1];
-  p.g = a->q->shape[1] / (c->streams / a->q->shape[0]);
+  p.Hkv = c->streams / a->q->shape[0];
+  p.g = a->q->shape[1] / p.Hkv;
+  p.hc = p.g % 8 == 0 ? 8 : p.g % 4 == 0 ? 4 : p.g % 2 == 0 ? 2 : 1;
   p.Tq = a->q->shape[2];
   p.n_tokens = a->n_tokens;
   p.scale = a->scale;
   p.causal = a->causal;
-  p.nqb = (int)((p.Tq + kPfRows - 1) / kPfRows);
+  p.nqb = (int)((p.Tq + 16 * (kPfWarps / p.hc) - 1) / (16 * (kPfWarps / p.hc)));
   p.status = status;
   if (p.Tq == 0) return TQ_OK;
   PfFn fn = G->head_dim == 128 ? pf_fn<128>(G->key_bits, G->value_bits)
@@ -441,7 +448,7 @@ int launch_prefill(const tq_geom* G, const tq_tables* t, const tq_cache* c,
     return TQ_ERR_INVALID;
   }
   if (set_smem_attr((const void*)fn, smem) != TQ_OK) return TQ_ERR_CUDA;
-  dim3 grid((unsigned)p.nqb, (unsigned)(a->q->shape[0] * p.Hq));
+  dim3 grid((unsigned)p.nqb, (unsigned)(a->q->shape[0] * p.Hq / p.hc));
   fn<<<grid, kPfThreads, smem, st>>>(p);
   return check_launch("tq_prefill_attn");
 }
