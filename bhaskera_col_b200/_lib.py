@@ -27,7 +27,7 @@ EXPORTED = (
     "tq_last_error", "tq_version", "tq_page_bytes", "tq_quantize_rotated",
     "tq_append", "tq_dequantize", "tq_decode_workspace_bytes", "tq_decode_attn",
     "tq_decode_step", "tq_decode_attn_noalloc", "tq_workspace_status", "tq_device_status",
-    "tq_append_tensor_core", "tq_prefill_attn",
+    "tq_append_tensor_core", "tq_prefill_attn", "tq_prefill_tensor_core",
 )
 
 
@@ -73,7 +73,7 @@ class DecodeArgs(ctypes.Structure):
 class PrefillArgs(ctypes.Structure):
     _fields_ = [("q", ctypes.POINTER(Tensor4)), ("out", ctypes.POINTER(Tensor4)),
                 ("n_tokens", ctypes.c_int64), ("scale", ctypes.c_float),
-                ("causal", ctypes.c_int32)]
+                ("causal", ctypes.c_int32), ("engine", ctypes.c_int32)]
 
 
 _lock = threading.Lock()
@@ -110,6 +110,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             "tq_device_status": (I32, [P(ctypes.c_uint32), VP]),
             "tq_append_tensor_core": (I32, [P(Geom), P(Tables), P(Tensor4), P(Tensor4)]),
             "tq_prefill_attn": (I32, [P(Geom), P(Tables), P(Cache), P(PrefillArgs), VP]),
+            "tq_prefill_tensor_core": (I32, [P(Geom)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)

@@ -321,9 +321,14 @@ int32_t tq_prefill_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
     set_error("%s: tables.rot_f16 (R as fp16, 16-byte aligned) is required", fn);
     return TQ_ERR_INVALID;
   }
-  if (!prefill_supported(g->head_dim, g->key_bits, g->value_bits)) {
-    set_error("%s: no kernel for head_dim %d, key_bits %d, value_bits %d", fn, g->head_dim,
-              g->key_bits, g->value_bits);
+  if (a->engine != 0 && a->engine != 1) {
+    set_error("%s: engine must be 0 (fastest) or 1 (mma.sync), got %d", fn, a->engine);
+    return TQ_ERR_INVALID;
+  }
+  if (!prefill_supported(g->head_dim, g->key_bits, g->value_bits) &&
+      !(a->engine == 0 && prefill_tc_applies(g))) {
+    set_error("%s: no kernel for head_dim %d, key_bits %d, value_bits %d (engine %d)", fn,
+              g->head_dim, g->key_bits, g->value_bits, a->engine);
     return TQ_ERR_INVALID;
   }
   const tq_tensor4 *q = a->q, *o = a->out;
@@ -372,6 +377,11 @@ int32_t tq_append_tensor_core(const tq_geom* g, const tq_tables* t, const tq_ten
                               const tq_tensor4* v) {
   if (!g || !t || !k || !v) return 0;
   return append_tc_applies(g, t, k, v) ? 1 : 0;
+}
+
+int32_t tq_prefill_tensor_core(const tq_geom* g) {
+  if (!g || check_geom(g, "tq_prefill_tensor_core")) return 0;
+  return prefill_tc_applies(g) ? 1 : 0;
 }
 
 int32_t tq_device_status(uint32_t* status, void* stream) {

@@ -34,6 +34,11 @@ int read_tc_status(uint32_t* out, cudaStream_t st);
 // Device address of the library status word read by tq_device_status.
 uint32_t* device_status_word();
 bool prefill_supported(int D, int kb, int vb);
+// tcgen05 prefill attention (tq_prefill_tc.cu): TQ_OK when it ran, 1 when it
+// does not apply (the caller uses the mma.sync kernel), or an error.
+int launch_prefill_tc(const tq_geom* g, const tq_tables* t, const tq_cache* c,
+                      const tq_prefill_args* a, uint32_t* status, cudaStream_t st);
+bool prefill_tc_applies(const tq_geom* g);
 int launch_prefill(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                    const tq_prefill_args* a, uint32_t* status, cudaStream_t st);
 int launch_dequant(const tq_geom* g, const tq_tables* t, const tq_cache* c,

@@ -412,6 +412,10 @@ bool prefill_supported(int D, int kb, int vb) {
 
 int launch_prefill(const tq_geom* G, const tq_tables* t, const tq_cache* c,
                    const tq_prefill_args* a, uint32_t* status, cudaStream_t st) {
+  if (a->engine == 0) {
+    const int rc = launch_prefill_tc(G, t, c, a, status, st);
+    if (rc != 1) return rc;
+  }
   PrefillParams p;
   const PageGeom g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
   p.pages = c->pages;

@@ -1,0 +1,796 @@
+// tq_prefill_tc.cu — prefill attention straight off the packed pages on the
+// 5th-generation tensor cores (tcgen05 MMAs, accumulators in tensor memory),
+// for head_dim 128 with 2- to 4-bit K and V codes.  Other shapes use the
+// mma.sync kernel of tq_prefill.cu.
+//
+// Same result as tq_prefill.cu (which gives the reference mapping):
+// softmax(scale q K^T) V over the dequantised keys and values
+// x^ = n (c[idx] R), computed as
+//     O = softmax(q' K^T) V^,  out = O R_V
+// with q' = scale log2(e) q R_K^T, K^ = n_k c_k[idx] and V^ = n_v c_v[idx].
+// Columns stay in the packed orders of the page rows: K^ and q' in the quad
+// order of a K row, V^ and O in the octet order of a V row.  R_K and R_V are
+// R with its rows permuted into those orders, so no code is ever moved to its
+// coordinate.
+//
+// CTA = 128 query rows (hc heads x 128/hc positions of one KV head's GQA
+// group, as in tq_prefill.cu) and key tiles of 128 tokens (two pages).
+// Warp roles (13 warps):
+//   warp 0      owns tensor memory; one thread issues every MMA:
+//               q' = Q R_K^T, then per tile S_j = q' K^_j^T and O += P_j V^_j,
+//               finally OUT = O^ R_V
+//   warps 1-4   softmax, one thread per query row (= tensor-memory lane):
+//               reads S_j, writes P_j = exp2(S_j - m) as fp16 over the S_j
+//               columns (the A operand of the PV MMA, read from tensor memory),
+//               rescales O in tensor memory when the running max grows by more
+//               than 8 (p <= 2^8 otherwise: exact, fp16-safe)
+//   warps 5-12  decoders: codes -> fp16 K^ and V^ tiles in the 128-byte
+//               swizzled layout, through pair tables (two codes -> one half2)
+//               replicated across lanes; codes are read from the pages in
+//               global memory with one tile of register prefetch
+// Tensor memory, 512 columns: S/P double buffer at 0 and 128, O at 256.
+// Shared memory: q' (later O^) 32 KB, two K^ and two V^ stages of 32 KB, the
+// pair tables.  R_K is staged in V stage 0 before the first tile and R_V in
+// K stage 0 after the last.
+//
+// K^ (K-major B of S = q' K^^T) and V^ (MN-major B of O = P V^) share one
+// physical layout: [64-column half][128 keys][128 B], 16-byte chunks swizzled
+// by key & 7.  The operand descriptors differ: K-major walks 32 B along a row
+// per 16-deep MMA step, MN-major walks 16 rows (2048 B) with the halves 16 KB
+// apart.
+//
+// Every wait is bounded; on expiry the kernel sets TQ_DEV_WAIT_TIMEOUT in the
+// status word, the other roles see the abort flag, no MMA is left in flight
+// and tensor memory is released.
+#include "tq_common.cuh"
+#include "tq_internal.h"
+#include "tq_tc.cuh"
+
+#include <math.h>
+
+namespace tq {
+namespace {
+
+constexpr int kD = 128;
+constexpr int kRows = 128;                 // query rows per CTA
+constexpr int kKeys = 128;                 // keys per tile (two pages)
+constexpr int kSoftWarps = 4, kDecWarps = 8;
+constexpr int kWarps = 1 + kSoftWarps + kDecWarps;
+constexpr int kThreads = 32 * kWarps;      // 416
+constexpr int kDecThreads = 32 * kDecWarps;
+constexpr int kTmemCols = 512;
+constexpr int kOCol = 256;                 // O accumulator columns
+constexpr float kRescaleBits = 8.f;        // lazy rescale threshold (log2)
+constexpr float kLog2e = 1.4426950408889634f;
+
+constexpr uint32_t kHalfBytes = 16384;     // [128 rows][128 B]
+constexpr uint32_t kStage = 2 * kHalfBytes;
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_K = OFF_Q + kStage;
+constexpr uint32_t OFF_V = OFF_K + 2 * kStage;
+constexpr uint32_t OFF_LUT = OFF_V + 2 * kStage;
+constexpr uint32_t kLutMax = 36864;
+constexpr uint32_t OFF_BAR = OFF_LUT + kLutMax;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;   // + alignment slack
+
+enum Bar {
+  B_ROT = 0, B_QP = 1, B_KFULL = 2, B_KEMPTY = 4, B_VFULL = 6, B_VEMPTY = 8, B_SFULL = 10,
+  B_PFULL = 12, B_ODONE = 14, B_OFIN = 15, B_RV = 16, B_OUT = 17, B_MMA = 18, B_COUNT = 19
+};
+
+struct TcPrefillParams {
+  const uint8_t* pages;
+  int64_t pages_per_stream;
+  int page_bytes, off_v, off_kn, off_vn;
+  const __half* rot_h;          // R [128][128] fp16, row-major
+  const float* kc;
+  const float* vc;
+  const void* q; int q_dtype; int q_vec; int64_t qs[4];
+  void* out; int o_dtype; int o_vec; int64_t os[4];
+  int64_t Hkv, g, Tq, n_tokens;
+  int hc, pshift;               // heads per CTA; log2(positions per CTA)
+  int nqb;
+  float qscale;                 // softmax scale * log2(e)
+  int causal;
+  int rk, rv;                   // pair-table replication (lanes per copy set)
+  uint32_t* status;
+};
+
+// D (+)= A B with A and B in shared memory (kind::f16: fp16 or bf16 by idesc).
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  tc::umma_bf16(d_tmem, a_desc, b_desc, idesc, accumulate);
+}
+
+// D (+)= A B with A in tensor memory (lanes = rows, two 16-bit elements per
+// column) and B in shared memory.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// MN-major operand in the 128-byte swizzle layout: rows of 64 MN-contiguous
+// 16-bit elements (128 B), 8-row groups 1024 B apart (stride byte offset),
+// 64-element MN blocks `lbo` bytes apart (leading byte offset).
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// tcgen05.wait::ld that also names the destination registers, so no use of
+// them can be scheduled above the wait.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+        "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
+        "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+        "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :: "memory");
+}
+
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+        "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
+        "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
+               ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
+// Byte offset of 16-byte chunk `c` (0..15, 8 elements each) of row `r` in a
+// [2][rows][128 B] swizzled operand.
+__device__ __forceinline__ uint32_t sw_chunk(int r, int c) {
+  return (uint32_t)((c >> 3) * kHalfBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// Coordinate held at position i of a K row (quad order) / V row (octet order).
+__device__ __forceinline__ int k_coord(int i) {
+  const int t = i >> 5, e = i & 31;
+  return 16 * (e >> 2) + 2 * t + (e & 1) + 8 * ((e >> 1) & 1);
+}
+__device__ __forceinline__ int v_coord(int i) { return (i >> 4) + 8 * (i & 15); }
+
+__device__ __forceinline__ void fail(uint32_t* status, volatile int* abort_flag) {
+  *abort_flag = 1;
+  atomicOr(status, TQ_DEV_WAIT_TIMEOUT);
+}
+
+// Bounded wait that also gives up as soon as another role has aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag, uint32_t* status) {
+  for (uint32_t i = 0; i < 1000u; ++i) {
+    if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
+    if (*abort_flag) return false;
+  }
+  fail(status, abort_flag);
+  return false;
+}
+
+// 8-element fp16 chunk of a 16-bit source row -> fp16 scaled by s.
+__device__ __forceinline__ uint4 scale_chunk(uint4 raw, int dtype, float s) {
+  uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float lo, hi;
+    if (dtype == TQ_F16) {
+      const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      lo = __low2float(h); hi = __high2float(h);
+    } else {
+      lo = __uint_as_float(w[i] << 16);
+      hi = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+    o[i] = pack_half2(lo * s, hi * s);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Codes of one 32-position stream (a K quad or a V octet pair): NB words.
+template <int NB>
+struct Stream { uint32_t w[NB]; };
+
+template <int NB>
+__device__ __forceinline__ void load_stream(Stream<NB>& s, const uint8_t* src) {
+  if constexpr (NB == 4) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(src));
+    s.w[0] = v.x; s.w[1] = v.y; s.w[2] = v.z; s.w[3] = v.w;
+  } else if constexpr (NB == 2) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(src));
+    s.w[0] = v.x; s.w[1] = v.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < NB; ++i) s.w[i] = __ldg(reinterpret_cast<const uint32_t*>(src) + i);
+  }
+}
+
+// Pair p (positions 2p, 2p+1) of a stream of NB-bit codes: a 2*NB-bit index.
+template <int NB>
+__device__ __forceinline__ uint32_t pair_index(const Stream<NB>& s, int p) {
+  const int bo = 2 * NB * p, w = bo >> 5, sh = bo & 31;
+  constexpr uint32_t mask = (1u << (2 * NB)) - 1u;
+  if (sh + 2 * NB <= 32) return (s.w[w] >> sh) & mask;
+  return __funnelshift_r(s.w[w], s.w[w + 1], sh) & mask;
+}
+
+// Decode a 32-position stream into 4 fp16 chunks (x norm) and store them at
+// chunks c0..c0+3 of row `key` of the operand at `base`.
+template <int NB>
+__device__ __forceinline__ void decode_stream(const Stream<NB>& s, uint32_t lut, uint32_t rep4,
+                                              __half2 n2, uint32_t base, int key, int c0) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t h[4];
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      const uint32_t idx = pair_index<NB>(s, 4 * q + pp);
+      uint32_t v = tc::lds_u32(lut + idx * rep4);
+      __half2 x = *reinterpret_cast<__half2*>(&v);
+      x = __hmul2(x, n2);
+      h[pp] = *reinterpret_cast<uint32_t*>(&x);
+    }
+    sts128(base + sw_chunk(key, c0 + q), make_uint4(h[0], h[1], h[2], h[3]));
+  }
+}
+
+// The codes and norms one decoder thread needs for one tile: key kk of both
+// pages, K quad `part` and V octet pair `part`.
+template <int KB, int VB>
+struct TileRegs {
+  Stream<KB> k[2];
+  Stream<VB> v[2];
+  uint32_t nrm[2];              // kn | vn << 16 (fp16 bits)
+};
+
+struct TcParamsView {
+  const uint8_t* spages;        // this stream's pages
+  int page_bytes, off_v, off_kn, off_vn;
+  int kk, part;
+  int64_t kend;                 // keys this CTA needs
+};
+
+template <int KB, int VB>
+__device__ __forceinline__ void load_tile(TileRegs<KB, VB>& t, const TcParamsView& pv, int j) {
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int64_t key = (int64_t)j * kKeys + p * 64 + pv.kk;
+    if (key < pv.kend) {
+      const uint8_t* pg = pv.spages + (int64_t)(2 * j + p) * pv.page_bytes;
+      load_stream<KB>(t.k[p], pg + pv.kk * (16 * KB) + pv.part * (4 * KB));
+      load_stream<VB>(t.v[p], pg + pv.off_v + pv.kk * (16 * VB) + pv.part * (4 * VB));
+      const uint32_t kn = __ldg(reinterpret_cast<const unsigned short*>(pg + pv.off_kn) + pv.kk);
+      const uint32_t vn = __ldg(reinterpret_cast<const unsigned short*>(pg + pv.off_vn) + pv.kk);
+      t.nrm[p] = kn | (vn << 16);
+    } else {
+#pragma unroll
+      for (int i = 0; i < KB; ++i) t.k[p].w[i] = 0u;
+#pragma unroll
+      for (int i = 0; i < VB; ++i) t.v[p].w[i] = 0u;
+      t.nrm[p] = 0u;
+    }
+  }
+}
+
+template <int KB, int VB>
+__global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const uint32_t sbase = smem_u32(sm);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_COUNT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + B_COUNT + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int P = kRows / p.hc;                          // query positions per CTA
+  const int qb = p.nqb - 1 - (int)blockIdx.x;          // long rows first
+  const int nchunk = (int)(p.g / p.hc);
+  const int64_t stream = (int64_t)blockIdx.y / nchunk;
+  const int chunk = (int)((int64_t)blockIdx.y % nchunk);
+  const int64_t b = stream / p.Hkv, kvh = stream % p.Hkv;
+  const int64_t t_base = p.n_tokens - p.Tq;
+  const int64_t qpos_max = t_base + tmin<int64_t>((int64_t)(qb + 1) * P, p.Tq) - 1;
+  const int64_t kend = p.causal ? qpos_max + 1 : p.n_tokens;
+  const int ntiles = (int)((kend + kKeys - 1) / kKeys);
+
+  if (tid == 0) {
+    mbar_init(&bars[B_ROT], 1);
+    mbar_init(&bars[B_QP], kSoftWarps);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[B_KFULL + s], kDecWarps);
+      mbar_init(&bars[B_KEMPTY + s], 1);
+      mbar_init(&bars[B_VFULL + s], kDecWarps);
+      mbar_init(&bars[B_VEMPTY + s], 1);
+      mbar_init(&bars[B_SFULL + s], 1);
+      mbar_init(&bars[B_PFULL + s], kSoftWarps);
+    }
+    mbar_init(&bars[B_ODONE], 1);
+    mbar_init(&bars[B_OFIN], kSoftWarps);
+    mbar_init(&bars[B_RV], kDecWarps);
+    mbar_init(&bars[B_OUT], 1);
+    mbar_init(&bars[B_MMA], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+
+  // ---- per-role setup: Q rows (softmax), R_K and the pair tables (decoders) --
+  const int nk = 1 << (2 * KB), nv = 1 << (2 * VB);
+  const uint32_t lut_k = sbase + OFF_LUT;
+  const uint32_t lut_v = lut_k + (uint32_t)(nk * p.rk * 4);
+  if (warp >= 1 && warp <= kSoftWarps) {
+    const int r = 32 * (warp & 3) + lane;
+    const int pl = r & (P - 1), hl = r >> p.pshift;
+    const int t = qb * P + pl;
+    const int64_t h = kvh * p.g + (int64_t)chunk * p.hc + hl;
+    const uint32_t qdst = sbase + OFF_Q;
+    if (t < p.Tq) {
+      const int64_t base = b * p.qs[0] + h * p.qs[1] + (int64_t)t * p.qs[2];
+      if (p.q_vec) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            reinterpret_cast<const uint16_t*>(p.q) + base);
+#pragma unroll 4
+        for (int c = 0; c < 16; ++c)
+          sts128(qdst + sw_chunk(r, c), scale_chunk(__ldg(src + c), p.q_dtype, p.qscale));
+      } else {
+        for (int c = 0; c < 16; ++c) {
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int64_t i = base + (int64_t)(8 * c + 2 * e) * p.qs[3];
+            o[e] = pack_half2(load_elem(p.q, p.q_dtype, i) * p.qscale,
+                              load_elem(p.q, p.q_dtype, i + p.qs[3]) * p.qscale);
+          }
+          sts128(qdst + sw_chunk(r, c), make_uint4(o[0], o[1], o[2], o[3]));
+        }
+      }
+    } else {
+      for (int c = 0; c < 16; ++c) sts128(qdst + sw_chunk(r, c), make_uint4(0, 0, 0, 0));
+    }
+  } else if (warp > kSoftWarps) {
+    const int dt = tid - 32 * (1 + kSoftWarps);
+    // R_K (K-major B of q' = Q R_K^T): row i = R[k_coord(i)] -> V stage 0
+    for (int it = dt; it < kD * 16; it += kDecThreads) {
+      const int i = it >> 4, c = it & 15;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.rot_h + k_coord(i) * kD) + c);
+      sts128(sbase + OFF_V + sw_chunk(i, c), v);
+    }
+    for (int it = dt; it < nk * p.rk; it += kDecThreads) {
+      const int idx = it / p.rk;
+      const uint32_t v = pack_half2(__ldg(p.kc + (idx & ((1 << KB) - 1))), __ldg(p.kc + (idx >> KB)));
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(lut_k + 4u * it), "r"(v) : "memory");
+    }
+    for (int it = dt; it < nv * p.rv; it += kDecThreads) {
+      const int idx = it / p.rv;
+      const uint32_t v = pack_half2(__ldg(p.vc + (idx & ((1 << VB) - 1))), __ldg(p.vc + (idx >> VB)));
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(lut_v + 4u * it), "r"(v) : "memory");
+    }
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  constexpr uint32_t idesc_kk = tc::idesc_f16_f32(kRows, 128);            // A, B K-major
+  constexpr uint32_t idesc_kmn = tc::idesc_f16_f32(kRows, 128) | (1u << 16);   // B MN-major
+
+  if (warp == 0) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      // q' = Q R_K^T into columns 0..127
+#pragma unroll
+      for (int st = 0; st < 8; ++st) {
+        const uint32_t off = (uint32_t)((st >> 2) * kHalfBytes + (st & 3) * 32);
+        umma_ss(tmem, tc::sdesc_kmajor_sw128(sbase + OFF_Q + off),
+                      tc::sdesc_kmajor_sw128(sbase + OFF_V + off), idesc_kk, st ? 1u : 0u);
+      }
+      tc::umma_commit(&bars[B_ROT]);
+      ok = wait_or_abort(&bars[B_QP], 0u, abort_flag, p.status);
+      tc::tc_fence_after();
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!wait_or_abort(&bars[B_KFULL + s], (uint32_t)((j >> 1) & 1), abort_flag, p.status))
+          return false;
+        tc::tc_fence_after();
+        const uint32_t kbase = sbase + OFF_K + s * kStage;
+#pragma unroll
+        for (int st = 0; st < 8; ++st) {
+          const uint32_t off = (uint32_t)((st >> 2) * kHalfBytes + (st & 3) * 32);
+          umma_ss(tmem + s * 128, tc::sdesc_kmajor_sw128(sbase + OFF_Q + off),
+                        tc::sdesc_kmajor_sw128(kbase + off), idesc_kk, st ? 1u : 0u);
+        }
+        tc::umma_commit(&bars[B_KEMPTY + s]);
+        tc::umma_commit(&bars[B_SFULL + s]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int s = j & 1;
+        const uint32_t par = (uint32_t)((j >> 1) & 1);
+        if (!wait_or_abort(&bars[B_PFULL + s], par, abort_flag, p.status) ||
+            !wait_or_abort(&bars[B_VFULL + s], par, abort_flag, p.status))
+          return false;
+        tc::tc_fence_after();
+        const uint32_t vbase = sbase + OFF_V + s * kStage;
+#pragma unroll
+        for (int st = 0; st < 8; ++st)
+          umma_ts(tmem + kOCol, tmem + s * 128 + 8 * st,
+                  sdesc_mnmajor_sw128(vbase + st * 2048, kHalfBytes), idesc_kmn,
+                  (j | st) ? 1u : 0u);
+        tc::umma_commit(&bars[B_VEMPTY + s]);
+        tc::umma_commit(&bars[B_ODONE]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && ntiles > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        ok = issue_pv(j);
+        if (ok && j + 2 < ntiles) ok = issue_s(j + 2);
+      }
+      // OUT = O^ R_V into columns 0..127
+      if (ok && wait_or_abort(&bars[B_OFIN], 0u, abort_flag, p.status) &&
+          wait_or_abort(&bars[B_RV], 0u, abort_flag, p.status)) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int st = 0; st < 8; ++st) {
+          const uint32_t off = (uint32_t)((st >> 2) * kHalfBytes + (st & 3) * 32);
+          umma_ss(tmem, tc::sdesc_kmajor_sw128(sbase + OFF_Q + off),
+                        sdesc_mnmajor_sw128(sbase + OFF_K + st * 2048, kHalfBytes), idesc_kmn,
+                        st ? 1u : 0u);
+        }
+        tc::umma_commit(&bars[B_OUT]);
+      }
+      // never leave with an MMA in flight
+      tc::umma_commit(&bars[B_MMA]);
+      mbar_wait_bounded(&bars[B_MMA], 0u, 16u);
+    }
+    __syncwarp();
+  } else if (warp <= kSoftWarps) {
+    // ================================================================ softmax
+    const int quarter = warp & 3;
+    const int r = 32 * quarter + lane;
+    const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);
+    const int pl = r & (P - 1), hl = r >> p.pshift;
+    const int t = qb * P + pl;
+    const bool valid = t < p.Tq;
+    const int64_t qpos = valid ? t_base + t : qpos_max;
+    const int64_t lim = p.causal ? qpos : p.n_tokens - 1;    // keys <= lim are seen
+    bool ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status));
+    if (ok) {
+      // q' (fp32, K order) -> fp16 A operand over Q
+      tc::tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t x[32];
+        tc::tmem_ld_x32(tl + 32 * c, x);
+        tmem_ld_wait(x);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t h[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            h[e] = pack_half2(__uint_as_float(x[8 * q + 2 * e]), __uint_as_float(x[8 * q + 2 * e + 1]));
+          sts128(sbase + OFF_Q + sw_chunk(r, 4 * c + q), make_uint4(h[0], h[1], h[2], h[3]));
+        }
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cta(&bars[B_QP]);
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; ok && j < ntiles; ++j) {
+      const int s = j & 1;
+      ok = __all_sync(0xffffffffu,
+                      wait_or_abort(&bars[B_SFULL + s], (uint32_t)((j >> 1) & 1), abort_flag,
+                                    p.status));
+      if (!ok) break;
+      tc::tc_fence_after();
+      const int64_t k0 = (int64_t)j * kKeys;
+      const bool need_mask = k0 + kKeys - 1 > lim;
+      const uint32_t scol = tl + s * 128;
+      // pass 1: row max
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t x[32];
+        tc::tmem_ld_x32(scol + 32 * c, x);
+        tmem_ld_wait(x);
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (k0 + 32 * c + e <= lim) mx = fmaxf(mx, __uint_as_float(x[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(x[e]));
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      const bool resc = m != -INFINITY && m_new > m + kRescaleBits;
+      const float f = resc ? fast_exp2(m - m_new) : 1.f;
+      if (m == -INFINITY || resc) m = m_new;
+      const float bias = m == -INFINITY ? 0.f : m;
+      // pass 2: P = exp2(S - m) as fp16 over the S columns
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t x[32];
+        tc::tmem_ld_x32(scol + 32 * c, x);
+        tmem_ld_wait(x);
+        uint32_t h[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int64_t key = k0 + 32 * c + 2 * e;
+          float p0 = fast_exp2(__uint_as_float(x[2 * e]) - bias);
+          float p1 = fast_exp2(__uint_as_float(x[2 * e + 1]) - bias);
+          if (need_mask) {
+            p0 = key <= lim ? p0 : 0.f;
+            p1 = key + 1 <= lim ? p1 : 0.f;
+          }
+          sum += p0 + p1;
+          h[e] = pack_half2(p0, p1);
+        }
+        tmem_st_x16(scol + 16 * c, h);
+      }
+      l = l * f + sum;
+      // O += P V^ of the previous tile must be complete before O is rescaled
+      // (and the phase is consumed on every tile, so parities never alias)
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu,
+                        wait_or_abort(&bars[B_ODONE], (uint32_t)((j - 1) & 1), abort_flag,
+                                      p.status));
+        if (ok && __any_sync(0xffffffffu, resc)) {
+          tc::tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t x[32];
+            tc::tmem_ld_x32(tl + kOCol + 32 * c, x);
+            tmem_ld_wait(x);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) x[e] = __float_as_uint(__uint_as_float(x[e]) * f);
+            tc::tmem_st_x32(tl + kOCol + 32 * c, x);
+          }
+        }
+      }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (ok && lane == 0) tc::mbar_arrive_cta(&bars[B_PFULL + s]);
+    }
+    // O^ = O / l (V order) -> fp16 A operand over q'
+    if (ok)
+      ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_ODONE], (uint32_t)((ntiles - 1) & 1),
+                                                 abort_flag, p.status));
+    if (ok) {
+      tc::tc_fence_after();
+      const float il = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t x[32];
+        tc::tmem_ld_x32(tl + kOCol + 32 * c, x);
+        tmem_ld_wait(x);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t h[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            h[e] = pack_half2(__uint_as_float(x[8 * q + 2 * e]) * il,
+                              __uint_as_float(x[8 * q + 2 * e + 1]) * il);
+          sts128(sbase + OFF_Q + sw_chunk(r, 4 * c + q), make_uint4(h[0], h[1], h[2], h[3]));
+        }
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cta(&bars[B_OFIN]);
+      ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_OUT], 0u, abort_flag, p.status));
+    }
+    if (ok) {
+      tc::tc_fence_after();
+      const int64_t h = kvh * p.g + (int64_t)chunk * p.hc + hl;
+      const int64_t base = b * p.os[0] + h * p.os[1] + (int64_t)t * p.os[2];
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t x[32];
+        tc::tmem_ld_x32(tl + 32 * c, x);
+        tmem_ld_wait(x);
+        if (!valid) continue;
+        if (p.o_vec) {
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + base) + 4 * c;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float lo = __uint_as_float(x[8 * q + 2 * e]);
+              const float hi = __uint_as_float(x[8 * q + 2 * e + 1]);
+              if (p.o_dtype == TQ_F16) {
+                h[e] = pack_half2(lo, hi);
+              } else {
+                __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+                h[e] = *reinterpret_cast<uint32_t*>(&v);
+              }
+            }
+            dst[q] = make_uint4(h[0], h[1], h[2], h[3]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            store_elem(p.out, p.o_dtype, base + (int64_t)(32 * c + e) * p.os[3],
+                       __uint_as_float(x[e]));
+        }
+      }
+    }
+  } else {
+    // ================================================================ decoders
+    const int dt = tid - 32 * (1 + kSoftWarps);
+    TcParamsView pv;
+    pv.spages = p.pages + stream * p.pages_per_stream * (int64_t)p.page_bytes;
+    pv.page_bytes = p.page_bytes;
+    pv.off_v = p.off_v;
+    pv.off_kn = p.off_kn;
+    pv.off_vn = p.off_vn;
+    pv.kk = dt >> 2;
+    pv.part = dt & 3;
+    pv.kend = kend;
+    const uint32_t lk = lut_k + 4u * (uint32_t)(lane & (p.rk - 1));
+    const uint32_t lv = lut_v + 4u * (uint32_t)(lane & (p.rv - 1));
+    const uint32_t rk4 = 4u * (uint32_t)p.rk, rv4 = 4u * (uint32_t)p.rv;
+    TileRegs<KB, VB> cur, nxt;
+    load_tile<KB, VB>(cur, pv, 0);
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j & 1;
+      if (j + 1 < ntiles) load_tile<KB, VB>(nxt, pv, j + 1);
+      // K^ tile: the S MMA of tile j - 2 has read this stage
+      if (j >= 2)
+        ok = wait_or_abort(&bars[B_KEMPTY + s], (uint32_t)(((j >> 1) - 1) & 1), abort_flag,
+                           p.status);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const uint32_t kb = sbase + OFF_K + s * kStage;
+#pragma unroll
+      for (int pg = 0; pg < 2; ++pg) {
+        const uint32_t nk2 = (cur.nrm[pg] & 0xFFFFu) * 0x10001u;
+        decode_stream<KB>(cur.k[pg], lk, rk4, *reinterpret_cast<const __half2*>(&nk2), kb,
+                          pg * 64 + pv.kk, 4 * pv.part);
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL + s]);
+      // V^ tile: the PV MMA of tile j - 2 (or, for tile 0, q' = Q R_K^T, whose
+      // R_K sits in V stage 0) has read this stage
+      if (j >= 2)
+        ok = wait_or_abort(&bars[B_VEMPTY + s], (uint32_t)(((j >> 1) - 1) & 1), abort_flag,
+                           p.status);
+      else if (j == 0)
+        ok = wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const uint32_t vb = sbase + OFF_V + s * kStage;
+#pragma unroll
+      for (int pg = 0; pg < 2; ++pg) {
+        const uint32_t vn2 = (cur.nrm[pg] >> 16) * 0x10001u;
+        decode_stream<VB>(cur.v[pg], lv, rv4, *reinterpret_cast<const __half2*>(&vn2), vb,
+                          pg * 64 + pv.kk, 4 * pv.part);
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cta(&bars[B_VFULL + s]);
+      cur = nxt;
+    }
+    // R_V (MN-major B of OUT = O^ R_V): row i = R[v_coord(i)] -> K stage 0,
+    // once the last S MMA that reads K stage 0 is complete
+    if (ok) {
+      const int jl = (ntiles - 1) & ~1;                   // last tile in stage 0
+      ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_KEMPTY], (uint32_t)((jl >> 1) & 1),
+                                                 abort_flag, p.status));
+    }
+    if (ok) {
+      for (int it = dt; it < kD * 16; it += kDecThreads) {
+        const int i = it >> 4, c = it & 15;
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.rot_h + v_coord(i) * kD) + c);
+        sts128(sbase + OFF_K + sw_chunk(i, c), v);
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cta(&bars[B_RV]);
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+using TcFn = void (*)(TcPrefillParams);
+
+TcFn tc_fn(int kb, int vb) {
+#define TQ_PTC(K, V) if (kb == K && vb == V) return prefill_tc_kernel<K, V>;
+  TQ_PTC(4, 2) TQ_PTC(4, 4) TQ_PTC(3, 3) TQ_PTC(2, 2) TQ_PTC(3, 2) TQ_PTC(4, 3)
+  TQ_PTC(2, 4) TQ_PTC(3, 4) TQ_PTC(2, 3)
+#undef TQ_PTC
+  return nullptr;
+}
+
+bool vec_ok(const tq_tensor4* x) {
+  if (x->dtype != TQ_BF16 && x->dtype != TQ_F16) return false;
+  if (x->stride[3] != 1 || reinterpret_cast<uintptr_t>(x->data) % 16) return false;
+  for (int i = 0; i < 3; ++i)
+    if (x->stride[i] % 8) return false;
+  return true;
+}
+
+}  // namespace
+
+bool prefill_tc_applies(const tq_geom* G) {
+  return G->head_dim == kD && tc_fn(G->key_bits, G->value_bits) != nullptr;
+}
+
+int launch_prefill_tc(const tq_geom* G, const tq_tables* t, const tq_cache* c,
+                      const tq_prefill_args* a, uint32_t* status, cudaStream_t st) {
+  if (!prefill_tc_applies(G)) return 1;
+  TcFn fn = tc_fn(G->key_bits, G->value_bits);
+  const PageGeom g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
+  TcPrefillParams p;
+  p.pages = c->pages;
+  p.pages_per_stream = c->pages_per_stream;
+  p.page_bytes = g.page_bytes;
+  p.off_v = g.off_v;
+  p.off_kn = g.off_kn;
+  p.off_vn = g.off_vn;
+  p.rot_h = reinterpret_cast<const __half*>(t->rot_f16);
+  p.kc = t->k_centroids;
+  p.vc = t->v_centroids;
+  p.q = a->q->data; p.q_dtype = a->q->dtype; p.q_vec = vec_ok(a->q);
+  p.out = a->out->data; p.o_dtype = a->out->dtype; p.o_vec = vec_ok(a->out);
+  for (int i = 0; i < 4; ++i) { p.qs[i] = a->q->stride[i]; p.os[i] = a->out->stride[i]; }
+  const int64_t B = a->q->shape[0], Hq = a->q->shape[1];
+  p.Hkv = c->streams / B;
+  p.g = Hq / p.Hkv;
+  p.hc = p.g % 8 == 0 ? 8 : p.g % 4 == 0 ? 4 : p.g % 2 == 0 ? 2 : 1;
+  const int P = kRows / p.hc;
+  p.pshift = 0;
+  while ((1 << p.pshift) < P) ++p.pshift;
+  p.Tq = a->q->shape[2];
+  p.n_tokens = a->n_tokens;
+  p.nqb = (int)((p.Tq + P - 1) / P);
+  p.qscale = a->scale * kLog2e;
+  p.causal = a->causal;
+  // pair tables: 32 copies (one per lane) where they fit, else 16 / 8
+  const int nk = 1 << (2 * G->key_bits), nv = 1 << (2 * G->value_bits);
+  int rk = 32, rv = 32;
+  while ((nk * rk + nv * rv) * 4 > (int)kLutMax) {
+    if (nk * rk >= nv * rv) rk >>= 1; else rv >>= 1;
+  }
+  p.rk = rk;
+  p.rv = rv;
+  p.status = status;
+  if (p.Tq == 0) return TQ_OK;
+  if (set_smem_attr((const void*)fn, SMEM_BYTES) != TQ_OK) return TQ_ERR_CUDA;
+  dim3 grid((unsigned)p.nqb, (unsigned)(B * Hq / p.hc));
+  fn<<<grid, kThreads, SMEM_BYTES, st>>>(p);
+  return check_launch("tq_prefill_attn");
+}
+
+}  // namespace tq

@@ -262,12 +262,20 @@ def decode_step(tables: LayerTables, pages: torch.Tensor, k_new: torch.Tensor,
     return out
 
 
+def prefill_uses_tensor_cores(tables: LayerTables) -> bool:
+    """Whether prefill_attention (engine 0) runs the tcgen05 kernel for this
+    layer's geometry."""
+    return bool(_lib.load().tq_prefill_tensor_core(ctypes.byref(tables.geom())))
+
+
 def prefill_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
                       n_tokens: int, scale: Optional[float] = None, causal: bool = True,
-                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      out: Optional[torch.Tensor] = None, engine: int = 0) -> torch.Tensor:
     """Attention of queries q (B, Hq, Tq, D) at positions n_tokens - Tq ..
     n_tokens - 1 over the packed tokens [0, n_tokens) of every stream (causal:
-    a query sees keys at or before its position)."""
+    a query sees keys at or before its position).  ``engine`` 0 picks the
+    fastest kernel (tcgen05 where prefill_uses_tensor_cores), 1 the mma.sync
+    kernel."""
     _require_cuda(pages, q)
     lib = _lib.load()
     if out is None:
@@ -276,7 +284,7 @@ def prefill_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
     qt, ot = tensor4(q), tensor4(out)
     a = _lib.PrefillArgs(ctypes.pointer(qt), ctypes.pointer(ot), int(n_tokens),
                          float(scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])),
-                         1 if causal else 0)
+                         1 if causal else 0, int(engine))
     _lib.check("tq_prefill_attn", lib.tq_prefill_attn(
         ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(a), _stream(q.device)))
     return out

@@ -191,10 +191,17 @@ typedef struct tq_prefill_args {
   int64_t n_tokens;            /* tokens per stream, the Tq new ones included */
   float scale;                 /* softmax scale                               */
   int32_t causal;              /* 1: causal; 0: every query sees all tokens   */
+  int32_t engine;              /* 0: the fastest kernel for the shape (tcgen05
+                                  tensor cores where tq_prefill_tensor_core
+                                  says so); 1: the mma.sync kernel             */
 } tq_prefill_args;
 
 int32_t tq_prefill_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                         const tq_prefill_args* a, void* stream);
+
+/* 1 when tq_prefill_attn with engine 0 runs on the tcgen05 tensor cores for
+ * this geometry (head_dim 128, key and value codes of 2 to 4 bits), else 0. */
+int32_t tq_prefill_tensor_core(const tq_geom* g);
 
 /* tq_decode_attn for callers that cannot allocate device memory (a runtime
  * that owns all device memory through its own pool, or code that must not

@@ -47,21 +47,71 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("engine", [0, 1])
 @pytest.mark.parametrize("D,kb,vb,qjl,B,Hkv,g,n,Tq,causal", CASES)
-def test_prefill_matches_oracle(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal):
+def test_prefill_matches_oracle(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, engine):
+    _run_case(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, engine)
+
+
+def _run_case(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, engine, q_dtype=torch.bfloat16,
+              transpose_q=False, key_growth=0.0):
     t = make_tables(D, kb, vb, qjl)
     k = rand_kv((B, Hkv, n, D), 21)
+    if key_growth:
+        k = (k.float() * (1.0 + key_growth * torch.arange(n).view(1, 1, n, 1))).bfloat16()
     v = rand_kv((B, Hkv, n, D), 22)
     q = rand_kv((B, Hkv * g, Tq, D), 23)
     pages = new_pages(B * Hkv, n, t)
     ops.append(t, pages, k.to(DEV), v.to(DEV), 0)
-    out = ops.prefill_attention(t, pages, q.to(DEV), n, causal=causal)
+    qd = q.to(DEV, q_dtype)
+    if transpose_q:            # (B, Tq, Hq, D) storage seen as (B, Hq, Tq, D)
+        qd = qd.transpose(1, 2).contiguous().transpose(1, 2)
+    out = ops.prefill_attention(t, pages, qd, n, causal=causal, engine=engine)
     torch.cuda.synchronize()
     assert ops.device_status(DEV) == 0
     kd, vd = _dequant(t, pages, n)
-    want = O.sdpa(q.float().numpy(), kd.reshape(B, Hkv, n, D), vd.reshape(B, Hkv, n, D),
-                  causal=causal)
+    want = O.sdpa(qd.float().cpu().numpy(), kd.reshape(B, Hkv, n, D),
+                  vd.reshape(B, Hkv, n, D), causal=causal)
     _check(out, want)
+
+
+TC_CASES = [
+    # D, kb, vb, qjl, B, Hkv, g, n_tokens, Tq, causal
+    (128, 4, 2, True, 1, 2, 4, 1000, 1000, True),    # 8 key tiles, odd page count
+    (128, 2, 2, False, 1, 1, 1, 700, 300, True),     # MHA: 128 positions per CTA, chunk 400..699
+    (128, 3, 4, False, 1, 1, 8, 390, 390, False),    # group 8: 16 positions per CTA, non-causal
+    (128, 4, 3, False, 2, 1, 2, 129, 5, True),       # 5 queries, one key on the third page
+    (128, 2, 4, False, 1, 2, 3, 256, 256, True),     # group 3: one head per CTA
+    (128, 3, 2, False, 1, 1, 4, 64, 1, True),        # a single query
+]
+
+
+@pytest.mark.parametrize("D,kb,vb,qjl,B,Hkv,g,n,Tq,causal", TC_CASES)
+def test_tensor_core_prefill_matches_oracle(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal):
+    assert ops.prefill_uses_tensor_cores(make_tables(D, kb, vb, qjl))
+    _run_case(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, 0)
+
+
+@pytest.mark.parametrize("q_dtype,transpose_q", [(torch.float16, False), (torch.bfloat16, True),
+                                                 (torch.float32, False)])
+def test_tensor_core_prefill_query_layouts(q_dtype, transpose_q):
+    _run_case(128, 4, 2, False, 1, 2, 4, 300, 300, True, 0, q_dtype=q_dtype,
+              transpose_q=transpose_q)
+
+
+@pytest.mark.parametrize("engine", [0, 1])
+def test_prefill_growing_scores(engine):
+    """Key norms growing 5x along the sequence lift the running max by more
+    than 8 (log2 units) over the tiles, so the tcgen05 kernel rescales its
+    output accumulator in tensor memory (scores stay within the range where
+    fp16 operands keep the 4e-3 bar)."""
+    _run_case(128, 4, 4, False, 1, 1, 4, 900, 900, True, engine, key_growth=0.005)
+
+
+def test_tensor_core_coverage():
+    assert not ops.prefill_uses_tensor_cores(make_tables(64, 4, 2, False))
+    assert not ops.prefill_uses_tensor_cores(make_tables(128, 6, 4, False))
+    assert ops.prefill_uses_tensor_cores(make_tables(128, 4, 2, True))
 
 
 def test_prefill_last_row_equals_decode():
