@@ -153,6 +153,27 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
   return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for a hot hand-off: polls try_wait without a suspend-time hint
+// (a hinted wait resumes about 0.1 us after the phase completes) and gives up
+// after about 2 s.
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u) {
+      const uint64_t t = global_ns();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > 2000000000ull) return false;
+    }
+  }
+}
+
 // Bounded wait: returns false (and never hangs) if the phase does not
 // complete within `limit` suspended polls of at most 1 ms each.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,

@@ -306,7 +306,7 @@ decode_kernel(DecodeParams p) {
       for (int i = gr, k = 0; i < npages; i += G::NG, ++k) {
         const int st = gr * G::SG + k % G::SG;
         if (k >= G::SG && !s_abort) {
-          if (!mbar_wait_bounded(&empty[st], (uint32_t)(((k / G::SG) - 1) & 1))) {
+          if (!mbar_wait_poll(&empty[st], (uint32_t)(((k / G::SG) - 1) & 1))) {
             atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
             s_abort = 1;
           }
@@ -371,7 +371,7 @@ decode_kernel(DecodeParams p) {
     for (; inext < i1; inext += G::NG) {
       const int st = grp * G::SG + ring;
       const int pg = pg0 + (inext - i0);
-      if (!s_abort && !mbar_wait_bounded(&full[st], phase)) {
+      if (!s_abort && !mbar_wait_poll(&full[st], phase)) {
         atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
         s_abort = 1;
       }

@@ -28,10 +28,15 @@
 //               swizzled layout, through pair tables (two codes -> one half2)
 //               replicated across lanes; codes are read from the pages in
 //               global memory with one tile of register prefetch
-// Tensor memory, 512 columns: S/P double buffer at 0 and 128, O at 256.
-// Shared memory: q' (later O^) 32 KB, two K^ and two V^ stages of 32 KB, the
-// pair tables.  R_K is staged in V stage 0 before the first tile and R_V in
-// K stage 0 after the last.
+// Tensor memory, 512 columns: S/P double buffer at 0 and 128, O at 256, at
+// 384 the row sums l = P x ones (an N = 16 MMA beside each PV MMA, so l is
+// the sum of the fp16 P the PV MMA used and is rescaled with O), and at 416
+// q' as fp16 pairs: both S and PV MMAs take A from tensor memory and read
+// only their B tiles from shared memory.
+// Shared memory: Q (later O^) 32 KB, two K^ and two V^ stages of 32 KB, the
+// pair tables.  R_K is staged in V stage 0 before the first tile; after the
+// last, R_V (fp16 hi and lo terms) takes both K stages and the lo term of O^
+// V stage 0, so the output rotation carries no fp16 rounding of O^ or R.
 //
 // K^ (K-major B of S = q' K^^T) and V^ (MN-major B of O = P V^) share one
 // physical layout: [64-column half][128 keys][128 B], 16-byte chunks swizzled
@@ -60,6 +65,8 @@ constexpr int kThreads = 32 * kWarps;      // 416
 constexpr int kDecThreads = 32 * kDecWarps;
 constexpr int kTmemCols = 512;
 constexpr int kOCol = 256;                 // O accumulator columns
+constexpr int kLCol = 384;                 // row sums of P (16 equal columns)
+constexpr int kQCol = 416;                 // q' as fp16 pairs (64 columns): A of S = q' K^^T
 constexpr float kRescaleBits = 8.f;        // lazy rescale threshold (log2)
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -70,12 +77,14 @@ constexpr uint32_t OFF_K = OFF_Q + kStage;
 constexpr uint32_t OFF_V = OFF_K + 2 * kStage;
 constexpr uint32_t OFF_LUT = OFF_V + 2 * kStage;
 constexpr uint32_t kLutMax = 36864;
-constexpr uint32_t OFF_BAR = OFF_LUT + kLutMax;
+constexpr uint32_t OFF_ONES = OFF_LUT + kLutMax;   // [2][16 rows][128 B] of fp16 1.0
+constexpr uint32_t OFF_BAR = OFF_ONES + 4096;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;   // + alignment slack
 
 enum Bar {
   B_ROT = 0, B_QP = 1, B_KFULL = 2, B_KEMPTY = 4, B_VFULL = 6, B_VEMPTY = 8, B_SFULL = 10,
-  B_PFULL = 12, B_ODONE = 14, B_OFIN = 15, B_RV = 16, B_OUT = 17, B_MMA = 18, B_COUNT = 19
+  B_PFULL = 12, B_ODONE = 14, B_OFIN = 15, B_RV = 16, B_OUT = 17, B_MMA = 18, B_PREV = 19,
+  B_COUNT = 20
 };
 
 struct TcPrefillParams {
@@ -83,6 +92,7 @@ struct TcPrefillParams {
   int64_t pages_per_stream;
   int page_bytes, off_v, off_kn, off_vn;
   const __half* rot_h;          // R [128][128] fp16, row-major
+  const float* rot;             // R [128][128] fp32, row-major
   const float* kc;
   const float* vc;
   const void* q; int q_dtype; int q_vec; int64_t qs[4];
@@ -138,6 +148,40 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
       :: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Scores of keys past `last` (an index into this 32-key chunk) -> -inf.
+__device__ __forceinline__ void mask_keys(uint32_t (&x)[32], int64_t last) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e)
+    if (e > last) x[e] = 0xFF800000u;
+}
+
+// fp16 pair {exp2(a - bias), exp2(b - bias)} (a in the low half): the
+// differences rounded to fp16 (|a - bias| < 2^4 carries an error below 2^-7
+// in the exponent only for p < 2^-4), then one SFU op for both exponentials.
+__device__ __forceinline__ uint32_t exp2_pair(uint32_t a, uint32_t b, float bias) {
+  uint32_t h, p;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;"
+      : "=r"(h) : "f"(__uint_as_float(b) - bias), "f"(__uint_as_float(a) - bias));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(p) : "r"(h));
+  return p;
+}
+
 __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -171,12 +215,20 @@ __device__ __forceinline__ void fail(uint32_t* status, volatile int* abort_flag)
   atomicOr(status, TQ_DEV_WAIT_TIMEOUT);
 }
 
-// Bounded wait that also gives up as soon as another role has aborted.
+// Bounded wait (2 s) that also gives up as soon as another role has aborted.
+// try_wait without a suspend-time hint: a hinted wait wakes about 0.1 us
+// late, which costs more than the polling on this kernel's per-tile handoffs.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
                                               volatile int* abort_flag, uint32_t* status) {
-  for (uint32_t i = 0; i < 1000u; ++i) {
-    if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
-    if (*abort_flag) return false;
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u) {
+      if (*abort_flag) return false;
+      const uint64_t t = global_ns();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > 2000000000ull) break;
+    }
   }
   fail(status, abort_flag);
   return false;
@@ -320,6 +372,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
       mbar_init(&bars[B_PFULL + s], kSoftWarps);
     }
     mbar_init(&bars[B_ODONE], 1);
+    mbar_init(&bars[B_PREV], 1);
     mbar_init(&bars[B_OFIN], kSoftWarps);
     mbar_init(&bars[B_RV], kDecWarps);
     mbar_init(&bars[B_OUT], 1);
@@ -337,51 +390,74 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
   const uint32_t lut_k = sbase + OFF_LUT;
   const uint32_t lut_v = lut_k + (uint32_t)(nk * p.rk * 4);
   if (warp >= 1 && warp <= kSoftWarps) {
-    const int r = 32 * (warp & 3) + lane;
-    const int pl = r & (P - 1), hl = r >> p.pshift;
-    const int t = qb * P + pl;
-    const int64_t h = kvh * p.g + (int64_t)chunk * p.hc + hl;
+    // this warp's 32 rows, two rows per pass: 16 lanes x 16 bytes of a row
     const uint32_t qdst = sbase + OFF_Q;
-    if (t < p.Tq) {
-      const int64_t base = b * p.qs[0] + h * p.qs[1] + (int64_t)t * p.qs[2];
-      if (p.q_vec) {
-        const uint4* src = reinterpret_cast<const uint4*>(
-            reinterpret_cast<const uint16_t*>(p.q) + base);
-#pragma unroll 4
-        for (int c = 0; c < 16; ++c)
-          sts128(qdst + sw_chunk(r, c), scale_chunk(__ldg(src + c), p.q_dtype, p.qscale));
-      } else {
-        for (int c = 0; c < 16; ++c) {
-          uint32_t o[4];
+    const int half = lane >> 4, c = lane & 15;
+    if (p.q_vec) {
+      uint4 raw[16];                            // every load in flight at once
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const int r = 32 * (warp & 3) + 2 * m + half;
+        const int t = qb * P + (r & (P - 1));
+        const int64_t h = kvh * p.g + (int64_t)chunk * p.hc + (r >> p.pshift);
+        raw[m] = make_uint4(0, 0, 0, 0);
+        if (t < p.Tq)
+          raw[m] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.q) +
+                                                        b * p.qs[0] + h * p.qs[1] +
+                                                        (int64_t)t * p.qs[2]) + c);
+      }
+#pragma unroll
+      for (int m = 0; m < 16; ++m)
+        sts128(qdst + sw_chunk(32 * (warp & 3) + 2 * m + half, c),
+               scale_chunk(raw[m], p.q_dtype, p.qscale));
+    } else {
+      for (int m = 0; m < 16; ++m) {
+        const int r = 32 * (warp & 3) + 2 * m + half;
+        const int t = qb * P + (r & (P - 1));
+        const int64_t h = kvh * p.g + (int64_t)chunk * p.hc + (r >> p.pshift);
+        uint32_t o[4] = {0u, 0u, 0u, 0u};
+        if (t < p.Tq) {
+          const int64_t base = b * p.qs[0] + h * p.qs[1] + (int64_t)t * p.qs[2];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int64_t i = base + (int64_t)(8 * c + 2 * e) * p.qs[3];
             o[e] = pack_half2(load_elem(p.q, p.q_dtype, i) * p.qscale,
                               load_elem(p.q, p.q_dtype, i + p.qs[3]) * p.qscale);
           }
-          sts128(qdst + sw_chunk(r, c), make_uint4(o[0], o[1], o[2], o[3]));
         }
+        sts128(qdst + sw_chunk(r, c), make_uint4(o[0], o[1], o[2], o[3]));
       }
-    } else {
-      for (int c = 0; c < 16; ++c) sts128(qdst + sw_chunk(r, c), make_uint4(0, 0, 0, 0));
     }
   } else if (warp > kSoftWarps) {
     const int dt = tid - 32 * (1 + kSoftWarps);
+    if (dt < 256) sts128(sbase + OFF_ONES + 16u * dt, make_uint4(0x3C003C00u, 0x3C003C00u,
+                                                                 0x3C003C00u, 0x3C003C00u));
     // R_K (K-major B of q' = Q R_K^T): row i = R[k_coord(i)] -> V stage 0
-    for (int it = dt; it < kD * 16; it += kDecThreads) {
-      const int i = it >> 4, c = it & 15;
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.rot_h + k_coord(i) * kD) + c);
-      sts128(sbase + OFF_V + sw_chunk(i, c), v);
+    {
+      constexpr int kIt = kD * 16 / kDecThreads;      // 8 chunks per thread, all in flight
+      uint4 v[kIt];
+#pragma unroll
+      for (int m = 0; m < kIt; ++m) {
+        const int it = dt + m * kDecThreads, i = it >> 4, c = it & 15;
+        v[m] = __ldg(reinterpret_cast<const uint4*>(p.rot_h + k_coord(i) * kD) + c);
+      }
+#pragma unroll
+      for (int m = 0; m < kIt; ++m) {
+        const int it = dt + m * kDecThreads;
+        sts128(sbase + OFF_V + sw_chunk(it >> 4, it & 15), v[m]);
+      }
     }
-    for (int it = dt; it < nk * p.rk; it += kDecThreads) {
-      const int idx = it / p.rk;
-      const uint32_t v = pack_half2(__ldg(p.kc + (idx & ((1 << KB) - 1))), __ldg(p.kc + (idx >> KB)));
-      asm volatile("st.shared.u32 [%0], %1;" ::"r"(lut_k + 4u * it), "r"(v) : "memory");
+    // pair tables: one entry per thread, its rk (rv) copies written 16 bytes
+    // at a time (rk, rv >= 8 and nk, nv <= 256 = decoder threads)
+    if (dt < nk) {
+      const uint32_t v = pack_half2(__ldg(p.kc + (dt & ((1 << KB) - 1))), __ldg(p.kc + (dt >> KB)));
+      const uint4 v4 = make_uint4(v, v, v, v);
+      for (int c = 0; c < p.rk; c += 4) sts128(lut_k + 4u * (uint32_t)(dt * p.rk + c), v4);
     }
-    for (int it = dt; it < nv * p.rv; it += kDecThreads) {
-      const int idx = it / p.rv;
-      const uint32_t v = pack_half2(__ldg(p.vc + (idx & ((1 << VB) - 1))), __ldg(p.vc + (idx >> VB)));
-      asm volatile("st.shared.u32 [%0], %1;" ::"r"(lut_v + 4u * it), "r"(v) : "memory");
+    if (dt < nv) {
+      const uint32_t v = pack_half2(__ldg(p.vc + (dt & ((1 << VB) - 1))), __ldg(p.vc + (dt >> VB)));
+      const uint4 v4 = make_uint4(v, v, v, v);
+      for (int c = 0; c < p.rv; c += 4) sts128(lut_v + 4u * (uint32_t)(dt * p.rv + c), v4);
     }
   }
   tc::fence_proxy_async_smem();
@@ -392,6 +468,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
 
   constexpr uint32_t idesc_kk = tc::idesc_f16_f32(kRows, 128);            // A, B K-major
   constexpr uint32_t idesc_kmn = tc::idesc_f16_f32(kRows, 128) | (1u << 16);   // B MN-major
+  constexpr uint32_t idesc_l = tc::idesc_f16_f32(kRows, 16);                   // P x ones
 
   if (warp == 0) {
     // ================================================================ MMA issuer
@@ -416,8 +493,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
 #pragma unroll
         for (int st = 0; st < 8; ++st) {
           const uint32_t off = (uint32_t)((st >> 2) * kHalfBytes + (st & 3) * 32);
-          umma_ss(tmem + s * 128, tc::sdesc_kmajor_sw128(sbase + OFF_Q + off),
-                        tc::sdesc_kmajor_sw128(kbase + off), idesc_kk, st ? 1u : 0u);
+          umma_ts(tmem + s * 128, tmem + kQCol + 8 * st, tc::sdesc_kmajor_sw128(kbase + off),
+                  idesc_kk, st ? 1u : 0u);
         }
         tc::umma_commit(&bars[B_KEMPTY + s]);
         tc::umma_commit(&bars[B_SFULL + s]);
@@ -436,8 +513,14 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
           umma_ts(tmem + kOCol, tmem + s * 128 + 8 * st,
                   sdesc_mnmajor_sw128(vbase + st * 2048, kHalfBytes), idesc_kmn,
                   (j | st) ? 1u : 0u);
+#pragma unroll
+        for (int st = 0; st < 8; ++st)
+          umma_ts(tmem + kLCol, tmem + s * 128 + 8 * st,
+                  tc::sdesc_kmajor_sw128(sbase + OFF_ONES + (st >> 2) * 2048 + (st & 3) * 32),
+                  idesc_l, (j | st) ? 1u : 0u);
         tc::umma_commit(&bars[B_VEMPTY + s]);
-        tc::umma_commit(&bars[B_ODONE]);
+        if (j == ntiles - 2) tc::umma_commit(&bars[B_PREV]);
+        if (j == ntiles - 1) tc::umma_commit(&bars[B_ODONE]);
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -450,12 +533,18 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
       if (ok && wait_or_abort(&bars[B_OFIN], 0u, abort_flag, p.status) &&
           wait_or_abort(&bars[B_RV], 0u, abort_flag, p.status)) {
         tc::tc_fence_after();
+        // O^hi R_V,hi + O^lo R_V,hi + O^hi R_V,lo
 #pragma unroll
-        for (int st = 0; st < 8; ++st) {
-          const uint32_t off = (uint32_t)((st >> 2) * kHalfBytes + (st & 3) * 32);
-          umma_ss(tmem, tc::sdesc_kmajor_sw128(sbase + OFF_Q + off),
-                        sdesc_mnmajor_sw128(sbase + OFF_K + st * 2048, kHalfBytes), idesc_kmn,
-                        st ? 1u : 0u);
+        for (int term = 0; term < 3; ++term) {
+          const uint32_t abase = sbase + (term == 1 ? OFF_V : OFF_Q);
+          const uint32_t bbase = sbase + OFF_K + (term == 2 ? kStage : 0u);
+#pragma unroll
+          for (int st = 0; st < 8; ++st) {
+            const uint32_t off = (uint32_t)((st >> 2) * kHalfBytes + (st & 3) * 32);
+            umma_ss(tmem, tc::sdesc_kmajor_sw128(abase + off),
+                    sdesc_mnmajor_sw128(bbase + st * 2048, kHalfBytes), idesc_kmn,
+                    (term | st) ? 1u : 0u);
+          }
         }
         tc::umma_commit(&bars[B_OUT]);
       }
@@ -476,28 +565,29 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
     const int64_t lim = p.causal ? qpos : p.n_tokens - 1;    // keys <= lim are seen
     bool ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status));
     if (ok) {
-      // q' (fp32, K order) -> fp16 A operand over Q
+      // q' (fp32, K order) -> fp16 pairs in tensor memory (A of the S MMA)
       tc::tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t x[32];
-        tc::tmem_ld_x32(tl + 32 * c, x);
-        tmem_ld_wait(x);
+      for (int c = 0; c < 4; c += 2) {
+        uint32_t x0[32], x1[32];
+        tc::tmem_ld_x32(tl + 32 * c, x0);
+        tc::tmem_ld_x32(tl + 32 * c + 32, x1);
+        tmem_ld_wait(x0);
+        tmem_ld_wait(x1);
+        uint32_t h[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t h[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            h[e] = pack_half2(__uint_as_float(x[8 * q + 2 * e]), __uint_as_float(x[8 * q + 2 * e + 1]));
-          sts128(sbase + OFF_Q + sw_chunk(r, 4 * c + q), make_uint4(h[0], h[1], h[2], h[3]));
+        for (int e = 0; e < 16; ++e) {
+          h[e] = pack_half2(__uint_as_float(x0[2 * e]), __uint_as_float(x0[2 * e + 1]));
+          h[16 + e] = pack_half2(__uint_as_float(x1[2 * e]), __uint_as_float(x1[2 * e + 1]));
         }
+        tc::tmem_st_x32(tl + kQCol + 16 * c, h);
       }
-      tc::fence_proxy_async_smem();
+      tc::tmem_wait_st();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cta(&bars[B_QP]);
     }
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY;
     for (int j = 0; ok && j < ntiles; ++j) {
       const int s = j & 1;
       ok = __all_sync(0xffffffffu,
@@ -508,57 +598,74 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
       const int64_t k0 = (int64_t)j * kKeys;
       const bool need_mask = k0 + kKeys - 1 > lim;
       const uint32_t scol = tl + s * 128;
-      // pass 1: row max
-      float mx = -INFINITY;
+      // pass 1: row max (four independent 3-input chains)
+      float mx;
+      {
+        float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t x[32];
-        tc::tmem_ld_x32(scol + 32 * c, x);
-        tmem_ld_wait(x);
-        if (need_mask) {
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t x0[32], x1[32];
+          tc::tmem_ld_x32(scol + 64 * hh, x0);
+          tc::tmem_ld_x32(scol + 64 * hh + 32, x1);
+          tmem_ld_wait(x0);
+          tmem_ld_wait(x1);
+          if (need_mask) {
+            mask_keys(x0, lim - (k0 + 64 * hh));
+            mask_keys(x1, lim - (k0 + 64 * hh + 32));
+          }
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (k0 + 32 * c + e <= lim) mx = fmaxf(mx, __uint_as_float(x[e]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(x[e]));
+          for (int e = 0; e < 32; e += 8) {
+            a0 = fmax3(a0, __uint_as_float(x0[e]), __uint_as_float(x0[e + 1]));
+            a1 = fmax3(a1, __uint_as_float(x0[e + 2]), __uint_as_float(x0[e + 3]));
+            a2 = fmax3(a2, __uint_as_float(x0[e + 4]), __uint_as_float(x0[e + 5]));
+            a3 = fmax3(a3, __uint_as_float(x0[e + 6]), __uint_as_float(x0[e + 7]));
+            a0 = fmax3(a0, __uint_as_float(x1[e]), __uint_as_float(x1[e + 1]));
+            a1 = fmax3(a1, __uint_as_float(x1[e + 2]), __uint_as_float(x1[e + 3]));
+            a2 = fmax3(a2, __uint_as_float(x1[e + 4]), __uint_as_float(x1[e + 5]));
+            a3 = fmax3(a3, __uint_as_float(x1[e + 6]), __uint_as_float(x1[e + 7]));
+          }
         }
+        mx = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
       }
       const float m_new = fmaxf(m, mx);
       const bool resc = m != -INFINITY && m_new > m + kRescaleBits;
       const float f = resc ? fast_exp2(m - m_new) : 1.f;
       if (m == -INFINITY || resc) m = m_new;
       const float bias = m == -INFINITY ? 0.f : m;
-      // pass 2: P = exp2(S - m) as fp16 over the S columns
-      float sum = 0.f;
+      // pass 2: P = exp2(S - m) as fp16 pairs over the S columns (masked
+      // scores are -inf: p = 0); the row sum comes from the P x ones MMA
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t x[32];
-        tc::tmem_ld_x32(scol + 32 * c, x);
-        tmem_ld_wait(x);
-        uint32_t h[16];
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t x0[32], x1[32];
+        tc::tmem_ld_x32(scol + 64 * hh, x0);
+        tc::tmem_ld_x32(scol + 64 * hh + 32, x1);
+        tmem_ld_wait(x0);
+        tmem_ld_wait(x1);
+        if (need_mask) {
+          mask_keys(x0, lim - (k0 + 64 * hh));
+          mask_keys(x1, lim - (k0 + 64 * hh + 32));
+        }
+        uint32_t h[32];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const int64_t key = k0 + 32 * c + 2 * e;
-          float p0 = fast_exp2(__uint_as_float(x[2 * e]) - bias);
-          float p1 = fast_exp2(__uint_as_float(x[2 * e + 1]) - bias);
-          if (need_mask) {
-            p0 = key <= lim ? p0 : 0.f;
-            p1 = key + 1 <= lim ? p1 : 0.f;
-          }
-          sum += p0 + p1;
-          h[e] = pack_half2(p0, p1);
+          h[e] = exp2_pair(x0[2 * e], x0[2 * e + 1], bias);
+          h[16 + e] = exp2_pair(x1[2 * e], x1[2 * e + 1], bias);
         }
-        tmem_st_x16(scol + 16 * c, h);
+        tc::tmem_st_x32(scol + 32 * hh, h);
       }
-      l = l * f + sum;
-      // O += P V^ of the previous tile must be complete before O is rescaled
-      // (and the phase is consumed on every tile, so parities never alias)
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu,
-                        wait_or_abort(&bars[B_ODONE], (uint32_t)((j - 1) & 1), abort_flag,
-                                      p.status));
-        if (ok && __any_sync(0xffffffffu, resc)) {
+      // rescaling O needs O += P V^ of tile j - 1 complete.  Commits complete
+      // in issue order and S_{j+1} was issued after PV_{j-1}, so S_{j+1}
+      // complete (a phase this warp waits for next anyway; it cannot advance
+      // again before P_{j+1} exists) implies it; the last tile waits for the
+      // commit that follows PV_{j-1}.
+      if (j > 0 && __any_sync(0xffffffffu, resc)) {
+        if (j + 1 < ntiles)
+          ok = wait_or_abort(&bars[B_SFULL + ((j + 1) & 1)], (uint32_t)(((j + 1) >> 1) & 1),
+                             abort_flag, p.status);
+        else
+          ok = wait_or_abort(&bars[B_PREV], 0u, abort_flag, p.status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
           tc::tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
@@ -569,6 +676,14 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
             for (int e = 0; e < 32; ++e) x[e] = __float_as_uint(__uint_as_float(x[e]) * f);
             tc::tmem_st_x32(tl + kOCol + 32 * c, x);
           }
+          {
+            uint32_t x[32];
+            tmem_ld_x16(tl + kLCol, x);
+            tmem_ld_wait(x);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) x[e] = __float_as_uint(__uint_as_float(x[e]) * f);
+            tmem_st_x16(tl + kLCol, reinterpret_cast<const uint32_t(&)[16]>(x));
+          }
         }
       }
       tc::tmem_wait_st();
@@ -576,12 +691,19 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
       __syncwarp();
       if (ok && lane == 0) tc::mbar_arrive_cta(&bars[B_PFULL + s]);
     }
-    // O^ = O / l (V order) -> fp16 A operand over q'
+    // O^ = O / l (V order) -> fp16 hi (over q') + lo (V stage 0; every PV MMA
+    // is complete) A operands
     if (ok)
-      ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_ODONE], (uint32_t)((ntiles - 1) & 1),
-                                                 abort_flag, p.status));
+      ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_ODONE], 0u, abort_flag, p.status));
     if (ok) {
       tc::tc_fence_after();
+      float l;
+      {
+        uint32_t x[32];
+        tmem_ld_x16(tl + kLCol, x);
+        tmem_ld_wait(x);
+        l = __uint_as_float(x[0]);
+      }
       const float il = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -590,12 +712,17 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
         tmem_ld_wait(x);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint32_t h[4];
+          uint32_t h[4], lo[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            h[e] = pack_half2(__uint_as_float(x[8 * q + 2 * e]) * il,
-                              __uint_as_float(x[8 * q + 2 * e + 1]) * il);
+          for (int e = 0; e < 4; ++e) {
+            const float a = __uint_as_float(x[8 * q + 2 * e]) * il;
+            const float b = __uint_as_float(x[8 * q + 2 * e + 1]) * il;
+            h[e] = pack_half2(a, b);
+            const __half2 hh = *reinterpret_cast<const __half2*>(&h[e]);
+            lo[e] = pack_half2(a - __low2float(hh), b - __high2float(hh));
+          }
           sts128(sbase + OFF_Q + sw_chunk(r, 4 * c + q), make_uint4(h[0], h[1], h[2], h[3]));
+          sts128(sbase + OFF_V + sw_chunk(r, 4 * c + q), make_uint4(lo[0], lo[1], lo[2], lo[3]));
         }
       }
       tc::fence_proxy_async_smem();
@@ -649,8 +776,16 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
     pv.off_v = p.off_v;
     pv.off_kn = p.off_kn;
     pv.off_vn = p.off_vn;
-    pv.kk = dt >> 2;
-    pv.part = dt & 3;
+    // lane -> (key, part): a warp covers 8 keys x 4 parts (512 contiguous
+    // code bytes per load); within each 8-lane group of a 16-byte store the
+    // 8 lanes hit 8 distinct 16-byte slots of the swizzled rows (parts 0 and
+    // 2 of one key would share a slot in the two 64-column halves)
+    {
+      const int G = lane >> 3, u = lane & 7, part = u & 3;
+      const int klo = ((u >> 2) ^ ((((part >> 1) ^ G) & 1) << 1)) | ((G >> 1) << 2);
+      pv.kk = 8 * (dt >> 5) + klo;
+      pv.part = part;
+    }
     pv.kend = kend;
     const uint32_t lk = lut_k + 4u * (uint32_t)(lane & (p.rk - 1));
     const uint32_t lv = lut_v + 4u * (uint32_t)(lane & (p.rv - 1));
@@ -696,18 +831,43 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
       if (lane == 0) tc::mbar_arrive_cta(&bars[B_VFULL + s]);
       cur = nxt;
     }
-    // R_V (MN-major B of OUT = O^ R_V): row i = R[v_coord(i)] -> K stage 0,
-    // once the last S MMA that reads K stage 0 is complete
-    if (ok) {
-      const int jl = (ntiles - 1) & ~1;                   // last tile in stage 0
-      ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_KEMPTY], (uint32_t)((jl >> 1) & 1),
-                                                 abort_flag, p.status));
+    // R_V (MN-major B of OUT = O^ R_V): row i = R[v_coord(i)], fp16 hi in K
+    // stage 0 and lo = R - hi in K stage 1, once the last S MMAs that read
+    // those stages are complete.  The fp32 rows are fetched first (all loads
+    // in flight), then the stages are awaited.
+    constexpr int kIt = kD * 16 / kDecThreads;            // 8 chunks per thread
+    float4 rv[kIt][2];
+#pragma unroll
+    for (int m = 0; m < kIt; ++m) {
+      const int it = dt + m * kDecThreads, i = it >> 4, c = it & 15;
+      const float4* src = reinterpret_cast<const float4*>(p.rot + v_coord(i) * kD + 8 * c);
+      rv[m][0] = __ldg(src);
+      rv[m][1] = __ldg(src + 1);
     }
     if (ok) {
-      for (int it = dt; it < kD * 16; it += kDecThreads) {
-        const int i = it >> 4, c = it & 15;
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.rot_h + v_coord(i) * kD) + c);
-        sts128(sbase + OFF_K + sw_chunk(i, c), v);
+      const int j0 = (ntiles - 1) & ~1;                   // last tile in stage 0
+      ok = wait_or_abort(&bars[B_KEMPTY], (uint32_t)((j0 >> 1) & 1), abort_flag, p.status);
+      if (ok && ntiles >= 2) {
+        const int j1 = (ntiles - 1) & 1 ? ntiles - 1 : ntiles - 2;   // last tile in stage 1
+        ok = wait_or_abort(&bars[B_KEMPTY + 1], (uint32_t)((j1 >> 1) & 1), abort_flag, p.status);
+      }
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+#pragma unroll
+      for (int m = 0; m < kIt; ++m) {
+        const int it = dt + m * kDecThreads, i = it >> 4, c = it & 15;
+        const float v[8] = {rv[m][0].x, rv[m][0].y, rv[m][0].z, rv[m][0].w,
+                            rv[m][1].x, rv[m][1].y, rv[m][1].z, rv[m][1].w};
+        uint32_t h[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          h[e] = pack_half2(v[2 * e], v[2 * e + 1]);
+          const __half2 hh = *reinterpret_cast<const __half2*>(&h[e]);
+          lo[e] = pack_half2(v[2 * e] - __low2float(hh), v[2 * e + 1] - __high2float(hh));
+        }
+        sts128(sbase + OFF_K + sw_chunk(i, c), make_uint4(h[0], h[1], h[2], h[3]));
+        sts128(sbase + OFF_K + kStage + sw_chunk(i, c), make_uint4(lo[0], lo[1], lo[2], lo[3]));
       }
       tc::fence_proxy_async_smem();
       __syncwarp();
@@ -760,6 +920,7 @@ int launch_prefill_tc(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   p.off_kn = g.off_kn;
   p.off_vn = g.off_vn;
   p.rot_h = reinterpret_cast<const __half*>(t->rot_f16);
+  p.rot = t->rot;
   p.kc = t->k_centroids;
   p.vc = t->v_centroids;
   p.q = a->q->data; p.q_dtype = a->q->dtype; p.q_vec = vec_ok(a->q);

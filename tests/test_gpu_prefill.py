@@ -5,7 +5,9 @@ repeat) over the dequantised K/V x^ = n (c[idx] R) that update() returns at
 residual_window 0 (kv_cache.py:422-439, 483-488), evaluated on the codes and
 norms the kernel's own append stored.  The kernel rotates queries, attends
 fp16 centroid values and un-rotates outputs with fp16 operands, so the bar is
-cosine >= 0.9999 and max-abs <= 4e-3 * max|o| per case.
+cosine >= 0.9999 and max-abs <= 4e-3 * max|o| per case, plus half a unit in
+the last place of the output dtype at max|o| (the rounding of an exact result
+to bf16 alone reaches 0.0156 at |o| = 6).
 """
 import math
 
@@ -28,11 +30,16 @@ def _dequant(t, pages, n):
     return k, v                                   # (S, n, D) float32
 
 
+_MANTISSA = {torch.bfloat16: 8, torch.float16: 11, torch.float32: 24}
+
+
 def _check(got, want, tol=4e-3):
+    top = float(np.abs(want).max())
+    half_ulp = 2.0 ** (math.floor(math.log2(top)) - _MANTISSA[got.dtype]) if top > 0 else 0.0
     got = got.float().cpu().numpy()
     assert cosine(got, want) >= 0.9999, cosine(got, want)
     err = np.abs(got - want).max()
-    assert err <= tol * np.abs(want).max(), (err, np.abs(want).max())
+    assert err <= tol * top + half_ulp, (err, top, half_ulp)
 
 
 CASES = [
@@ -54,7 +61,7 @@ def test_prefill_matches_oracle(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, engine
 
 
 def _run_case(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, engine, q_dtype=torch.bfloat16,
-              transpose_q=False, key_growth=0.0):
+              transpose_q=False, key_growth=0.0, out_dtype=None):
     t = make_tables(D, kb, vb, qjl)
     k = rand_kv((B, Hkv, n, D), 21)
     if key_growth:
@@ -66,7 +73,8 @@ def _run_case(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, engine, q_dtype=torch.bf
     qd = q.to(DEV, q_dtype)
     if transpose_q:            # (B, Tq, Hq, D) storage seen as (B, Hq, Tq, D)
         qd = qd.transpose(1, 2).contiguous().transpose(1, 2)
-    out = ops.prefill_attention(t, pages, qd, n, causal=causal, engine=engine)
+    out = None if out_dtype is None else torch.empty(qd.shape, dtype=out_dtype, device=DEV)
+    out = ops.prefill_attention(t, pages, qd, n, causal=causal, engine=engine, out=out)
     torch.cuda.synchronize()
     assert ops.device_status(DEV) == 0
     kd, vd = _dequant(t, pages, n)
@@ -86,10 +94,13 @@ TC_CASES = [
 ]
 
 
+@pytest.mark.parametrize("out_dtype", [None, torch.float32])
 @pytest.mark.parametrize("D,kb,vb,qjl,B,Hkv,g,n,Tq,causal", TC_CASES)
-def test_tensor_core_prefill_matches_oracle(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal):
+def test_tensor_core_prefill_matches_oracle(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, out_dtype):
+    """bf16 output (the query dtype) and fp32 output, where the comparison
+    sees the kernel's own error without the output rounding."""
     assert ops.prefill_uses_tensor_cores(make_tables(D, kb, vb, qjl))
-    _run_case(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, 0)
+    _run_case(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, 0, out_dtype=out_dtype)
 
 
 @pytest.mark.parametrize("q_dtype,transpose_q", [(torch.float16, False), (torch.bfloat16, True),
