@@ -514,27 +514,35 @@ def bench_prefill(dev, args):
     ops.append(t, pages, k, k, 0)
     q = torch.randn((B, H * g, T, Dd), device=dev, generator=gen).to(torch.bfloat16)
     out = torch.empty_like(q)
-    for _ in range(2):
-        ops.prefill_attention(t, pages, q, T, out=out)
-    torch.cuda.synchronize()
-    reps = max(2, min(args.steps, 5))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        ops.prefill_attention(t, pages, q, T, out=out)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
     flops = 4.0 * B * H * g * (T * T / 2) * Dd
+    reps = max(2, min(args.steps, 5))
+
+    def timed(engine):
+        for _ in range(2):
+            ops.prefill_attention(t, pages, q, T, out=out, engine=engine)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            ops.prefill_attention(t, pages, q, T, out=out, engine=engine)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    ms_cc = timed(1)                 # the mma.sync kernel, for comparison
+    ms = timed(0)
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peak = float(json.load(f)["bf16_tflops"])
     except Exception:
         peak = 1590.0
+    tc = ops.prefill_uses_tensor_cores(t)
     return {"workload": f"prefill attention over the packed cache, 1 layer: B{B} x Hq{H * g}/Hkv{H} "
                         f"x {T} tokens causal, D{Dd}, K{bits}/V{bits}", "ms": ms,
             "tflops": flops / (ms / 1e3) / 1e12, "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peak,
-            "kernel": "prefill_kernel (mma.sync m16n8k16 fp16)"}
+            "kernel": ("prefill_tc_kernel (tcgen05.mma, S/P and O in tensor memory)" if tc
+                       else "prefill_kernel (mma.sync m16n8k16 fp16)"),
+            "mma_sync_kernel_ms": ms_cc}
 
 
 def run_profile(args):

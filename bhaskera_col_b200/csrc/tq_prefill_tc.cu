@@ -174,10 +174,12 @@ __device__ __forceinline__ void mask_keys(uint32_t (&x)[32], int64_t last) {
 // fp16 pair {exp2(a - bias), exp2(b - bias)} (a in the low half): the
 // differences rounded to fp16 (|a - bias| < 2^4 carries an error below 2^-7
 // in the exponent only for p < 2^-4), then one SFU op for both exponentials.
-__device__ __forceinline__ uint32_t exp2_pair(uint32_t a, uint32_t b, float bias) {
+__device__ __forceinline__ uint32_t exp2_pair(uint32_t a, uint32_t b, uint64_t nbias2) {
   uint32_t h, p;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;"
-      : "=r"(h) : "f"(__uint_as_float(b) - bias), "f"(__uint_as_float(a) - bias));
+  asm("{\n .reg .b64 x, y;\n .reg .f32 lo, hi;\n"
+      " mov.b64 x, {%1, %2};\n add.rn.f32x2 y, x, %3;\n mov.b64 {lo, hi}, y;\n"
+      " cvt.rn.f16x2.f32 %0, hi, lo;\n}"
+      : "=r"(h) : "r"(a), "r"(b), "l"(nbias2));
   asm("ex2.approx.f16x2 %0, %1;" : "=r"(p) : "r"(h));
   return p;
 }
@@ -216,13 +218,15 @@ __device__ __forceinline__ void fail(uint32_t* status, volatile int* abort_flag)
 }
 
 // Bounded wait (2 s) that also gives up as soon as another role has aborted.
-// try_wait without a suspend-time hint: a hinted wait wakes about 0.1 us
-// late, which costs more than the polling on this kernel's per-tile handoffs.
+// try_wait without a suspend-time hint (a hinted wait wakes about 0.1 us late,
+// more than this kernel's per-tile hand-offs can afford) and a short sleep
+// between polls, so waiting warps leave the issue slots to working ones.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
                                               volatile int* abort_flag, uint32_t* status) {
   uint64_t t0 = 0;
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(32);
     if ((i & 255u) == 255u) {
       if (*abort_flag) return false;
       const uint64_t t = global_ns();
@@ -280,34 +284,39 @@ __device__ __forceinline__ uint32_t pair_index(const Stream<NB>& s, int p) {
   return __funnelshift_r(s.w[w], s.w[w + 1], sh) & mask;
 }
 
+// Byte offsets (within a stage, page 0) of the four 16-byte chunks a decoder
+// thread writes: chunks 4 part .. 4 part + 3 of row kk.  With the XOR swizzle
+// they are (c ^ q) << 4 for one per-thread constant c, so no address math is
+// left in the tile loop.
+struct ChunkOffsets { uint32_t o[4]; };
+__device__ __forceinline__ ChunkOffsets chunk_offsets(int kk, int part) {
+  ChunkOffsets r;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) r.o[q] = sw_chunk(kk, 4 * part + q);
+  return r;
+}
+
 // Decode a 32-position stream into 4 fp16 chunks (x norm) and store them at
-// chunks c0..c0+3 of row `key` of the operand at `base`.
+// `tile` + co.o[q].  Plain C++ shared loads and stores (no volatile asm), so
+// the compiler can issue every table lookup of a tile ahead of the stores;
+// the proxy fence that follows a tile orders the stores before the hand-off.
 template <int NB>
-__device__ __forceinline__ void decode_stream(const Stream<NB>& s, uint32_t lut, uint32_t rep4,
-                                              __half2 n2, uint32_t base, int key, int c0) {
+__device__ __forceinline__ void decode_stream(const Stream<NB>& s, const unsigned char* lut,
+                                              int rep4, __half2 n2, unsigned char* tile,
+                                              const ChunkOffsets& co) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint32_t h[4];
 #pragma unroll
     for (int pp = 0; pp < 4; ++pp) {
-      const uint32_t idx = pair_index<NB>(s, 4 * q + pp);
-      uint32_t v = tc::lds_u32(lut + idx * rep4);
+      uint32_t v = *reinterpret_cast<const uint32_t*>(lut + pair_index<NB>(s, 4 * q + pp) * rep4);
       __half2 x = *reinterpret_cast<__half2*>(&v);
       x = __hmul2(x, n2);
       h[pp] = *reinterpret_cast<uint32_t*>(&x);
     }
-    sts128(base + sw_chunk(key, c0 + q), make_uint4(h[0], h[1], h[2], h[3]));
+    *reinterpret_cast<uint4*>(tile + co.o[q]) = make_uint4(h[0], h[1], h[2], h[3]);
   }
 }
-
-// The codes and norms one decoder thread needs for one tile: key kk of both
-// pages, K quad `part` and V octet pair `part`.
-template <int KB, int VB>
-struct TileRegs {
-  Stream<KB> k[2];
-  Stream<VB> v[2];
-  uint32_t nrm[2];              // kn | vn << 16 (fp16 bits)
-};
 
 struct TcParamsView {
   const uint8_t* spages;        // this stream's pages
@@ -316,25 +325,42 @@ struct TcParamsView {
   int64_t kend;                 // keys this CTA needs
 };
 
-template <int KB, int VB>
-__device__ __forceinline__ void load_tile(TileRegs<KB, VB>& t, const TcParamsView& pv, int j) {
+// One operand's codes and norms that a decoder thread needs for one tile:
+// key kk of both pages, K quad / V octet pair `part`.
+template <int NB>
+struct HalfRegs {
+  Stream<NB> c[2];
+  uint32_t n[2];                // fp16 norm bits
+};
+
+template <int NB>
+__device__ __forceinline__ void load_half(HalfRegs<NB>& t, const TcParamsView& pv, int j,
+                                          int off_codes, int off_norm) {
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
     const int64_t key = (int64_t)j * kKeys + p * 64 + pv.kk;
     if (key < pv.kend) {
       const uint8_t* pg = pv.spages + (int64_t)(2 * j + p) * pv.page_bytes;
-      load_stream<KB>(t.k[p], pg + pv.kk * (16 * KB) + pv.part * (4 * KB));
-      load_stream<VB>(t.v[p], pg + pv.off_v + pv.kk * (16 * VB) + pv.part * (4 * VB));
-      const uint32_t kn = __ldg(reinterpret_cast<const unsigned short*>(pg + pv.off_kn) + pv.kk);
-      const uint32_t vn = __ldg(reinterpret_cast<const unsigned short*>(pg + pv.off_vn) + pv.kk);
-      t.nrm[p] = kn | (vn << 16);
+      load_stream<NB>(t.c[p], pg + off_codes + pv.kk * (16 * NB) + pv.part * (4 * NB));
+      t.n[p] = __ldg(reinterpret_cast<const unsigned short*>(pg + off_norm) + pv.kk);
     } else {
 #pragma unroll
-      for (int i = 0; i < KB; ++i) t.k[p].w[i] = 0u;
-#pragma unroll
-      for (int i = 0; i < VB; ++i) t.v[p].w[i] = 0u;
-      t.nrm[p] = 0u;
+      for (int i = 0; i < NB; ++i) t.c[p].w[i] = 0u;
+      t.n[p] = 0u;
     }
+  }
+}
+
+// Decode both pages of one operand tile into the stage at `tile` (page 1's
+// rows sit 64 rows = 8 KB below page 0's).
+template <int NB>
+__device__ __forceinline__ void decode_half(const HalfRegs<NB>& t, const unsigned char* lut,
+                                            int rep4, unsigned char* tile, const ChunkOffsets& co) {
+#pragma unroll
+  for (int pg = 0; pg < 2; ++pg) {
+    const uint32_t n2 = t.n[pg] * 0x10001u;
+    decode_stream<NB>(t.c[pg], lut, rep4, *reinterpret_cast<const __half2*>(&n2),
+                      tile + pg * 64 * 128, co);
   }
 }
 
@@ -632,6 +658,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
       const float f = resc ? fast_exp2(m - m_new) : 1.f;
       if (m == -INFINITY || resc) m = m_new;
       const float bias = m == -INFINITY ? 0.f : m;
+      const uint64_t nbias2 = (uint64_t)__float_as_uint(-bias) * 0x100000001ull;
       // pass 2: P = exp2(S - m) as fp16 pairs over the S columns (masked
       // scores are -inf: p = 0); the row sum comes from the P x ones MMA
 #pragma unroll 1
@@ -648,8 +675,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
         uint32_t h[32];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          h[e] = exp2_pair(x0[2 * e], x0[2 * e + 1], bias);
-          h[16 + e] = exp2_pair(x1[2 * e], x1[2 * e + 1], bias);
+          h[e] = exp2_pair(x0[2 * e], x0[2 * e + 1], nbias2);
+          h[16 + e] = exp2_pair(x1[2 * e], x1[2 * e + 1], nbias2);
         }
         tc::tmem_st_x32(scol + 32 * hh, h);
       }
@@ -787,49 +814,52 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
       pv.part = part;
     }
     pv.kend = kend;
-    const uint32_t lk = lut_k + 4u * (uint32_t)(lane & (p.rk - 1));
-    const uint32_t lv = lut_v + 4u * (uint32_t)(lane & (p.rv - 1));
-    const uint32_t rk4 = 4u * (uint32_t)p.rk, rv4 = 4u * (uint32_t)p.rv;
-    TileRegs<KB, VB> cur, nxt;
-    load_tile<KB, VB>(cur, pv, 0);
+    const unsigned char* lk = sm + OFF_LUT + 4 * (lane & (p.rk - 1));
+    const unsigned char* lv = sm + OFF_LUT + 4 * nk * p.rk + 4 * (lane & (p.rv - 1));
+    const int rk4 = 4 * p.rk, rv4 = 4 * p.rv;
+    const ChunkOffsets co = chunk_offsets(pv.kk, pv.part);
+    // K^ runs one tile ahead of V^, so the next S MMA's operand never waits
+    // behind a V^ stage that the PV MMA still holds
+    HalfRegs<KB> kc, kn;
+    HalfRegs<VB> vc, vn;
     bool ok = true;
+    load_half<KB>(kc, pv, 0, 0, p.off_kn);
+    decode_half<KB>(kc, lk, rk4, sm + OFF_K, co);
+    tc::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL]);
+    if (ntiles > 1) load_half<KB>(kc, pv, 1, 0, p.off_kn);
+    load_half<VB>(vc, pv, 0, p.off_v, p.off_vn);
     for (int j = 0; j < ntiles; ++j) {
-      const int s = j & 1;
-      if (j + 1 < ntiles) load_tile<KB, VB>(nxt, pv, j + 1);
-      // K^ tile: the S MMA of tile j - 2 has read this stage
-      if (j >= 2)
-        ok = wait_or_abort(&bars[B_KEMPTY + s], (uint32_t)(((j >> 1) - 1) & 1), abort_flag,
-                           p.status);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      const uint32_t kb = sbase + OFF_K + s * kStage;
-#pragma unroll
-      for (int pg = 0; pg < 2; ++pg) {
-        const uint32_t nk2 = (cur.nrm[pg] & 0xFFFFu) * 0x10001u;
-        decode_stream<KB>(cur.k[pg], lk, rk4, *reinterpret_cast<const __half2*>(&nk2), kb,
-                          pg * 64 + pv.kk, 4 * pv.part);
+      if (j + 2 < ntiles) load_half<KB>(kn, pv, j + 2, 0, p.off_kn);
+      if (j + 1 < ntiles) load_half<VB>(vn, pv, j + 1, p.off_v, p.off_vn);
+      if (j + 1 < ntiles) {
+        // K^ of tile j + 1: the S MMA of tile j - 1 has read this stage
+        const int jk = j + 1, sk = jk & 1;
+        if (jk >= 2)
+          ok = wait_or_abort(&bars[B_KEMPTY + sk], (uint32_t)(((jk >> 1) - 1) & 1), abort_flag,
+                             p.status);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        decode_half<KB>(kc, lk, rk4, sm + OFF_K + sk * kStage, co);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL + sk]);
       }
-      tc::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL + s]);
-      // V^ tile: the PV MMA of tile j - 2 (or, for tile 0, q' = Q R_K^T, whose
-      // R_K sits in V stage 0) has read this stage
+      // V^ of tile j: the PV MMA of tile j - 2 (or, for tile 0, q' = Q R_K^T,
+      // whose R_K sits in V stage 0) has read this stage
+      const int s = j & 1;
       if (j >= 2)
         ok = wait_or_abort(&bars[B_VEMPTY + s], (uint32_t)(((j >> 1) - 1) & 1), abort_flag,
                            p.status);
       else if (j == 0)
         ok = wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) break;
-      const uint32_t vb = sbase + OFF_V + s * kStage;
-#pragma unroll
-      for (int pg = 0; pg < 2; ++pg) {
-        const uint32_t vn2 = (cur.nrm[pg] >> 16) * 0x10001u;
-        decode_stream<VB>(cur.v[pg], lv, rv4, *reinterpret_cast<const __half2*>(&vn2), vb,
-                          pg * 64 + pv.kk, 4 * pv.part);
-      }
+      decode_half<VB>(vc, lv, rv4, sm + OFF_V + s * kStage, co);
       tc::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cta(&bars[B_VFULL + s]);
-      cur = nxt;
+      kc = kn;
+      vc = vn;
     }
     // R_V (MN-major B of OUT = O^ R_V): row i = R[v_coord(i)], fp16 hi in K
     // stage 0 and lo = R - hi in K stage 1, once the last S MMAs that read
