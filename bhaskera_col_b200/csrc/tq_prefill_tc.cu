@@ -33,10 +33,11 @@
 // the sum of the fp16 P the PV MMA used and is rescaled with O), and at 416
 // q' as fp16 pairs: both S and PV MMAs take A from tensor memory and read
 // only their B tiles from shared memory.
-// Shared memory: Q (later O^) 32 KB, two K^ and two V^ stages of 32 KB, the
-// pair tables.  R_K is staged in V stage 0 before the first tile; after the
-// last, R_V (fp16 hi and lo terms) takes both K stages and the lo term of O^
-// V stage 0, so the output rotation carries no fp16 rounding of O^ or R.
+// Shared memory: two K^ and two V^ stages of 32 KB, the pair tables (up to
+// 64 KB: 32 lane copies of K4 and V4 tables), a tile of fp16 ones.  R_K and Q
+// are staged in the two V stages before the first tiles; after the last,
+// R_V (fp16 hi and lo terms) takes both K stages and O^ (hi and lo) both V
+// stages, so the output rotation carries no fp16 rounding of O^ or R.
 //
 // K^ (K-major B of S = q' K^^T) and V^ (MN-major B of O = P V^) share one
 // physical layout: [64-column half][128 keys][128 B], 16-byte chunks swizzled
@@ -72,12 +73,15 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 constexpr uint32_t kHalfBytes = 16384;     // [128 rows][128 B]
 constexpr uint32_t kStage = 2 * kHalfBytes;
-constexpr uint32_t OFF_Q = 0;
-constexpr uint32_t OFF_K = OFF_Q + kStage;
+constexpr uint32_t OFF_K = 0;
 constexpr uint32_t OFF_V = OFF_K + 2 * kStage;
 constexpr uint32_t OFF_LUT = OFF_V + 2 * kStage;
-constexpr uint32_t kLutMax = 36864;
+constexpr uint32_t kLutMax = 65536;             // K4/V4: two 256-entry tables x 32 copies
 constexpr uint32_t OFF_ONES = OFF_LUT + kLutMax;   // [2][16 rows][128 B] of fp16 1.0
+constexpr uint32_t OFF_RK = OFF_V;                 // R_K, before the first V^ tile
+constexpr uint32_t OFF_QSTG = OFF_V + kStage;      // Q, before the second V^ tile
+constexpr uint32_t OFF_OHI = OFF_V;                // O^ hi / lo after the last PV MMA
+constexpr uint32_t OFF_OLO = OFF_V + kStage;
 constexpr uint32_t OFF_BAR = OFF_ONES + 4096;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;   // + alignment slack
 
@@ -417,7 +421,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
   const uint32_t lut_v = lut_k + (uint32_t)(nk * p.rk * 4);
   if (warp >= 1 && warp <= kSoftWarps) {
     // this warp's 32 rows, two rows per pass: 16 lanes x 16 bytes of a row
-    const uint32_t qdst = sbase + OFF_Q;
+    const uint32_t qdst = sbase + OFF_QSTG;
     const int half = lane >> 4, c = lane & 15;
     if (p.q_vec) {
       uint4 raw[16];                            // every load in flight at once
@@ -470,7 +474,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
 #pragma unroll
       for (int m = 0; m < kIt; ++m) {
         const int it = dt + m * kDecThreads;
-        sts128(sbase + OFF_V + sw_chunk(it >> 4, it & 15), v[m]);
+        sts128(sbase + OFF_RK + sw_chunk(it >> 4, it & 15), v[m]);
       }
     }
     // pair tables: one entry per thread, its rk (rv) copies written 16 bytes
@@ -504,8 +508,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
 #pragma unroll
       for (int st = 0; st < 8; ++st) {
         const uint32_t off = (uint32_t)((st >> 2) * kHalfBytes + (st & 3) * 32);
-        umma_ss(tmem, tc::sdesc_kmajor_sw128(sbase + OFF_Q + off),
-                      tc::sdesc_kmajor_sw128(sbase + OFF_V + off), idesc_kk, st ? 1u : 0u);
+        umma_ss(tmem, tc::sdesc_kmajor_sw128(sbase + OFF_QSTG + off),
+                      tc::sdesc_kmajor_sw128(sbase + OFF_RK + off), idesc_kk, st ? 1u : 0u);
       }
       tc::umma_commit(&bars[B_ROT]);
       ok = wait_or_abort(&bars[B_QP], 0u, abort_flag, p.status);
@@ -562,7 +566,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
         // O^hi R_V,hi + O^lo R_V,hi + O^hi R_V,lo
 #pragma unroll
         for (int term = 0; term < 3; ++term) {
-          const uint32_t abase = sbase + (term == 1 ? OFF_V : OFF_Q);
+          const uint32_t abase = sbase + (term == 1 ? OFF_OLO : OFF_OHI);
           const uint32_t bbase = sbase + OFF_K + (term == 2 ? kStage : 0u);
 #pragma unroll
           for (int st = 0; st < 8; ++st) {
@@ -748,8 +752,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
             const __half2 hh = *reinterpret_cast<const __half2*>(&h[e]);
             lo[e] = pack_half2(a - __low2float(hh), b - __high2float(hh));
           }
-          sts128(sbase + OFF_Q + sw_chunk(r, 4 * c + q), make_uint4(h[0], h[1], h[2], h[3]));
-          sts128(sbase + OFF_V + sw_chunk(r, 4 * c + q), make_uint4(lo[0], lo[1], lo[2], lo[3]));
+          sts128(sbase + OFF_OHI + sw_chunk(r, 4 * c + q), make_uint4(h[0], h[1], h[2], h[3]));
+          sts128(sbase + OFF_OLO + sw_chunk(r, 4 * c + q), make_uint4(lo[0], lo[1], lo[2], lo[3]));
         }
       }
       tc::fence_proxy_async_smem();
@@ -845,13 +849,12 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
         __syncwarp();
         if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL + sk]);
       }
-      // V^ of tile j: the PV MMA of tile j - 2 (or, for tile 0, q' = Q R_K^T,
-      // whose R_K sits in V stage 0) has read this stage
+      // V^ of tile j: the PV MMA of tile j - 2 has read this stage
       const int s = j & 1;
       if (j >= 2)
         ok = wait_or_abort(&bars[B_VEMPTY + s], (uint32_t)(((j >> 1) - 1) & 1), abort_flag,
                            p.status);
-      else if (j == 0)
+      else   // tiles 0 and 1: R_K and Q sit in the V stages until q' = Q R_K^T is done
         ok = wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) break;
       decode_half<VB>(vc, lv, rv4, sm + OFF_V + s * kStage, co);
