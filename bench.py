@@ -177,7 +177,7 @@ def run_reference(args, rank, world):
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": W.scaling,
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": _config(W, world),
+        "config": _config(W, world, args.gather),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": C.host_threads(),
                          "kind": "port",
                          "sample": f"1 of {LAYERS} layers per step timed, x{LAYERS}; "
@@ -189,7 +189,7 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def _config(W, world):
+def _config(W, world, gather="fused"):
     import math as _m
     B = W.batch * world if W.scaling == "weak" else W.batch
     bpt = W.d * (W.kb + W.vb) // 8 + 4 + ((W.d // 8 + 2) if W.qjl else 0)
@@ -202,7 +202,9 @@ def _config(W, world):
             "value_bits": W.vb, "qjl": W.qjl,
             "kv_data": ("N(0,1), 2 of 128 channels x8" if W.data == "outlier"
                         else "Student-t(4) / sqrt(2)"),
-            "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+            "parallelism": f"kv-head shard x{world}" + (
+                "" if world == 1 else " + NCCL all-gather" if gather == "nccl"
+                else " + all-gather fused into the decode (peer NVLink stores)"),
             "l2": (f"no flush: {per_gpu / 1e9:.2f} GB packed KV per step per GPU > 126 MB L2"
                    if per_gpu > 4 * 126e6 else
                    f"{per_gpu / 1e6:.0f} MB packed KV per step per GPU over {W.layers} "
@@ -215,7 +217,8 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
     from bhaskera_col_b200 import _lib
     from bhaskera_col_b200.inference import TurboQuantKVCache, ops
-    from bhaskera_col_b200.inference.head_parallel import HeadParallelDecoder, HeadShard
+    from bhaskera_col_b200.inference.head_parallel import (HeadParallelDecoder, HeadShard,
+                                                           SharedGather)
 
     W = _workload(args)
     LAYERS, HQ, HKV, D, T_CTX, KEY_BITS, VALUE_BITS, QJL = (W.layers, W.hq, W.hkv, W.d, W.t_ctx,
@@ -259,14 +262,23 @@ def run_ours(args, rank, world, local_rank):
     k_new = [synth((B, hkv, 1, D)) for _ in range(LAYERS)]
     v_new = [synth((B, hkv, 1, D)) for _ in range(LAYERS)]
     o_loc = [torch.empty((B, hq, 1, D), dtype=torch.bfloat16, device=dev) for _ in range(LAYERS)]
-    o_all = [torch.empty((world * B, hq, 1, D), dtype=torch.bfloat16, device=dev)
-             for _ in range(LAYERS)]
+    # the gathered outputs: for world > 1 by default in peer-mapped buffers
+    # that the decode itself fills (fused all-gather), else NCCL into o_all
+    fused = (SharedGather(shard, LAYERS, B, D, dev)
+             if world > 1 and args.gather == "fused" else None)
+    o_all = (fused.out if fused is not None else
+             torch.empty((LAYERS, world * B, hq, 1, D), dtype=torch.bfloat16, device=dev))
     ws = ops.DecodeWorkspace()
     n_tok = T_CTX + 1
 
     def step(phased_events=None):
         for layer in range(LAYERS):
             st = stores[layer]
+            if phased_events is None and fused is not None:
+                ops.decode_step(st.tables, st._pages, k_new[layer], v_new[layer], T_CTX,
+                                q_dev[layer], out=fused.block_view(layer), workspace=ws,
+                                gather=fused.args(layer))
+                continue
             if phased_events is None:
                 ops.decode_step(st.tables, st._pages, k_new[layer], v_new[layer], T_CTX,
                                 q_dev[layer], out=o_loc[layer], workspace=ws)
@@ -362,22 +374,53 @@ def run_ours(args, rank, world, local_rank):
     full_q = [torch.cat([q] * world, 1) for q in q_dev[:4]]
     full_k = [torch.cat([k] * world, 1) for k in k_new[:4]]
     full_v = [torch.cat([v] * world, 1) for v in v_new[:4]]
-    q_h = [q.cpu().pin_memory() for q in full_q]
-    k_h = [k.cpu().pin_memory() for k in full_k]
-    v_h = [v.cpu().pin_memory() for v in full_v]
-    o_h = torch.empty((B, HQ, 1, D), dtype=torch.bfloat16).pin_memory()
-    h2d = (q_h[0].numel() + k_h[0].numel() + v_h[0].numel()) * 2 * LAYERS
-    d2h = o_h.numel() * 2 * LAYERS
-    decoder = HeadParallelDecoder(cache, shard)
+    # every step copies all 32 layers' q/k/v from one pinned host buffer (in
+    # three chunks: layer 0, layers 1-3, the rest, so layer 0 starts after a
+    # 200 KB copy and later chunks land while earlier layers compute) and reads
+    # all 32 gathered outputs back (layers 0-30 behind the last layer's
+    # compute, then layer 31); copies run on their own stream
+    qn, kn = full_q[0].numel(), full_k[0].numel()
+    per = qn + 2 * kn
+    in_h = torch.empty((LAYERS, per), dtype=torch.bfloat16).pin_memory()
+    for layer in range(LAYERS):
+        in_h[layer, :qn] = full_q[layer % 4].flatten().cpu()
+        in_h[layer, qn:qn + kn] = full_k[layer % 4].flatten().cpu()
+        in_h[layer, qn + kn:] = full_v[layer % 4].flatten().cpu()
+    in_d = torch.empty((LAYERS, per), dtype=torch.bfloat16, device=dev)
+    q_in = [in_d[l, :qn].view(full_q[0].shape) for l in range(LAYERS)]
+    k_in = [in_d[l, qn:qn + kn].view(full_k[0].shape) for l in range(LAYERS)]
+    v_in = [in_d[l, qn + kn:].view(full_v[0].shape) for l in range(LAYERS)]
+    o_h = torch.empty(o_all.shape, dtype=torch.bfloat16).pin_memory()
+    h2d = in_h.numel() * 2
+    d2h = o_h.numel() * 2
+    decoder = HeadParallelDecoder(cache, shard, fused=fused)
+    main = torch.cuda.current_stream(dev)
+    copy_stream = torch.cuda.Stream(dev)
+    chunks = [(0, 1), (1, min(4, LAYERS)), (min(4, LAYERS), LAYERS)]
+    ev_in = [torch.cuda.Event() for _ in chunks]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
     def e2e_step():
+        with torch.cuda.stream(copy_stream):
+            for (a, b), ev in zip(chunks, ev_in):
+                if b > a:
+                    in_d[a:b].copy_(in_h[a:b], non_blocking=True)
+                ev.record(copy_stream)
         for layer in range(LAYERS):
-            qd = q_h[layer % 4].to(dev, non_blocking=True)
-            kd = k_h[layer % 4].to(dev, non_blocking=True)
-            vd = v_h[layer % 4].to(dev, non_blocking=True)
-            o = decoder.decode(qd, kd, vd, layer, buf=o_all[layer])
-            o_h.copy_(o, non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
+            for (a, _), ev in zip(chunks, ev_in):
+                if layer == a:
+                    main.wait_event(ev)
+            decoder.decode(q_in[layer], k_in[layer], v_in[layer], layer, buf=o_all[layer])
+            if layer == LAYERS - 2:
+                ev_out[0].record(main)
+        ev_out[1].record(main)
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(ev_out[0])
+            o_h[:LAYERS - 1].copy_(o_all[:LAYERS - 1], non_blocking=True)
+            copy_stream.wait_event(ev_out[1])
+            o_h[LAYERS - 1:].copy_(o_all[LAYERS - 1:], non_blocking=True)
+        copy_stream.synchronize()
+        main.synchronize()
 
     for st in stores:      # the e2e leg appends for real: start from T_CTX tokens
         st._comp_ptr = T_CTX
@@ -402,6 +445,8 @@ def run_ours(args, rank, world, local_rank):
     e2e_val = B / (e2e_ms / args.steps / 1e3)
     status = cache.device_status() | ws.status()
     del graph
+    if fused is not None:
+        fused.close()
 
     # ---- prefill append throughput (48 layers x B8 x Hkv8 x 4096, 4-bit) ----
     append_line = None
@@ -425,7 +470,7 @@ def run_ours(args, rank, world, local_rank):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": W.scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": _config(W, world),
+            "config": _config(W, world, args.gather),
             "packed_kv_gbs_per_gpu": LAYERS * alg_bytes / (ms_step / 1e3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
@@ -622,6 +667,9 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch")
     ap.add_argument("--context", type=int, default=0, help="override the context length")
     ap.add_argument("--bits", type=int, default=0, help="override K and V bit widths")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="multi-GPU output all-gather: fused into the decode (peer stores) "
+                         "or NCCL after it")
     args = ap.parse_args()
     if args.profile:
         run_profile(args)

@@ -28,7 +28,10 @@ EXPORTED = (
     "tq_append", "tq_dequantize", "tq_decode_workspace_bytes", "tq_decode_attn",
     "tq_decode_step", "tq_decode_attn_noalloc", "tq_workspace_status", "tq_device_status",
     "tq_append_tensor_core", "tq_prefill_attn", "tq_prefill_tensor_core",
+    "tq_shared_alloc", "tq_shared_open", "tq_shared_close", "tq_shared_free",
 )
+MAX_PEERS = 8
+SHARED_HANDLE_BYTES = 64
 
 
 class TqError(RuntimeError):
@@ -62,12 +65,18 @@ class Tensor4(ctypes.Structure):
                 ("shape", ctypes.c_int64 * 4), ("stride", ctypes.c_int64 * 4)]
 
 
+class Gather(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("peer_out", ctypes.c_void_p * MAX_PEERS),
+                ("peer_flag", ctypes.c_void_p * MAX_PEERS)]
+
+
 class DecodeArgs(ctypes.Structure):
     _fields_ = [("q", ctypes.POINTER(Tensor4)), ("out", ctypes.POINTER(Tensor4)),
                 ("window_k", ctypes.POINTER(Tensor4)), ("window_v", ctypes.POINTER(Tensor4)),
                 ("n_tokens", ctypes.c_int64), ("num_q_heads", ctypes.c_int64),
                 ("scale", ctypes.c_float), ("num_ctas", ctypes.c_int32),
-                ("phases", ctypes.c_int32)]
+                ("phases", ctypes.c_int32), ("gather", ctypes.POINTER(Gather))]
 
 
 class PrefillArgs(ctypes.Structure):
@@ -111,6 +120,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             "tq_append_tensor_core": (I32, [P(Geom), P(Tables), P(Tensor4), P(Tensor4)]),
             "tq_prefill_attn": (I32, [P(Geom), P(Tables), P(Cache), P(PrefillArgs), VP]),
             "tq_prefill_tensor_core": (I32, [P(Geom)]),
+            "tq_shared_alloc": (I32, [SZ, P(ctypes.c_void_p), VP]),
+            "tq_shared_open": (I32, [VP, P(ctypes.c_void_p)]),
+            "tq_shared_close": (I32, [VP]),
+            "tq_shared_free": (I32, [VP]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)

@@ -250,6 +250,27 @@ static int check_decode(const tq_geom* g, const tq_tables* t, const tq_cache* c,
     set_error("%s: window_k and window_v must both be given or both be NULL", fn);
     return TQ_ERR_INVALID;
   }
+  if (a->gather) {
+    const tq_gather* gt = a->gather;
+    if (gt->world < 1 || gt->world > TQ_MAX_PEERS || gt->rank < 0 || gt->rank >= gt->world) {
+      set_error("%s: gather.world must lie in [1, %d] and rank in [0, world)", fn, TQ_MAX_PEERS);
+      return TQ_ERR_INVALID;
+    }
+    for (int r = 0; r < gt->world; ++r)
+      if (!gt->peer_out[r] || !gt->peer_flag[r] ||
+          reinterpret_cast<uintptr_t>(gt->peer_flag[r]) % 8) {
+        set_error("%s: gather.peer_out / peer_flag[%d] missing or misaligned", fn, r);
+        return TQ_ERR_INVALID;
+      }
+    if (gt->peer_out[gt->rank] != a->out->data) {
+      set_error("%s: gather.peer_out[rank] must be out->data", fn);
+      return TQ_ERR_INVALID;
+    }
+    if (a->phases != 0 && !(a->phases & TQ_PHASE_MERGE)) {
+      set_error("%s: a gather needs the merge phase", fn);
+      return TQ_ERR_INVALID;
+    }
+  }
   if (a->window_k) {
     if ((rc = check_t4(a->window_k, "window_k", fn)) || (rc = check_t4(a->window_v, "window_v", fn))) return rc;
     for (int i = 0; i < 4; ++i)
@@ -387,6 +408,46 @@ int32_t tq_prefill_tensor_core(const tq_geom* g) {
 int32_t tq_device_status(uint32_t* status, void* stream) {
   if (!status) { set_error("tq_device_status: NULL argument"); return TQ_ERR_INVALID; }
   return read_tc_status(status, (cudaStream_t)stream);
+}
+
+int32_t tq_shared_alloc(size_t bytes, void** dptr, void* handle) {
+  if (!dptr || !handle || bytes == 0) { set_error("tq_shared_alloc: bad argument"); return TQ_ERR_INVALID; }
+  static_assert(sizeof(cudaIpcMemHandle_t) <= TQ_SHARED_HANDLE_BYTES, "IPC handle size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    set_error("tq_shared_alloc: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  memset(handle, 0, TQ_SHARED_HANDLE_BYTES);
+  memcpy(handle, &h, sizeof(h));
+  *dptr = p;
+  return TQ_OK;
+}
+
+int32_t tq_shared_open(const void* handle, void** dptr) {
+  if (!dptr || !handle) { set_error("tq_shared_open: bad argument"); return TQ_ERR_INVALID; }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) { set_error("tq_shared_open: %s", cudaGetErrorString(e)); return TQ_ERR_CUDA; }
+  return TQ_OK;
+}
+
+int32_t tq_shared_close(void* dptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(dptr);
+  if (e != cudaSuccess) { set_error("tq_shared_close: %s", cudaGetErrorString(e)); return TQ_ERR_CUDA; }
+  return TQ_OK;
+}
+
+int32_t tq_shared_free(void* dptr) {
+  cudaError_t e = cudaFree(dptr);
+  if (e != cudaSuccess) { set_error("tq_shared_free: %s", cudaGetErrorString(e)); return TQ_ERR_CUDA; }
+  return TQ_OK;
 }
 
 }  // extern "C"

@@ -822,6 +822,12 @@ struct MergeParams {
   const void* wk; const void* wv; int w_dtype; int64_t wk_stride[4], wv_stride[4]; int64_t W;
   float scale_log2;       // softmax scale * log2(e)
   void* out; int out_dtype; int64_t out_stride[4];
+  // fused output all-gather (world > 1): the block goes to every rank's
+  // buffer, then each CTA adds 1 to every rank's arrival counter
+  int world, rank;
+  void* peer_out[TQ_MAX_PEERS];
+  uint32_t* peer_flag[TQ_MAX_PEERS];   // [arrivals, this rank's finished CTAs]
+  uint32_t* status;
 };
 
 constexpr int kMaxSlots = 64;
@@ -964,8 +970,47 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
       if (hh >= nh) break;
       const float L = s_L[hh];
       const int64_t hq = kvh * p.g + hc * 8 + hh;
-      store_elem(p.out, p.out_dtype, b * p.out_stride[0] + hq * p.out_stride[1] + j * p.out_stride[3],
-                 L > 0.f ? o[h] / L : 0.f);
+      const int64_t off = b * p.out_stride[0] + hq * p.out_stride[1] + j * p.out_stride[3];
+      const float v = L > 0.f ? o[h] / L : 0.f;
+      if (p.world <= 1) {
+        store_elem(p.out, p.out_dtype, off, v);
+      } else {
+        for (int r = 0; r < p.world; ++r) store_elem(p.peer_out[r], p.out_dtype, off, v);
+      }
+    }
+  }
+  if (p.world > 1) {
+    // every thread's stores reach all ranks before the block's arrival counts
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+      for (int r = 0; r < p.world; ++r) atomicAdd_system(p.peer_flag[r], 1u);
+      // the last CTA of this rank (all others have finished) waits until every
+      // rank's CTAs have arrived, bounded by ~2 s of %globaltimer, and resets
+      // both counters for the layer's next call; only other GPUs' kernels are
+      // waited on, and no rank can add to the counter again before this rank
+      // has finished the step
+      uint32_t* arrived = p.peer_flag[p.rank];
+      uint32_t* done = arrived + 1;
+      const uint32_t nctas = gridDim.x * gridDim.y;
+      if (atomicAdd(done, 1u) + 1u == nctas) {
+        const uint32_t target = (uint32_t)p.world * nctas;
+        uint64_t t0 = 0;
+        for (uint32_t i = 0;; ++i) {
+          uint32_t v;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(arrived) : "memory");
+          if (v >= target) break;
+          __nanosleep(32);
+          if ((i & 63u) == 63u) {
+            const uint64_t t = global_ns();
+            if (t0 == 0) t0 = t;
+            else if (t - t0 > 2000000000ull) { atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT); break; }
+          }
+        }
+        *arrived = 0u;
+        *done = 0u;
+        __threadfence();
+      }
     }
   }
 }
@@ -1164,6 +1209,13 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   mp.scale_log2 = a->scale * kLog2e;
   mp.out = a->out->data; mp.out_dtype = a->out->dtype;
   for (int i = 0; i < 4; ++i) mp.out_stride[i] = a->out->stride[i];
+  mp.world = a->gather ? a->gather->world : 1;
+  mp.rank = a->gather ? a->gather->rank : 0;
+  mp.status = reinterpret_cast<uint32_t*>(ws);
+  for (int r = 0; r < TQ_MAX_PEERS; ++r) {
+    mp.peer_out[r] = a->gather && r < mp.world ? a->gather->peer_out[r] : nullptr;
+    mp.peer_flag[r] = a->gather && r < mp.world ? a->gather->peer_flag[r] : nullptr;
+  }
   if (pl.S > 0 && (phases & TQ_PHASE_MERGE)) {
     const size_t msmem =
         (size_t)(pl.D * pl.D + 16 * pl.D + 8 * kSlotChunk * pl.D + 8 * (mp.W > 0 ? mp.W : 1)) * 4;

@@ -347,18 +347,24 @@ class _LayerKVStore:
                                     workspace=self.workspace)
 
     def decode(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, residual_window: int,
-               scale: Optional[float] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+               scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+               gather=None) -> torch.Tensor:
         """Store one new token and attend q to everything stored, in one fused
-        call when exactly one token moves into packed storage this step."""
+        call when exactly one token moves into packed storage this step.
+        ``gather`` (a _lib.Gather, see head_parallel.SharedGather) fuses the
+        multi-GPU output all-gather into that call."""
         B, H, T, D = k.shape
         self._lazy_alloc(B, H)
         k = k.to(self.dtype)
         v = v.to(self.dtype)
         W = 0 if self._win_k is None else self._win_k.shape[2]
+        if gather is not None and not (T == 1 and residual_window <= 0 and W == 0):
+            raise ValueError("the fused all-gather needs a single-token decode without a "
+                             "residual window")
         if T == 1 and residual_window <= 0 and W == 0:
             self._ensure_capacity(1)
             out = ops.decode_step(self.tables, self._pages, k, v, self._comp_ptr, q, scale=scale,
-                                  out=out, workspace=self.workspace)
+                                  out=out, workspace=self.workspace, gather=gather)
             self._comp_ptr += 1
             return out
         if T == 1 and 0 < residual_window == W:
@@ -484,13 +490,14 @@ class TurboQuantKVCache(BaseKVCache):
 
     def decode(self, query_states: torch.Tensor, key_states: torch.Tensor,
                value_states: torch.Tensor, layer_idx: int, scale: Optional[float] = None,
-               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+               out: Optional[torch.Tensor] = None, gather=None) -> torch.Tensor:
         """One decode step of one layer: store the new token(s) (reference
         update() semantics, including the residual window) and return the
         attention of query_states (B, Hq, 1, D) over the whole cache, without
         materialising dense K/V."""
         return self._stores[layer_idx].decode(query_states, key_states, value_states,
-                                              self.residual_window, scale=scale, out=out)
+                                              self.residual_window, scale=scale, out=out,
+                                              gather=gather)
 
     def prefill(self, query_states: torch.Tensor, key_states: torch.Tensor,
                 value_states: torch.Tensor, layer_idx: int, scale: Optional[float] = None,

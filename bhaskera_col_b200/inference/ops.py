@@ -241,9 +241,11 @@ def decode_step(tables: LayerTables, pages: torch.Tensor, k_new: torch.Tensor,
                 window_v: Optional[torch.Tensor] = None, scale: Optional[float] = None,
                 out: Optional[torch.Tensor] = None,
                 workspace: Optional[DecodeWorkspace] = None,
-                num_ctas: int = 0) -> torch.Tensor:
+                num_ctas: int = 0, gather: Optional[_lib.Gather] = None) -> torch.Tensor:
     """Store the new (B, Hkv, 1, D) token at ``pos`` and attend q over tokens
-    [0, pos + 1) plus the window, in one call (tq_decode_step)."""
+    [0, pos + 1) plus the window, in one call (tq_decode_step).  ``gather``
+    (a filled _lib.Gather whose peer_out[rank] is ``out``) also delivers the
+    output block to every rank's gathered buffer (fused all-gather)."""
     _require_cuda(pages, q, k_new, v_new)
     lib = _lib.load()
     if out is None:
@@ -251,6 +253,8 @@ def decode_step(tables: LayerTables, pages: torch.Tensor, k_new: torch.Tensor,
     g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
     keep = []
     a = _decode_args(q, out, pos + 1, window_k, window_v, scale, num_ctas, 0, keep)
+    if gather is not None:
+        a.gather = ctypes.pointer(gather)
     kt, vt = tensor4(k_new), tensor4(v_new)
     nbytes = lib.tq_decode_workspace_bytes(ctypes.byref(g), ctypes.byref(c), ctypes.byref(a))
     if nbytes == 0:

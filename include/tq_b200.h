@@ -138,6 +138,29 @@ int32_t tq_dequantize(const tq_geom* g, const tq_tables* t, const tq_cache* c,
  * Keys [0, n_tokens) of every stream are attended.  scale is the softmax
  * scale (1/sqrt(D) for SDPA's default).  Workspace from
  * tq_decode_workspace_bytes(). */
+/* Output all-gather fused into the decode (one process per GPU, KV heads
+ * sharded over `world` ranks).  Each rank's merge kernel stores its
+ * (B, Hq/world, 1, D) output block into every rank's copy of the gathered
+ * buffer over peer memory (plain NVLink stores), then adds 1 per CTA to every
+ * rank's arrival counter of the layer; the rank's last CTA waits (bounded,
+ * TQ_DEV_WAIT_TIMEOUT in the status word on expiry) until all ranks' blocks
+ * have arrived and resets the counters, so the call completes with the
+ * gathered output in place.
+ * Buffers come from tq_shared_alloc / tq_shared_open.  Replaces the NCCL
+ * all-gather after each layer's attention (the multi-GPU form of the
+ * reference's single-process cache, kv_cache.py:516-624). */
+#define TQ_MAX_PEERS 8
+typedef struct tq_gather {
+  int32_t world;                       /* ranks (1..TQ_MAX_PEERS)              */
+  int32_t rank;                        /* this rank                            */
+  void* peer_out[TQ_MAX_PEERS];        /* on rank p: this rank's output block;
+                                          peer_out[rank] == out->data; the
+                                          block has out's strides on every rank */
+  uint32_t* peer_flag[TQ_MAX_PEERS];   /* on rank p: the layer's two counters
+                                          (arrivals, rank p's finished CTAs),
+                                          zero between calls                  */
+} tq_gather;
+
 typedef struct tq_decode_args {
   const tq_tensor4* q;
   const tq_tensor4* out;
@@ -150,6 +173,7 @@ typedef struct tq_decode_args {
   int32_t phases;              /* 0: all; else OR of TQ_PHASE_* (each phase  */
                                /* reads what the previous one left in the   */
                                /* same workspace)                            */
+  const tq_gather* gather;     /* NULL: out only; else the fused all-gather  */
 } tq_decode_args;
 
 #define TQ_PHASE_QPREP 1       /* rotate + sketch the query                  */
@@ -231,6 +255,17 @@ int32_t tq_append_tensor_core(const tq_geom* g, const tq_tables* t, const tq_ten
  * its bounded waits ran out).  Blocking copy on `stream`.  No reference
  * counterpart: the reference's append runs on the host. */
 int32_t tq_device_status(uint32_t* status, void* stream);
+
+/* Device memory shareable with the other processes of one node (CUDA IPC on
+ * a plain allocation; no multicast object).  tq_shared_alloc returns a zeroed
+ * allocation and its 64-byte handle; another process maps it with
+ * tq_shared_open (peer access enabled on first use) and unmaps it with
+ * tq_shared_close; the owner frees it with tq_shared_free. */
+#define TQ_SHARED_HANDLE_BYTES 64
+int32_t tq_shared_alloc(size_t bytes, void** dptr, void* handle);
+int32_t tq_shared_open(const void* handle, void** dptr);
+int32_t tq_shared_close(void* dptr);
+int32_t tq_shared_free(void* dptr);
 
 #ifdef __cplusplus
 }
