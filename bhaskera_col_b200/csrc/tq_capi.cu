@@ -342,12 +342,18 @@ int32_t tq_prefill_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
     set_error("%s: tables.rot_f16 (R as fp16, 16-byte aligned) is required", fn);
     return TQ_ERR_INVALID;
   }
-  if (a->engine != 0 && a->engine != 1) {
-    set_error("%s: engine must be 0 (fastest) or 1 (mma.sync), got %d", fn, a->engine);
+  if (a->engine < 0 || a->engine > 3) {
+    set_error("%s: engine must be 0 (fastest), 1 (mma.sync), 2 or 3 (tcgen05, 128 or 256 "
+              "rows per CTA), got %d", fn, a->engine);
+    return TQ_ERR_INVALID;
+  }
+  if (a->engine >= 2 && !prefill_tc_applies(g)) {
+    set_error("%s: no tcgen05 kernel for head_dim %d, key_bits %d, value_bits %d", fn,
+              g->head_dim, g->key_bits, g->value_bits);
     return TQ_ERR_INVALID;
   }
   if (!prefill_supported(g->head_dim, g->key_bits, g->value_bits) &&
-      !(a->engine == 0 && prefill_tc_applies(g))) {
+      !(a->engine != 1 && prefill_tc_applies(g))) {
     set_error("%s: no kernel for head_dim %d, key_bits %d, value_bits %d (engine %d)", fn,
               g->head_dim, g->key_bits, g->value_bits, a->engine);
     return TQ_ERR_INVALID;

@@ -412,7 +412,7 @@ bool prefill_supported(int D, int kb, int vb) {
 
 int launch_prefill(const tq_geom* G, const tq_tables* t, const tq_cache* c,
                    const tq_prefill_args* a, uint32_t* status, cudaStream_t st) {
-  if (a->engine == 0) {
+  if (a->engine != 1) {
     const int rc = launch_prefill_tc(G, t, c, a, status, st);
     if (rc != 1) return rc;
   }

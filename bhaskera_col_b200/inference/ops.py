@@ -279,7 +279,7 @@ def prefill_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
     n_tokens - 1 over the packed tokens [0, n_tokens) of every stream (causal:
     a query sees keys at or before its position).  ``engine`` 0 picks the
     fastest kernel (tcgen05 where prefill_uses_tensor_cores), 1 the mma.sync
-    kernel."""
+    kernel, 2 / 3 the tcgen05 kernel with 128 / 256 query rows per CTA."""
     _require_cuda(pages, q)
     lib = _lib.load()
     if out is None:

@@ -217,7 +217,10 @@ typedef struct tq_prefill_args {
   int32_t causal;              /* 1: causal; 0: every query sees all tokens   */
   int32_t engine;              /* 0: the fastest kernel for the shape (tcgen05
                                   tensor cores where tq_prefill_tensor_core
-                                  says so); 1: the mma.sync kernel             */
+                                  says so: 256 query rows per CTA for chunks
+                                  longer than one 128-row block); 1: the
+                                  mma.sync kernel; 2 / 3: the tcgen05 kernel
+                                  with 128 / 256 rows per CTA                 */
 } tq_prefill_args;
 
 int32_t tq_prefill_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,

@@ -94,23 +94,28 @@ TC_CASES = [
 ]
 
 
+@pytest.mark.parametrize("engine", [2, 3])
 @pytest.mark.parametrize("out_dtype", [None, torch.float32])
 @pytest.mark.parametrize("D,kb,vb,qjl,B,Hkv,g,n,Tq,causal", TC_CASES)
-def test_tensor_core_prefill_matches_oracle(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, out_dtype):
-    """bf16 output (the query dtype) and fp32 output, where the comparison
-    sees the kernel's own error without the output rounding."""
+def test_tensor_core_prefill_matches_oracle(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, out_dtype,
+                                            engine):
+    """Both tcgen05 kernels (engine 2: 128 query rows per CTA; 3: 256 rows, two
+    query tiles sharing each decoded K/V tile), bf16 output (the query dtype)
+    and fp32 output, where the comparison sees the kernel's own error without
+    the output rounding."""
     assert ops.prefill_uses_tensor_cores(make_tables(D, kb, vb, qjl))
-    _run_case(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, 0, out_dtype=out_dtype)
+    _run_case(D, kb, vb, qjl, B, Hkv, g, n, Tq, causal, engine, out_dtype=out_dtype)
 
 
+@pytest.mark.parametrize("engine", [2, 3])
 @pytest.mark.parametrize("q_dtype,transpose_q", [(torch.float16, False), (torch.bfloat16, True),
                                                  (torch.float32, False)])
-def test_tensor_core_prefill_query_layouts(q_dtype, transpose_q):
-    _run_case(128, 4, 2, False, 1, 2, 4, 300, 300, True, 0, q_dtype=q_dtype,
+def test_tensor_core_prefill_query_layouts(q_dtype, transpose_q, engine):
+    _run_case(128, 4, 2, False, 1, 2, 4, 300, 300, True, engine, q_dtype=q_dtype,
               transpose_q=transpose_q)
 
 
-@pytest.mark.parametrize("engine", [0, 1])
+@pytest.mark.parametrize("engine", [0, 1, 2, 3])
 def test_prefill_growing_scores(engine):
     """Key norms growing 5x along the sequence lift the running max by more
     than 8 (log2 units) over the tiles, so the tcgen05 kernel rescales its
