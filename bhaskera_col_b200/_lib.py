@@ -19,6 +19,7 @@ TQ_ERR_CUDA = -2
 TQ_ERR_WORKSPACE = -3
 TQ_ERR_DEVICE = -4
 TQ_F32, TQ_F16, TQ_BF16 = 0, 1, 2
+DEV_WAIT_TIMEOUT, DEV_BAD_BLOCK = 1, 2
 PAGE_TOKENS = 64
 PHASE_QPREP, PHASE_DECODE, PHASE_MERGE = 1, 2, 4
 
@@ -57,7 +58,8 @@ class Tables(ctypes.Structure):
 
 class Cache(ctypes.Structure):
     _fields_ = [("pages", ctypes.c_void_p), ("streams", ctypes.c_int64),
-                ("pages_per_stream", ctypes.c_int64)]
+                ("pages_per_stream", ctypes.c_int64), ("block_table", ctypes.c_void_p),
+                ("block_table_stride", ctypes.c_int64), ("num_blocks", ctypes.c_int64)]
 
 
 class Tensor4(ctypes.Structure):

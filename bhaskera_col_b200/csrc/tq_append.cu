@@ -41,7 +41,8 @@ struct AppendParams {
   const float* ST;      // S^T row-major (QJL)
   int vt;               // vectors per tile (<= kVT)
   uint8_t* pages;
-  int64_t pages_per_stream;
+  PageMap pm;
+  uint32_t* status;     // TQ_DEV_BAD_BLOCK on a block-table entry outside the pool
   const void* x[2];
   int dtype[2];
   int64_t stride[2][4];
@@ -153,7 +154,10 @@ append_kernel(AppendParams p) {
       const int v = i / words, w = i % words;
       const int64_t gv = v0 + v;
       const int64_t t = gv % p.T + p.pos, s = gv / p.T;
-      uint8_t* page = p.pages + (s * p.pages_per_stream + t / kPageTokens) * (int64_t)g.page_bytes;
+      bool ok;
+      const int64_t ps = page_slot(p.pm, s, t / kPageTokens, ok);
+      if (!ok) { atomicOr(p.status, TQ_DEV_BAD_BLOCK); continue; }
+      uint8_t* page = p.pages + ps * (int64_t)g.page_bytes;
       const int slot = (int)(t % kPageTokens);
       reinterpret_cast<uint32_t*>(page + sec + slot * rowbytes)[w] =
           pack_word(code + v * D, ord, bits, w, D);
@@ -164,7 +168,10 @@ append_kernel(AppendParams p) {
         const int v = i / qwords, w = i % qwords;
         const int64_t gv = v0 + v;
         const int64_t t = gv % p.T + p.pos, s = gv / p.T;
-        uint8_t* page = p.pages + (s * p.pages_per_stream + t / kPageTokens) * (int64_t)g.page_bytes;
+        bool ok;
+        const int64_t ps = page_slot(p.pm, s, t / kPageTokens, ok);
+        if (!ok) continue;
+        uint8_t* page = p.pages + ps * (int64_t)g.page_bytes;
         const int slot = (int)(t % kPageTokens);
         reinterpret_cast<uint32_t*>(page + g.off_q + slot * g.qrow)[w] =
             pack_qjl_word(qb + v * D, qinv, w);
@@ -173,7 +180,10 @@ append_kernel(AppendParams p) {
     for (int v = tid; v < nv; v += blockDim.x) {
       const int64_t gv = v0 + v;
       const int64_t t = gv % p.T + p.pos, s = gv / p.T;
-      uint8_t* page = p.pages + (s * p.pages_per_stream + t / kPageTokens) * (int64_t)g.page_bytes;
+      bool ok;
+      const int64_t ps = page_slot(p.pm, s, t / kPageTokens, ok);
+      if (!ok) continue;
+      uint8_t* page = p.pages + ps * (int64_t)g.page_bytes;
       const int slot = (int)(t % kPageTokens);
       reinterpret_cast<__half*>(page + nsec)[slot] = __float2half_rn(nrm[v]);
       if (qjl) reinterpret_cast<__half*>(page + g.off_kr)[slot] = __float2half_rn(gam[v]);
@@ -196,7 +206,8 @@ struct DequantParams {
   const float* cent[2];
   const float* R;
   const uint8_t* pages;
-  int64_t pages_per_stream;
+  PageMap pm;
+  uint32_t* status;
   int64_t H;
   int64_t t0, t1;
   void* out[2];
@@ -223,7 +234,10 @@ __global__ void __launch_bounds__(128) dequant_kernel(DequantParams p) {
   for (int i = threadIdx.x; i < nv * D; i += blockDim.x) {
     const int v = i / D, c = i % D;
     const int64_t t = tt0 + v;
-    const uint8_t* page = p.pages + (s * p.pages_per_stream + t / kPageTokens) * (int64_t)g.page_bytes;
+    bool ok;
+    const int64_t ps = page_slot(p.pm, s, t / kPageTokens, ok);
+    if (!ok) atomicOr(p.status, TQ_DEV_BAD_BLOCK);
+    const uint8_t* page = p.pages + ps * (int64_t)g.page_bytes;
     const uint8_t* row = page + sec + (t % kPageTokens) * rowbytes;
     const int pos = which == 0 ? k_pos_of(c, D) : v_pos_of(c, D);
     const int bo = pos * bits;
@@ -267,7 +281,7 @@ int launch_append(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   p.cent[0] = t->k_centroids; p.cent[1] = t->v_centroids;
   p.bnd[0] = t->k_boundaries; p.bnd[1] = t->v_boundaries;
   p.RT = t->rot_t; p.ST = t->qjl_t;
-  p.pages = c->pages; p.pages_per_stream = c->pages_per_stream;
+  p.pages = c->pages; p.pm = page_map(c); p.status = device_status_word();
   p.x[0] = k->data; p.x[1] = v->data;
   p.dtype[0] = k->dtype; p.dtype[1] = v->dtype;
   for (int i = 0; i < 4; ++i) { p.stride[0][i] = k->stride[i]; p.stride[1][i] = v->stride[i]; }
@@ -300,7 +314,7 @@ int launch_dequant(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   p.g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
   p.cent[0] = t->k_centroids; p.cent[1] = t->v_centroids;
   p.R = t->rot;
-  p.pages = c->pages; p.pages_per_stream = c->pages_per_stream;
+  p.pages = c->pages; p.pm = page_map(c); p.status = device_status_word();
   const tq_tensor4* o[2] = {ko, vo};
   p.H = 1;
   for (int w = 0; w < 2; ++w) {

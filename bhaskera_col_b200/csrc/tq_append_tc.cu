@@ -78,7 +78,7 @@ struct TcParams {
   const float* bnd;
   int nb;
   uint8_t* pages;
-  int64_t pages_per_stream;
+  PageMap pm;
   int page_bytes, row_bytes, sec_off, norm_off;
   int64_t H, T, pos, ntiles, nblk;
 };
@@ -353,9 +353,12 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
       }
       const int64_t s = tile / p.nblk, tb = tile % p.nblk;
       const int64_t t = tb * kM + r;
-      if (t < p.T) {
-        const int64_t tp = p.pos + t;
-        uint8_t* page = p.pages + (s * p.pages_per_stream + tp / kPageTokens) * (int64_t)p.page_bytes;
+      bool pok = true;
+      const int64_t tp = p.pos + t;
+      const int64_t ps = t < p.T ? page_slot(p.pm, s, tp / kPageTokens, pok) : 0;
+      if (!pok) atomicOr(&g_tc_status, TQ_DEV_BAD_BLOCK);
+      if (t < p.T && pok) {
+        uint8_t* page = p.pages + ps * (int64_t)p.page_bytes;
         const int slot = (int)(tp % kPageTokens);
         uint8_t* row = page + p.sec_off + slot * p.row_bytes + part * (kCW * BITS / 8);
         // widest store that the part's byte offset (part * NW * 4) keeps aligned
@@ -486,7 +489,7 @@ int launch_append_tc(const tq_geom* G, const tq_tables* t, const tq_cache* c,
     p.bnd = which == 0 ? t->k_boundaries : t->v_boundaries;
     p.nb = (1 << (which == 0 ? G->key_bits : G->value_bits)) - 1;
     p.pages = c->pages;
-    p.pages_per_stream = c->pages_per_stream;
+    p.pm = page_map(c);
     p.page_bytes = g.page_bytes;
     p.row_bytes = which == 0 ? g.krow : g.vrow;
     p.sec_off = which == 0 ? g.off_k : g.off_v;

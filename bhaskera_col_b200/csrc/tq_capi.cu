@@ -135,6 +135,13 @@ static int check_cache(const tq_cache* c, const char* fn) {
     set_error("%s: page storage must be 16-byte aligned", fn);
     return TQ_ERR_INVALID;
   }
+  if (c->block_table &&
+      (c->block_table_stride < c->pages_per_stream || c->num_blocks <= 0 ||
+       reinterpret_cast<uintptr_t>(c->block_table) % 4)) {
+    set_error("%s: block table needs stride >= pages_per_stream (%lld), num_blocks > 0 and "
+              "4-byte alignment", fn, (long long)c->pages_per_stream);
+    return TQ_ERR_INVALID;
+  }
   return TQ_OK;
 }
 

@@ -45,6 +45,29 @@ __host__ __device__ inline PageGeom make_geom(int D, int kb, int vb, int qjl) {
   return g;
 }
 
+// Pool slot of logical page `pg` of stream `s`: contiguous (s * pps + pg) or
+// through a block table.  `ok` is false for an entry outside the pool; the
+// caller then reads slot 0 / drops the write and flags TQ_DEV_BAD_BLOCK.
+struct PageMap {
+  int64_t pps;                 // pages per stream (contiguous layout)
+  const int32_t* bt;           // block table or nullptr
+  int64_t bt_stride, nblocks;
+};
+__host__ __device__ inline PageMap page_map(const tq_cache* c) {
+  PageMap m;
+  m.pps = c->pages_per_stream;
+  m.bt = c->block_table;
+  m.bt_stride = c->block_table_stride;
+  m.nblocks = c->num_blocks;
+  return m;
+}
+__device__ __forceinline__ int64_t page_slot(const PageMap& m, int64_t s, int64_t pg, bool& ok) {
+  if (m.bt == nullptr) { ok = true; return s * m.pps + pg; }
+  const int64_t slot = __ldg(m.bt + s * m.bt_stride + pg);
+  ok = slot >= 0 && slot < m.nblocks;
+  return ok ? slot : 0;
+}
+
 // Position of coordinate `coord` in the quad order of a K row.
 __host__ __device__ inline int k_pos_of(int coord, int D) {
   int j = coord >> 4, r = coord & 15;

@@ -40,7 +40,7 @@ constexpr float kNegInf = -INFINITY;
 
 struct DecodeParams {
   const uint8_t* pages;
-  int64_t pages_per_stream;
+  PageMap pm;
   int64_t S, Pv, T, Q;
   int nch, maxslot;
   const uint32_t* qf;    // [S][nch][8][D/2] half2
@@ -314,7 +314,10 @@ decode_kernel(DecodeParams p) {
         if (s_abort) break;
         const int64_t gpi = gp0 + i;
         const int64_t s = gpi / p.Pv, pg = gpi - s * p.Pv;
-        const uint8_t* src = p.pages + (s * p.pages_per_stream + pg) * (int64_t)G::PAGE;
+        bool pok;
+        const int64_t ps = page_slot(p.pm, s, pg, pok);
+        if (!pok) atomicOr(p.status, TQ_DEV_BAD_BLOCK);
+        const uint8_t* src = p.pages + ps * (int64_t)G::PAGE;
         mbar_expect_tx(&full[st], (uint32_t)G::PAGE);
         bulk_g2s(smem + G::STAGE0 + st * G::PB, src, (uint32_t)G::PAGE, &full[st]);
         issued = k + 1;
@@ -658,7 +661,8 @@ struct PrepParams {
   PageGeom g;
   const float* kc; const float* kb; const float* vc; const float* vb;
   const void* kx; const void* vx; int k_dtype, v_dtype; int64_t ks[4], vs[4];
-  uint8_t* pages; int64_t pages_per_stream; int64_t pos;
+  uint8_t* pages; PageMap pm; int64_t pos;
+  uint32_t* status;
 };
 
 constexpr int kPrepThreads = 256;
@@ -785,9 +789,15 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
       so[i] = pack_half2(xs[hl * D + 2 * c2] * p.scale_s, xs[hl * D + 2 * c2 + 1] * p.scale_s);
     }
   }
+  bool page_ok = true;
+  int64_t pslot = 0;
   if (app) {
+    pslot = page_slot(pp.pm, s, pp.pos / kPageTokens, page_ok);
+    if (!page_ok && tid == 0) atomicOr(pp.status, TQ_DEV_BAD_BLOCK);
+  }
+  if (app && page_ok) {
     const int64_t t = pp.pos;
-    uint8_t* page = pp.pages + (s * pp.pages_per_stream + t / kPageTokens) * (int64_t)g.page_bytes;
+    uint8_t* page = pp.pages + pslot * (int64_t)g.page_bytes;
     const int slot = (int)(t % kPageTokens);
     const int kw = g.krow / 4, vw = g.vrow / 4, qw = qjl ? D / 32 : 0;
     for (int i = tid; i < kw + vw + qw; i += kPrepThreads) {
@@ -1154,7 +1164,8 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
     pp.vc = t->v_centroids; pp.vb = t->v_boundaries;
     pp.kx = pp.vx = nullptr; pp.k_dtype = pp.v_dtype = 0;
     for (int i = 0; i < 4; ++i) pp.ks[i] = pp.vs[i] = 0;
-    pp.pages = c->pages; pp.pages_per_stream = c->pages_per_stream; pp.pos = 0;
+    pp.pages = c->pages; pp.pm = page_map(c); pp.pos = 0;
+    pp.status = reinterpret_cast<uint32_t*>(ws);
     if (step) {
       pp.kx = step->k->data; pp.vx = step->v->data;
       pp.k_dtype = step->k->dtype; pp.v_dtype = step->v->dtype;
@@ -1174,7 +1185,7 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   }
 
   DecodeParams dp;
-  dp.pages = c->pages; dp.pages_per_stream = c->pages_per_stream;
+  dp.pages = c->pages; dp.pm = page_map(c);
   dp.S = pl.S; dp.Pv = pl.Pv; dp.T = pl.T; dp.Q = pl.Q;
   dp.nch = pl.nch; dp.maxslot = pl.maxslot;
   dp.qf = qp.qf; dp.sqf = qp.sqf;

@@ -34,7 +34,7 @@ constexpr float kLog2eP = 1.4426950408889634f;
 
 struct PrefillParams {
   const uint8_t* pages;
-  int64_t pages_per_stream;
+  PageMap pm;
   int page_bytes, page_pitch, off_v, off_kn, off_vn;   // page geometry (make_geom)
   const __half* rot_h;          // R [D][D] fp16, row-major
   const float* kc;
@@ -136,11 +136,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(PrefillParams p)
     lutv[i] = __float2half_rn(i < (1 << VB) ? __ldg(p.vc + i) : 0.f);
   }
   __syncthreads();
-  const uint8_t* spages = p.pages + stream * p.pages_per_stream * (int64_t)PAGE;
+  // pool address of this stream's page pg (block table or contiguous)
+  auto page_src = [&](int64_t pg) -> const uint8_t* {
+    bool ok;
+    const int64_t ps = page_slot(p.pm, stream, pg, ok);
+    if (!ok) atomicOr(p.status, TQ_DEV_BAD_BLOCK);
+    return p.pages + ps * (int64_t)PAGE;
+  };
   if (tid == 0) {
     for (int i = 0; i < 2 && i < ntiles; ++i) {
       mbar_expect_tx(&full[i], PAGE);
-      bulk_g2s(smem + G::OFF_STG + i * p.page_pitch, spages + (int64_t)i * PAGE, PAGE, &full[i]);
+      bulk_g2s(smem + G::OFF_STG + i * p.page_pitch, page_src(i), PAGE, &full[i]);
     }
   }
 
@@ -254,7 +260,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(PrefillParams p)
     // the stage is decoded: refill it with page kt + 2
     if (tid == 0 && kt + 2 < ntiles) {
       mbar_expect_tx(&full[st], PAGE);
-      bulk_g2s(smem + G::OFF_STG + st * p.page_pitch, spages + (int64_t)(kt + 2) * PAGE, PAGE,
+      bulk_g2s(smem + G::OFF_STG + st * p.page_pitch, page_src(kt + 2), PAGE,
                &full[st]);
     }
 
@@ -419,7 +425,7 @@ int launch_prefill(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   PrefillParams p;
   const PageGeom g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
   p.pages = c->pages;
-  p.pages_per_stream = c->pages_per_stream;
+  p.pm = page_map(c);
   p.page_bytes = g.page_bytes;
   p.page_pitch = (g.page_bytes + 127) & ~127;
   p.off_v = g.off_v;

@@ -518,7 +518,10 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
     // ================================================================ decoders
     const int dt = tid - 32 * (1 + kSoftWarps);
     TcParamsView pv;
-    pv.spages = p.pages + stream * p.pages_per_stream * (int64_t)p.page_bytes;
+    pv.pool = p.pages;
+    pv.pm = p.pm;
+    pv.stream = stream;
+    pv.status = p.status;
     pv.page_bytes = p.page_bytes;
     pv.off_v = p.off_v;
     pv.off_kn = p.off_kn;
@@ -663,7 +666,7 @@ int launch_prefill_tc(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   const PageGeom g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
   TcPrefillParams p;
   p.pages = c->pages;
-  p.pages_per_stream = c->pages_per_stream;
+  p.pm = page_map(c);
   p.page_bytes = g.page_bytes;
   p.off_v = g.off_v;
   p.off_kn = g.off_kn;

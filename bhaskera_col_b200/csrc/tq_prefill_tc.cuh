@@ -27,7 +27,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 struct TcPrefillParams {
   const uint8_t* pages;
-  int64_t pages_per_stream;
+  PageMap pm;
   int page_bytes, off_v, off_kn, off_vn;
   const __half* rot_h;          // R [128][128] fp16, row-major
   const float* rot;             // R [128][128] fp32, row-major
@@ -259,7 +259,10 @@ __device__ __forceinline__ void decode_stream(const Stream<NB>& s, const unsigne
 }
 
 struct TcParamsView {
-  const uint8_t* spages;        // this stream's pages
+  const uint8_t* pool;          // the pages (contiguous streams or a block pool)
+  PageMap pm;
+  int64_t stream;
+  uint32_t* status;             // TQ_DEV_BAD_BLOCK on a block-table entry outside the pool
   int page_bytes, off_v, off_kn, off_vn;
   int kk, part;
   int64_t kend;                 // keys this CTA needs
@@ -278,12 +281,23 @@ template <int NB, int NR>
 __device__ __forceinline__ void load_half(HalfRegs<NB, NR>& t, const TcParamsView& pv, int j,
                                           int off_codes, int off_norm) {
   constexpr int RPP = NR / 2, STEP = 64 / RPP;
+  const uint8_t* pgs[2];
+#pragma unroll
+  for (int pgi = 0; pgi < 2; ++pgi) {
+    pgs[pgi] = pv.pool;
+    if ((int64_t)j * kKeys + pgi * 64 < pv.kend) {     // the page holds needed keys
+      bool ok;
+      const int64_t ps = page_slot(pv.pm, pv.stream, 2 * (int64_t)j + pgi, ok);
+      if (!ok) atomicOr(pv.status, TQ_DEV_BAD_BLOCK);
+      pgs[pgi] = pv.pool + ps * (int64_t)pv.page_bytes;
+    }
+  }
 #pragma unroll
   for (int r = 0; r < NR; ++r) {
     const int pgi = r / RPP, key_in_page = pv.kk + STEP * (r % RPP);
     const int64_t key = (int64_t)j * kKeys + pgi * 64 + key_in_page;
     if (key < pv.kend) {
-      const uint8_t* pg = pv.spages + (int64_t)(2 * j + pgi) * pv.page_bytes;
+      const uint8_t* pg = pgs[pgi];
       load_stream<NB>(t.c[r], pg + off_codes + key_in_page * (16 * NB) + pv.part * (4 * NB));
       t.n[r] = __ldg(reinterpret_cast<const unsigned short*>(pg + off_norm) + key_in_page);
     } else {

@@ -478,7 +478,10 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
     // ================================================================ decoders
     const int dt = tid - 32 * (1 + kSoftWarps);
     TcParamsView pv;
-    pv.spages = p.pages + stream * p.pages_per_stream * (int64_t)p.page_bytes;
+    pv.pool = p.pages;
+    pv.pm = p.pm;
+    pv.stream = stream;
+    pv.status = p.status;
     pv.page_bytes = p.page_bytes;
     pv.off_v = p.off_v;
     pv.off_kn = p.off_kn;

@@ -133,7 +133,44 @@ def page_bytes(head_dim: int, key_bits: int, value_bits: int, qjl: bool) -> int:
     return _lib.PAGE_TOKENS * (krow + vrow + qrow + 4 + (2 if qjl else 0))
 
 
-def _cache_desc(pages: torch.Tensor) -> _lib.Cache:
+@dataclass
+class PagedPages:
+    """Paged storage (vLLM-style): a pool of pages and one block table row per
+    stream; logical page p of stream s is pool[block_table[s, p]].  Accepted
+    wherever a contiguous (streams, pages, page_bytes) tensor is.  Entries
+    outside the pool are never dereferenced: the kernels read pool page 0 /
+    drop the write and set _lib.DEV_BAD_BLOCK in the device status word."""
+    pool: torch.Tensor          # uint8 (num_blocks, page_bytes)
+    block_table: torch.Tensor   # int32 (streams, max_pages)
+
+    def __post_init__(self):
+        if self.pool.dtype != torch.uint8 or self.pool.dim() != 2:
+            raise ValueError("pool must be uint8 (num_blocks, page_bytes)")
+        if self.block_table.dtype != torch.int32 or self.block_table.dim() != 2 or \
+                self.block_table.stride(1) != 1:
+            raise ValueError("block_table must be int32 (streams, max_pages), rows contiguous")
+        if self.block_table.device != self.pool.device:
+            raise ValueError("pool and block_table must be on the same device")
+
+    @property
+    def is_cuda(self) -> bool:
+        return self.pool.is_cuda
+
+    @property
+    def device(self) -> torch.device:
+        return self.pool.device
+
+    @property
+    def shape(self):
+        """(streams, pages per stream, page_bytes), as a contiguous page tensor."""
+        return (self.block_table.shape[0], self.block_table.shape[1], self.pool.shape[1])
+
+
+def _cache_desc(pages) -> _lib.Cache:
+    if isinstance(pages, PagedPages):
+        bt = pages.block_table
+        return _lib.Cache(pages.pool.data_ptr(), bt.shape[0], bt.shape[1], bt.data_ptr(),
+                          bt.stride(0), pages.pool.shape[0])
     return _lib.Cache(pages.data_ptr(), pages.shape[0], pages.shape[1])
 
 

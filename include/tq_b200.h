@@ -61,6 +61,7 @@ extern "C" {
 
 /* device status word bits (written by kernels into the workspace) */
 #define TQ_DEV_WAIT_TIMEOUT 1u  /* a bounded mbarrier wait ran out          */
+#define TQ_DEV_BAD_BLOCK 2u     /* a block-table entry was outside the pool */
 
 typedef struct tq_geom {
   int32_t head_dim;    /* D: multiple of 32, 32..256                        */
@@ -92,9 +93,18 @@ typedef struct tq_tables {
 
 /* Packed cache of one layer. */
 typedef struct tq_cache {
-  uint8_t* pages;             /* [streams][pages_per_stream][page_bytes]     */
+  uint8_t* pages;             /* [streams][pages_per_stream][page_bytes], or
+                                 with a block table a pool of num_blocks pages */
   int64_t streams;            /* B * Hkv                                     */
-  int64_t pages_per_stream;   /* capacity in pages                           */
+  int64_t pages_per_stream;   /* capacity in pages (logical, per stream)     */
+  /* Optional paged layout (vLLM-style block tables): logical page p of stream
+   * s lives at pool page block_table[s * block_table_stride + p].  NULL: the
+   * contiguous layout above.  Entries outside [0, num_blocks) are never
+   * dereferenced: reads take pool page 0, writes are dropped, and
+   * TQ_DEV_BAD_BLOCK is set in the status word. */
+  const int32_t* block_table;
+  int64_t block_table_stride; /* >= pages_per_stream                          */
+  int64_t num_blocks;         /* pages in the pool                            */
 } tq_cache;
 
 /* A strided 4-d tensor view (B, H, T, D); strides in elements. */

@@ -96,3 +96,38 @@ def test_quantize_argument_validation():
     assert rc == _lib.TQ_ERR_INVALID
     rc = lib.tq_quantize_rotated(16, 10, 16, 300, 16, None)
     assert rc == _lib.TQ_ERR_INVALID
+
+
+def test_block_table_validation():
+    lib = _lib.load()
+    g = _geom(q=0)
+    t = _lib.Tables(*([16] * 10))
+    k = _lib.Tensor4(16, _lib.TQ_BF16, (ctypes.c_int64 * 4)(1, 2, 5, 128),
+                     (ctypes.c_int64 * 4)(1280, 640, 128, 1))
+    bad = [_lib.Cache(1024, 2, 4, 1024, 3, 16),      # stride below pages_per_stream
+           _lib.Cache(1024, 2, 4, 1024, 4, 0),       # empty pool
+           _lib.Cache(1024, 2, 4, 1026, 4, 16)]      # misaligned table
+    for c in bad:
+        rc = lib.tq_append(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(k),
+                           ctypes.byref(k), 0, None)
+        assert rc == _lib.TQ_ERR_INVALID and "block table" in _lib.last_error()
+
+
+def test_paged_pages_holder():
+    import torch
+    from bhaskera_col_b200.inference import ops
+    pool = torch.zeros((10, 64), dtype=torch.uint8)
+    bt = torch.zeros((3, 6), dtype=torch.int32)[:, :4]
+    pp = ops.PagedPages(pool, bt)
+    assert pp.shape == (3, 4, 64) and not pp.is_cuda
+    c = ops._cache_desc(pp)
+    assert (c.streams, c.pages_per_stream, c.block_table_stride, c.num_blocks) == (3, 4, 6, 10)
+    assert c.block_table == bt.data_ptr() and c.pages == pool.data_ptr()
+    with pytest.raises(ValueError):
+        ops.PagedPages(pool.float(), bt)
+    with pytest.raises(ValueError):
+        ops.PagedPages(pool, bt.long())
+    with pytest.raises(ValueError):
+        ops.PagedPages(pool, torch.zeros((4, 3), dtype=torch.int32).t())
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.append(None, pp, torch.zeros(1), torch.zeros(1), 0)
