@@ -78,7 +78,8 @@ class DecodeArgs(ctypes.Structure):
                 ("window_k", ctypes.POINTER(Tensor4)), ("window_v", ctypes.POINTER(Tensor4)),
                 ("n_tokens", ctypes.c_int64), ("num_q_heads", ctypes.c_int64),
                 ("scale", ctypes.c_float), ("num_ctas", ctypes.c_int32),
-                ("phases", ctypes.c_int32), ("gather", ctypes.POINTER(Gather))]
+                ("phases", ctypes.c_int32), ("gather", ctypes.POINTER(Gather)),
+                ("seq_lens", ctypes.c_void_p)]
 
 
 class PrefillArgs(ctypes.Structure):

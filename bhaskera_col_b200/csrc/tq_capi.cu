@@ -257,6 +257,16 @@ static int check_decode(const tq_geom* g, const tq_tables* t, const tq_cache* c,
     set_error("%s: window_k and window_v must both be given or both be NULL", fn);
     return TQ_ERR_INVALID;
   }
+  if (a->seq_lens) {
+    if (reinterpret_cast<uintptr_t>(a->seq_lens) % 4) {
+      set_error("%s: seq_lens must be 4-byte aligned", fn);
+      return TQ_ERR_INVALID;
+    }
+    if (a->phases != 0 && !(a->phases & TQ_PHASE_QPREP)) {
+      set_error("%s: seq_lens needs the query-preparation phase (it lays out the pages)", fn);
+      return TQ_ERR_INVALID;
+    }
+  }
   if (a->gather) {
     const tq_gather* gt = a->gather;
     if (gt->world < 1 || gt->world > TQ_MAX_PEERS || gt->rank < 0 || gt->rank >= gt->world) {

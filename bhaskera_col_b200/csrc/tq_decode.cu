@@ -38,18 +38,60 @@ constexpr int kTileWarps = 4;     // warps sharing one 64-token page (16 tokens 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegInf = -INFINITY;
 
+// Which pages a decode walks.  Stream s owns the compacted page range
+// [start(s), start(s + 1)): s * Pv for a uniform batch, and for a ragged one
+// (per-row token counts) the prefix sums the query preparation lays out.
+// CTA c takes compacted pages [c * Q, (c + 1) * Q).
+struct PageLayout {
+  int64_t S, Pv, T, Q;    // streams, pages and tokens per stream (bounds), pages per CTA
+  int hkv;                // streams per batch row
+  int64_t nid;            // partial-result ids per head chunk: CTAs + S
+  const int32_t* lens;    // [B] tokens of each batch row; NULL: uniform (T each)
+  int32_t* cum;           // [S + 1] ragged: first compacted page of each stream
+  int32_t* rq;            // ragged: pages per CTA
+};
+
+__device__ __forceinline__ int64_t lay_start(const PageLayout& L, int64_t s) {
+  return L.lens ? (int64_t)__ldcg(L.cum + s) : s * L.Pv;
+}
+
+__device__ __forceinline__ int lay_tokens(const PageLayout& L, int64_t s) {
+  if (!L.lens) return (int)L.T;
+  const int64_t n = __ldg(L.lens + s / L.hkv);
+  return (int)(n < 0 ? 0 : n > L.T ? L.T : n);
+}
+
+// The stream owning compacted page x (< cum[S]): the largest s with
+// cum[s] <= x, found by a 32-way search of the whole warp (two rounds up to
+// 1,024 streams).  Invariant: cum[lo] <= x < cum[hi] (cum[S] is the total).
+__device__ __forceinline__ int64_t find_stream(const int32_t* cum, int64_t S, int64_t x, int lane) {
+  int64_t lo = 0, hi = S;
+  while (hi - lo > 1) {
+    const int64_t step = (hi - lo + 31) / 32;
+    const int64_t i = lo + lane * step;
+    const bool le = i < hi && (int64_t)__ldcg(cum + i) <= x;
+    const unsigned m = __ballot_sync(0xffffffffu, le);
+    lo += (31 - __clz(m)) * step;
+    hi = tmin<int64_t>(hi, lo + step);
+  }
+  return lo;
+}
+
 struct DecodeParams {
   const uint8_t* pages;
   PageMap pm;
-  int64_t S, Pv, T, Q;
-  int nch, maxslot;
+  PageLayout lay;
+  int nch;
   const uint32_t* qf;    // [S][nch][8][D/2] half2
   const uint32_t* sqf;   // [S][nch][8][D/2] half2
   const float* kc;
   const float* vc;
-  float* part_m;         // [S][nch*8][maxslot]
+  // partial results of segment (CTA c, stream s) under id c + s: the id
+  // grows along every CTA's walk and from one CTA to the next, so ids of
+  // different segments never meet
+  float* part_m;         // [nch][nid][8]
   float* part_l;
-  float* part_o;         // [S][nch*8][maxslot][D]
+  float* part_o;         // [nch][nid][8][D]
   uint32_t* status;
 };
 
@@ -269,11 +311,7 @@ decode_kernel(DecodeParams p) {
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hc = blockIdx.y;
-  const int64_t TP = p.S * p.Pv;
-  const int64_t gp0 = (int64_t)blockIdx.x * p.Q;
-  const int64_t gp1 = tmin<int64_t>(gp0 + p.Q, TP);
-  const int npages = (int)tmax<int64_t>(0, gp1 - gp0);
-  const int T32 = (int)p.T, Pv32 = (int)p.Pv;   // token and page indices fit 32 bits
+  const PageLayout& L = p.lay;
   constexpr int NCT = 32 * kConsumerWarps;   // consumer threads
 
   if (tid == 0) {
@@ -294,7 +332,14 @@ decode_kernel(DecodeParams p) {
     }
   }
   __syncthreads();
-  pdl_wait();   // pages and query fragments come from the preceding kernels
+  pdl_wait();   // pages, query fragments and a ragged layout come from the preceding kernels
+
+  const int64_t Q = L.lens ? (int64_t)__ldcg(L.rq) : L.Q;
+  const int64_t total = L.lens ? (int64_t)__ldcg(L.cum + L.S) : L.S * L.Pv;
+  const int64_t gp0 = (int64_t)blockIdx.x * Q;
+  const int npages = (int)tmax<int64_t>(0, tmin<int64_t>(gp0 + Q, total) - gp0);
+  int64_t s_first = 0;                           // the stream of page gp0 (warp-uniform)
+  if (npages > 0) s_first = L.lens ? find_stream(L.cum, L.S, gp0, lane) : gp0 / L.Pv;
 
   // ------------------------------------------------------------ producer
   // Lane g feeds page group g (pages i = g, g + NG, ...) through its own ring
@@ -303,6 +348,7 @@ decode_kernel(DecodeParams p) {
     if (lane < G::NG) {
       const int gr = lane;
       int issued = 0;
+      int64_t sp = s_first, sp0 = lay_start(L, sp);   // stream of the lane's page, its start
       for (int i = gr, k = 0; i < npages; i += G::NG, ++k) {
         const int st = gr * G::SG + k % G::SG;
         if (k >= G::SG && !s_abort) {
@@ -313,9 +359,12 @@ decode_kernel(DecodeParams p) {
         }
         if (s_abort) break;
         const int64_t gpi = gp0 + i;
-        const int64_t s = gpi / p.Pv, pg = gpi - s * p.Pv;
+        for (int64_t nx = lay_start(L, sp + 1); nx <= gpi; nx = lay_start(L, sp + 1)) {
+          ++sp;                                  // gpi < total, so this stops before S
+          sp0 = nx;
+        }
         bool pok;
-        const int64_t ps = page_slot(p.pm, s, pg, pok);
+        const int64_t ps = page_slot(p.pm, sp, gpi - sp0, pok);
         if (!pok) atomicOr(p.status, TQ_DEV_BAD_BLOCK);
         const uint8_t* src = p.pages + ps * (int64_t)G::PAGE;
         mbar_expect_tx(&full[st], (uint32_t)G::PAGE);
@@ -362,14 +411,17 @@ decode_kernel(DecodeParams p) {
   // Segments are the runs of one stream's pages in this CTA's range; each
   // warp takes its group's pages of a segment, then all consumer warps
   // combine their partial results for the segment.
-  int64_t s = gp0 / p.Pv;                       // stream of the segment
-  int pg0 = (int)(gp0 - s * p.Pv);              // its first page
+  int64_t s = s_first;                          // stream of the segment
+  int64_t st0 = lay_start(L, s);                // its first compacted page
+  int pg0 = (int)(gp0 - st0);                   // the segment's first page in the stream
   int i0 = 0;                                   // CTA-relative index of that page
   int inext = grp;                              // next page of this warp's group
   int ring = 0;                                 // position in the group's stage ring
   uint32_t phase = 0;
   while (i0 < npages) {
-    const int i1 = tmin(npages, i0 + (Pv32 - pg0));   // the segment: pages [i0, i1)
+    const int64_t st1 = lay_start(L, s + 1);
+    const int i1 = (int)tmin<int64_t>(npages, i0 + (st1 - st0 - pg0));   // pages [i0, i1)
+    const int Ts = lay_tokens(L, s);            // valid tokens of the stream
     if (inext < i1) load_q(s);
     for (; inext < i1; inext += G::NG) {
       const int st = grp * G::SG + ring;
@@ -381,7 +433,7 @@ decode_kernel(DecodeParams p) {
       const uint8_t* pgb = smem + G::STAGE0 + st * G::PB;
       const int tok0 = pg * kPageTokens + tw * 16;
 
-      if (tok0 < T32) {
+      if (tok0 < Ts) {
         // ---------------- scores: S^T tile (16 tokens x 8 heads) --------------
         const int r0 = tw * 16 + gq, r1 = r0 + 8;
         uint32_t wk0[KQW], wk1[KQW];
@@ -433,7 +485,7 @@ decode_kernel(DecodeParams p) {
         }
         const __half* kn = reinterpret_cast<const __half*>(pgb + G::OFF_KN);
         const __half* vn = reinterpret_cast<const __half*>(pgb + G::OFF_VN);
-        const bool ok0 = tok0 + gq < T32, ok1 = tok0 + gq + 8 < T32;
+        const bool ok0 = tok0 + gq < Ts, ok1 = tok0 + gq + 8 < Ts;
         const float n0 = __half2float(kn[r0]), n1 = __half2float(kn[r1]);
         float s00 = acc[0] * n0, s01 = acc[1] * n0, s10 = acc[2] * n1, s11 = acc[3] * n1;
         if constexpr (QJL) {
@@ -596,8 +648,7 @@ decode_kernel(DecodeParams p) {
         co[(2 * tq + 1) * D + 16 * i2 + gq + 8] = O[i2][3];
       }
       named_bar(1, NCT);
-      const int64_t first = (s * p.Pv) / p.Q;
-      const int slot = (int)(blockIdx.x - first);
+      const int64_t hrow0 = ((int64_t)hc * L.nid + blockIdx.x + s) * 8;
       for (int idx = tid; idx < 8 * D; idx += NCT) {
         const int h = idx / D, d = idx % D;
         float M = kNegInf;
@@ -613,11 +664,11 @@ decode_kernel(DecodeParams p) {
             Osum = fmaf(wt, cw[16 + h * D + d], Osum);
           }
         }
-        const int64_t hrow = (s * p.nch + hc) * 8 + h;
-        p.part_o[(hrow * p.maxslot + slot) * D + d] = Osum;
+        const int64_t hrow = hrow0 + h;
+        p.part_o[hrow * D + d] = Osum;
         if (d == 0) {
-          p.part_m[hrow * p.maxslot + slot] = M;
-          p.part_l[hrow * p.maxslot + slot] = Lsum;
+          p.part_m[hrow] = M;
+          p.part_l[hrow] = Lsum;
         }
       }
       named_bar(1, NCT);
@@ -631,8 +682,11 @@ decode_kernel(DecodeParams p) {
       reset_state();
     }
     i0 = i1;
-    ++s;
     pg0 = 0;
+    st0 = st1;
+    ++s;
+    // a ragged batch may hold empty streams: step to the next one with pages
+    while (i0 < npages && lay_start(L, s + 1) == st0) ++s;
   }
 }
 
@@ -663,9 +717,55 @@ struct PrepParams {
   const void* kx; const void* vx; int k_dtype, v_dtype; int64_t ks[4], vs[4];
   uint8_t* pages; PageMap pm; int64_t pos;
   uint32_t* status;
+  PageLayout lay;        // ragged (lay.lens set): store at row length - 1, lay out the pages
+  int ctas;              // the decode's grid
 };
 
 constexpr int kPrepThreads = 256;
+
+// Ragged page layout, by all threads of one CTA: cum[s] = compacted pages of
+// the streams before s, cum[S] = all pages, *rq = pages per CTA (at least
+// Pv / (kMaxSlots - 1), so no stream has more segments than the merge's slot
+// table).  Each thread sums a run of rows; the run totals are scanned by warp
+// shuffles.
+constexpr int kMaxSlots = 64;
+
+__device__ __noinline__ void ragged_layout(const PageLayout L, int ctas, int tid) {
+  __shared__ int64_t s_warp[kPrepThreads / 32];
+  const int lane = tid & 31, warp = tid >> 5;
+  const int64_t B = L.S / L.hkv;
+  const int64_t run = (B + kPrepThreads - 1) / kPrepThreads;
+  const int64_t b0 = tmin<int64_t>(B, tid * run), b1 = tmin<int64_t>(B, b0 + run);
+  auto row_pages = [&](int64_t b) {
+    return ((int64_t)lay_tokens(L, b * L.hkv) + kPageTokens - 1) / kPageTokens;
+  };
+  int64_t mine = 0;
+  for (int64_t b = b0; b < b1; ++b) mine += row_pages(b) * L.hkv;
+  int64_t incl = mine;                            // inclusive scan within the warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  int64_t before = incl - mine, all = 0;
+  for (int w = 0; w < kPrepThreads / 32; ++w) {
+    if (w < warp) before += s_warp[w];
+    all += s_warp[w];
+  }
+  for (int64_t b = b0; b < b1; ++b) {
+    const int64_t pg = row_pages(b);
+    for (int h = 0; h < L.hkv; ++h) L.cum[b * L.hkv + h] = (int32_t)(before + h * pg);
+    before += pg * L.hkv;
+  }
+  if (tid == 0) {
+    L.cum[L.S] = (int32_t)all;
+    const int64_t q = tmax<int64_t>(tmax<int64_t>((all + ctas - 1) / tmax(ctas, 1), 1),
+                                    (L.Pv + kMaxSlots - 2) / (kMaxSlots - 1));
+    *L.rq = (int32_t)q;
+  }
+}
 
 template <int D>
 struct PrepSmem {
@@ -791,12 +891,13 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   }
   bool page_ok = true;
   int64_t pslot = 0;
-  if (app) {
-    pslot = page_slot(pp.pm, s, pp.pos / kPageTokens, page_ok);
+  // a ragged row stores its token at its length - 1 (not at all when empty)
+  const int64_t t = pp.lay.lens ? (int64_t)lay_tokens(pp.lay, s) - 1 : pp.pos;
+  if (app && t >= 0) {
+    pslot = page_slot(pp.pm, s, t / kPageTokens, page_ok);
     if (!page_ok && tid == 0) atomicOr(pp.status, TQ_DEV_BAD_BLOCK);
   }
-  if (app && page_ok) {
-    const int64_t t = pp.pos;
+  if (app && t >= 0 && page_ok) {
     uint8_t* page = pp.pages + pslot * (int64_t)g.page_bytes;
     const int slot = (int)(t % kPageTokens);
     const int kw = g.krow / 4, vw = g.vrow / 4, qw = qjl ? D / 32 : 0;
@@ -817,6 +918,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
       if (qjl) reinterpret_cast<__half*>(page + g.off_kr)[slot] = __float2half_rn(nrm[2]);
     }
   }
+  if (pp.lay.lens && blockIdx.x == 0 && blockIdx.y == 0) ragged_layout(pp.lay, pp.ctas, tid);
 }
 
 // ---------------------------------------------------------------------------
@@ -824,8 +926,8 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
 // grid = (S, nch), 128 threads
 // ---------------------------------------------------------------------------
 struct MergeParams {
-  int D, g, Hkv, nch, maxslot;
-  int64_t Pv, Q;
+  int D, g, Hkv, nch;
+  PageLayout lay;
   const float* part_m; const float* part_l; const float* part_o;
   const float* R;
   const void* q; int q_dtype; int64_t q_stride[4];
@@ -840,7 +942,6 @@ struct MergeParams {
   uint32_t* status;
 };
 
-constexpr int kMaxSlots = 64;
 constexpr int kMergeThreads = 256;
 constexpr int kSlotChunk = 8;
 
@@ -864,15 +965,24 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int NWARP = kMergeThreads / 32;
   const int nh = tmin(8, p.g - hc * 8);
-  int nslot = 0;
-  if (p.Pv > 0) {
-    const int64_t first = (s * p.Pv) / p.Q, last = ((s + 1) * p.Pv - 1) / p.Q;
-    nslot = (int)(last - first + 1);
-  }
-  const int64_t hrow0 = (s * p.nch + hc) * 8;
   stage_async(rs, p.R, D * D * 4, tid, kMergeThreads);
   pdl_launch_dependents();
   pdl_wait();
+  // the stream's segments: CTAs first .. last of the decode, ids first + s ..
+  int nslot = 0;
+  int64_t hrow0 = 0;                               // (chunk, id) row of the first segment, x 8
+  {
+    const PageLayout& L = p.lay;
+    const int64_t Q = L.lens ? (int64_t)__ldcg(L.rq) : L.Q;
+    const int64_t a0 = lay_start(L, s), a1 = lay_start(L, s + 1);
+    if (a1 > a0) {
+      const int64_t first = a0 / Q;
+      // <= kMaxSlots: Q >= Pv / (kMaxSlots - 1) on both layouts (the clamp
+      // only keeps the slot table in bounds)
+      nslot = tmin((int)((a1 - 1) / Q - first + 1), kMaxSlots);
+      hrow0 = ((int64_t)hc * L.nid + first + s) * 8;
+    }
+  }
 
   // --- window scores (unrotated), all heads --------------------------------
   if (W > 0) {
@@ -904,7 +1014,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
     const int h = warp;
     float M = kNegInf;
     if (h < nh) {
-      for (int k = lane; k < nslot; k += 32) M = fmaxf(M, p.part_m[(hrow0 + h) * p.maxslot + k]);
+      for (int k = lane; k < nslot; k += 32) M = fmaxf(M, p.part_m[hrow0 + 8 * k + h]);
       for (int64_t t = lane; t < W; t += 32) M = fmaxf(M, sc[h * W + t]);
     }
 #pragma unroll
@@ -912,10 +1022,10 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
     const float Ms = M == kNegInf ? 0.f : M;
     float L = 0.f;
     for (int k = lane; k < nslot; k += 32) {
-      const float mk = p.part_m[(hrow0 + h) * p.maxslot + k];
+      const float mk = p.part_m[hrow0 + 8 * k + h];
       const float wt = (h < nh && mk != kNegInf) ? exp2f(mk - Ms) : 0.f;
       s_wt[h][k] = wt;
-      L = fmaf(wt, p.part_l[(hrow0 + h) * p.maxslot + k], L);
+      L = fmaf(wt, p.part_l[hrow0 + 8 * k + h], L);
     }
     for (int64_t t = lane; t < W; t += 32) {
       const float e = h < nh ? exp2f(sc[h * W + t] - Ms) : 0.f;
@@ -931,9 +1041,8 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   float acc[OUT] = {0.f, 0.f, 0.f, 0.f};
   for (int k0 = 0; k0 < nslot; k0 += kSlotChunk) {
     const int kn = tmin(kSlotChunk, nslot - k0);
-    for (int h = 0; h < 8; ++h)
-      stage_async(po + h * kSlotChunk * D, p.part_o + ((hrow0 + h) * p.maxslot + k0) * D,
-                  kn * D * 4, tid, kMergeThreads);
+    // slots k0 .. k0 + kn - 1 of all 8 heads are one run: po[k][h][D]
+    stage_async(po, p.part_o + (hrow0 + 8 * k0) * D, kn * 8 * D * 4, tid, kMergeThreads);
     cp_async_wait_all();
     __syncthreads();
 #pragma unroll
@@ -941,7 +1050,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
       const int i = tid + r * kMergeThreads;
       if (i < 8 * D) {
         const int h = i / D, d = i % D;
-        for (int k = 0; k < kn; ++k) acc[r] = fmaf(s_wt[h][k0 + k], po[(h * kSlotChunk + k) * D + d], acc[r]);
+        for (int k = 0; k < kn; ++k) acc[r] = fmaf(s_wt[h][k0 + k], po[(k * 8 + h) * D + d], acc[r]);
       }
     }
     __syncthreads();
@@ -1030,10 +1139,14 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
 // ---------------------------------------------------------------------------
 namespace {
 
+// Workspace: [0, 4) the status word, [64, 68) a ragged batch's pages per
+// CTA, then the query fragments, the partials and a ragged page layout.
+constexpr size_t kWsRaggedQ = 64;
+
 struct Plan {
-  int D, g, nch, maxslot, ctas;
-  int64_t S, Pv, T, Q;
-  size_t off_qf, off_sqf, off_m, off_l, off_o, total;
+  int D, g, nch, ctas;
+  int64_t S, Pv, T, Q, nid;
+  size_t off_qf, off_sqf, off_m, off_l, off_o, off_cum, total;
 };
 
 using DecodeFn = void (*)(DecodeParams);
@@ -1086,16 +1199,20 @@ Plan make_plan(const tq_geom* G, const tq_cache* c, const tq_decode_args* a, int
   // every stream's partials must fit the merge kernel's slot table
   if (pl.Pv > 0) pl.Q = tmax<int64_t>(pl.Q, (pl.Pv + kMaxSlots - 2) / (kMaxSlots - 1));
   pl.ctas = TP > 0 ? (int)((TP + pl.Q - 1) / pl.Q) : 0;
-  pl.maxslot = pl.Pv > 0 ? (int)((pl.Pv + pl.Q - 1) / pl.Q + 1) : 1;
+  // a ragged batch has at most TP pages, so it keeps this grid and takes
+  // fewer pages per CTA; its segment ids stay below ctas + S as well
+  pl.nid = pl.ctas + pl.S;
   size_t off = 256;
   const size_t heads = (size_t)pl.S * pl.nch * 8;
+  const size_t rows = (size_t)pl.nch * pl.nid * 8;
   pl.off_qf = off;  off += heads * (pl.D / 2) * 4;
   pl.off_sqf = off; off += heads * (pl.D / 2) * 4;
   off = (off + 255) & ~(size_t)255;
-  pl.off_m = off;   off += heads * pl.maxslot * 4;
-  pl.off_l = off;   off += heads * pl.maxslot * 4;
+  pl.off_m = off;   off += rows * 4;
+  pl.off_l = off;   off += rows * 4;
   off = (off + 255) & ~(size_t)255;
-  pl.off_o = off;   off += heads * pl.maxslot * pl.D * 4;
+  pl.off_o = off;   off += rows * pl.D * 4;
+  pl.off_cum = off; off += ((size_t)pl.S + 1) * 4;
   pl.total = (off + 255) & ~(size_t)255;
   return pl;
 }
@@ -1145,6 +1262,16 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   const int64_t Hkv = c->streams / a->q->shape[0];
   const float alpha = sqrtf(3.14159265358979f / 2.f) / (float)pl.D;
   const int phases = a->phases ? a->phases : (TQ_PHASE_QPREP | TQ_PHASE_DECODE | TQ_PHASE_MERGE);
+  if (a->seq_lens && pl.S * pl.Pv >= ((int64_t)1 << 31)) {
+    set_error("tq_decode_attn: a ragged batch needs streams x pages < 2^31");
+    return TQ_ERR_INVALID;
+  }
+  PageLayout lay;
+  lay.S = pl.S; lay.Pv = pl.Pv; lay.T = pl.T; lay.Q = pl.Q;
+  lay.hkv = (int)Hkv; lay.nid = pl.nid;
+  lay.lens = a->seq_lens;
+  lay.cum = reinterpret_cast<int32_t*>(w + pl.off_cum);
+  lay.rq = reinterpret_cast<int32_t*>(w + kWsRaggedQ);
 
   QPrepParams qp;
   qp.D = pl.D; qp.g = pl.g; qp.Hkv = (int)Hkv; qp.nch = pl.nch;
@@ -1157,6 +1284,8 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   qp.sqf = reinterpret_cast<uint32_t*>(w + pl.off_sqf);
   if (pl.S > 0 && (step || (phases & TQ_PHASE_QPREP))) {
     PrepParams pp;
+    pp.lay = lay;
+    pp.ctas = pl.ctas;
     pp.q = qp;
     pp.append = step != nullptr;
     pp.g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
@@ -1186,8 +1315,8 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
 
   DecodeParams dp;
   dp.pages = c->pages; dp.pm = page_map(c);
-  dp.S = pl.S; dp.Pv = pl.Pv; dp.T = pl.T; dp.Q = pl.Q;
-  dp.nch = pl.nch; dp.maxslot = pl.maxslot;
+  dp.lay = lay;
+  dp.nch = pl.nch;
   dp.qf = qp.qf; dp.sqf = qp.sqf;
   dp.kc = t->k_centroids; dp.vc = t->v_centroids;
   dp.part_m = reinterpret_cast<float*>(w + pl.off_m);
@@ -1201,8 +1330,8 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   }
 
   MergeParams mp;
-  mp.D = pl.D; mp.g = pl.g; mp.Hkv = (int)Hkv; mp.nch = pl.nch; mp.maxslot = pl.maxslot;
-  mp.Pv = pl.Pv; mp.Q = pl.Q;
+  mp.D = pl.D; mp.g = pl.g; mp.Hkv = (int)Hkv; mp.nch = pl.nch;
+  mp.lay = lay;
   mp.part_m = dp.part_m; mp.part_l = dp.part_l; mp.part_o = dp.part_o;
   mp.R = t->rot;
   mp.q = a->q->data; mp.q_dtype = a->q->dtype;

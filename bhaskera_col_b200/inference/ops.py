@@ -254,7 +254,19 @@ class DecodeWorkspace:
         return int(st.value)
 
 
-def _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, keep):
+def _seq_lens_ptr(seq_lens: Optional[torch.Tensor], q: torch.Tensor) -> Optional[int]:
+    if seq_lens is None:
+        return None
+    if seq_lens.dtype != torch.int32 or seq_lens.dim() != 1 or \
+            seq_lens.shape[0] != q.shape[0] or not seq_lens.is_contiguous():
+        raise ValueError("seq_lens must be a contiguous int32 (B,) tensor")
+    if seq_lens.device != q.device:
+        raise ValueError("seq_lens must be on the query's device")
+    return seq_lens.data_ptr()
+
+
+def _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, keep,
+                 seq_lens=None):
     qt, ot = tensor4(q), tensor4(out)
     wk = tensor4(window_k) if window_k is not None and window_k.shape[2] > 0 else None
     wv = tensor4(window_v) if wk is not None else None
@@ -269,6 +281,7 @@ def _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, 
     a.scale = float(scale if scale is not None else 1.0 / math.sqrt(q.shape[-1]))
     a.num_ctas = int(num_ctas)
     a.phases = int(phases)
+    a.seq_lens = _seq_lens_ptr(seq_lens, q)
     return a
 
 
@@ -278,18 +291,23 @@ def decode_step(tables: LayerTables, pages: torch.Tensor, k_new: torch.Tensor,
                 window_v: Optional[torch.Tensor] = None, scale: Optional[float] = None,
                 out: Optional[torch.Tensor] = None,
                 workspace: Optional[DecodeWorkspace] = None,
-                num_ctas: int = 0, gather: Optional[_lib.Gather] = None) -> torch.Tensor:
+                num_ctas: int = 0, gather: Optional[_lib.Gather] = None,
+                seq_lens: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Store the new (B, Hkv, 1, D) token at ``pos`` and attend q over tokens
     [0, pos + 1) plus the window, in one call (tq_decode_step).  ``gather``
     (a filled _lib.Gather whose peer_out[rank] is ``out``) also delivers the
-    output block to every rank's gathered buffer (fused all-gather)."""
+    output block to every rank's gathered buffer (fused all-gather).
+
+    ``seq_lens`` (int32 (B,) on the device, each <= pos + 1) makes the batch
+    ragged: row b stores its token at seq_lens[b] - 1 and attends tokens
+    [0, seq_lens[b]); ``pos`` is then the bound (the longest row's position)."""
     _require_cuda(pages, q, k_new, v_new)
     lib = _lib.load()
     if out is None:
         out = torch.empty_like(q)
     g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
     keep = []
-    a = _decode_args(q, out, pos + 1, window_k, window_v, scale, num_ctas, 0, keep)
+    a = _decode_args(q, out, pos + 1, window_k, window_v, scale, num_ctas, 0, keep, seq_lens)
     if gather is not None:
         a.gather = ctypes.pointer(gather)
     kt, vt = tensor4(k_new), tensor4(v_new)
@@ -336,19 +354,23 @@ def decode_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
                      window_v: Optional[torch.Tensor] = None, scale: Optional[float] = None,
                      out: Optional[torch.Tensor] = None,
                      workspace: Optional[DecodeWorkspace] = None,
-                     num_ctas: int = 0, phases: int = 0) -> torch.Tensor:
+                     num_ctas: int = 0, phases: int = 0,
+                     seq_lens: Optional[torch.Tensor] = None) -> torch.Tensor:
     """softmax(q K^T * scale) V over the packed tokens [0, n_tokens) of every
     stream plus an optional full-precision window.  q: (B, Hq, 1, D).
 
     ``phases`` (OR of _lib.PHASE_*) runs a subset of the three kernels; the
-    later phases read what the earlier ones left in the same ``workspace``."""
+    later phases read what the earlier ones left in the same ``workspace``.
+    ``seq_lens`` (int32 (B,) on the device) gives each batch row its own
+    token count, clamped to [0, n_tokens] (continuous batching)."""
     _require_cuda(pages, q)
     lib = _lib.load()
     if out is None:
         out = torch.empty_like(q)
     g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
     keep = []
-    a = _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, keep)
+    a = _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, keep,
+                     seq_lens)
     nbytes = lib.tq_decode_workspace_bytes(ctypes.byref(g), ctypes.byref(c), ctypes.byref(a))
     if nbytes == 0:
         raise _lib.TqError("tq_decode_workspace_bytes", _lib.TQ_ERR_INVALID, _lib.last_error())

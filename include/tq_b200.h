@@ -184,6 +184,14 @@ typedef struct tq_decode_args {
                                /* reads what the previous one left in the   */
                                /* same workspace)                            */
   const tq_gather* gather;     /* NULL: out only; else the fused all-gather  */
+  /* Ragged batches (continuous batching, vLLM's seq_lens): NULL, or a device
+   * int32[B] whose entry b is the token count of batch row b (its streams
+   * b*Hkv .. b*Hkv + Hkv - 1), clamped on the device to [0, n_tokens];
+   * n_tokens is then the longest row's bound.  The decode splits only the
+   * rows' real pages evenly over its CTAs.  With tq_decode_step, row b's new
+   * token is stored at seq_lens[b] - 1 (nothing is stored where that is
+   * negative).  Needs TQ_PHASE_QPREP in `phases` (0 = all phases). */
+  const int32_t* seq_lens;
 } tq_decode_args;
 
 #define TQ_PHASE_QPREP 1       /* rotate + sketch the query                  */
