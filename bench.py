@@ -451,9 +451,11 @@ def run_ours(args, rank, world, local_rank):
     # ---- prefill append throughput (48 layers x B8 x Hkv8 x 4096, 4-bit) ----
     append_line = None
     prefill_line = None
+    ragged_line = None
     if rank == 0 and not args.skip_append and args.workload == "mixtral":
         append_line = bench_append(dev, args)
         prefill_line = bench_prefill(dev, args)
+        ragged_line = bench_ragged(dev, args)
 
     cpu_line = None
     if rank == 0 and world == 1 and not args.skip_cpu and args.workload == "mixtral":
@@ -488,6 +490,7 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks,
             "append": append_line,
             "prefill_attention": prefill_line,
+            "ragged_decode": ragged_line,
             "device_status": status,
         }
         print(json.dumps(line), flush=True)
@@ -588,6 +591,78 @@ def bench_prefill(dev, args):
             "kernel": ("prefill_tc_kernel (tcgen05.mma, S/P and O in tensor memory)" if tc
                        else "prefill_kernel (mma.sync m16n8k16 fp16)"),
             "mma_sync_kernel_ms": ms_cc}
+
+
+def bench_ragged(dev, args):
+    """Continuous-batching decode step, vLLM-shaped: one layer (Hq32/Hkv8,
+    D128, K4/V2 without QJL, as the reference's vLLM compressor), 64 requests
+    whose context lengths are log-uniform in [256, 16384] (seeded), pages in a
+    shuffled block-table pool, per-request lengths on the device: one
+    tq_decode_step (store + attend).  Against it, the same batch padded to its
+    longest request on contiguous pages (what a caller without per-request
+    lengths runs).  Bytes = the requests' real packed tokens."""
+    import numpy as np
+    import torch
+    from bhaskera_col_b200.inference import ops
+    from bhaskera_col_b200.inference.kv_cache import (FastLloydMaxCodebook,
+                                                      _generate_rotation_matrix)
+    R, H, g, Dd, kb, vb, T = 64, 8, 4, 128, 4, 2, 16384
+    rng = np.random.default_rng(11)
+    lens = np.exp(rng.uniform(math.log(256), math.log(T), R)).astype(np.int64)
+    lens[0] = T
+    kc, vc = FastLloydMaxCodebook.get(Dd, kb, dev), FastLloydMaxCodebook.get(Dd, vb, dev)
+    t = ops.LayerTables(Dd, kb, vb, False, kc.centroids, kc.boundaries, vc.centroids,
+                        vc.boundaries, _generate_rotation_matrix(Dd, 42, dev).contiguous())
+    pb = ops.page_bytes(Dd, kb, vb, False)
+    P = T // 64
+    cont = torch.zeros((R * H, P, pb), dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    for r0 in range(0, R, 8):
+        k = torch.randn((8, H, T, Dd), device=dev, generator=gen).to(torch.bfloat16)
+        ops.append(t, cont[r0 * H:(r0 + 8) * H], k, k, 0)
+        del k
+    perm = torch.randperm(R * H * P, device=dev, generator=gen)
+    pool = torch.empty((R * H * P, pb), dtype=torch.uint8, device=dev)
+    pool[perm] = cont.view(R * H * P, pb)
+    paged = ops.PagedPages(pool, perm.view(R * H, P).to(torch.int32))
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    q = torch.randn((R, H * g, 1, Dd), device=dev, generator=gen).to(torch.bfloat16)
+    kn = torch.randn((R, H, 1, Dd), device=dev, generator=gen).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ws = ops.DecodeWorkspace()
+    reps = max(5, min(args.steps, 20))
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    ms = timed(lambda: ops.decode_step(t, paged, kn, kn, T - 1, q, out=out, workspace=ws,
+                                       seq_lens=sl))
+    ms_pad = timed(lambda: ops.decode_step(t, cont, kn, kn, T - 1, q, out=out, workspace=ws))
+    status = ws.status()
+    alg = int(lens.sum()) * H * (pb // 64)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["hbm_gbs"])
+    except Exception:
+        peak = 6650.0
+    gbs = alg / (ms / 1e3) / 1e9
+    return {"workload": f"continuous-batching decode step, 1 layer: {R} requests, context "
+                        f"log-uniform 256..{T} (sum {int(lens.sum())}), Hq32/Hkv8, D128, "
+                        f"K{kb}/V{vb}, block-table pool", "ms": ms, "gbs": gbs,
+            "frac_of_hbm": gbs / peak, "tokens_per_s": R / (ms / 1e3),
+            "padded_to_longest_ms": ms_pad, "speedup_vs_padded": ms_pad / ms,
+            "algorithmic_bytes": alg, "device_status": status,
+            "l2": "no flush: %.0f MB of packed KV per step > 126 MB L2" % (alg / 1e6)}
 
 
 def run_profile(args):
