@@ -30,6 +30,7 @@ EXPORTED = (
     "tq_decode_step", "tq_decode_attn_noalloc", "tq_workspace_status", "tq_device_status",
     "tq_append_tensor_core", "tq_prefill_attn", "tq_prefill_tensor_core",
     "tq_shared_alloc", "tq_shared_open", "tq_shared_close", "tq_shared_free",
+    "tq_tables_bytes", "tq_init_tables",
 )
 MAX_PEERS = 8
 SHARED_HANDLE_BYTES = 64
@@ -127,6 +128,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             "tq_shared_open": (I32, [VP, P(ctypes.c_void_p)]),
             "tq_shared_close": (I32, [VP]),
             "tq_shared_free": (I32, [VP]),
+            "tq_tables_bytes": (SZ, [P(Geom)]),
+            "tq_init_tables": (I32, [P(Geom), VP, VP, VP, VP, VP, VP, VP, SZ, P(Tables), VP]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)

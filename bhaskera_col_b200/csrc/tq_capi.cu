@@ -7,6 +7,10 @@
 #include <mutex>
 #include <tuple>
 #include <utility>
+#include <vector>
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "tq_common.cuh"
 #include "tq_internal.h"
@@ -470,6 +474,140 @@ int32_t tq_shared_close(void* dptr) {
 int32_t tq_shared_free(void* dptr) {
   cudaError_t e = cudaFree(dptr);
   if (e != cudaSuccess) { set_error("tq_shared_free: %s", cudaGetErrorString(e)); return TQ_ERR_CUDA; }
+  return TQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// tables from host arrays
+// ---------------------------------------------------------------------------
+namespace {
+
+struct TableLayout {
+  size_t kc, kb, vc, vb, rot, rot_t, qjl, qjl_t, bf3, f16, total;
+};
+
+TableLayout table_layout(const tq_geom* g) {
+  const size_t D = (size_t)g->head_dim, DD = D * D;
+  TableLayout L;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = (off + bytes + 255) & ~(size_t)255;
+    return at;
+  };
+  L.kc = take(((size_t)1 << g->key_bits) * 4);
+  L.kb = take((((size_t)1 << g->key_bits) - 1) * 4 + 4);
+  L.vc = take(((size_t)1 << g->value_bits) * 4);
+  L.vb = take((((size_t)1 << g->value_bits) - 1) * 4 + 4);
+  L.rot = take(DD * 4);
+  L.rot_t = take(DD * 4);
+  L.qjl = g->qjl ? take(DD * 4) : 0;
+  L.qjl_t = g->qjl ? take(DD * 4) : 0;
+  L.bf3 = D == 128 ? take(6 * DD * 2) : 0;
+  L.f16 = take(DD * 2);
+  L.total = off;
+  return L;
+}
+
+uint16_t bf16_bits(float x) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(x);
+  uint16_t u;
+  memcpy(&u, &h, 2);
+  return u;
+}
+
+float bf16_value(uint16_t u) {
+  const uint32_t w = (uint32_t)u << 16;
+  float f;
+  memcpy(&f, &w, 4);
+  return f;
+}
+
+}  // namespace
+
+size_t tq_tables_bytes(const tq_geom* g) {
+  if (check_geom(g, "tq_tables_bytes")) return 0;
+  return table_layout(g).total;
+}
+
+int32_t tq_init_tables(const tq_geom* g, const float* k_centroids, const float* k_boundaries,
+                       const float* v_centroids, const float* v_boundaries, const float* rot,
+                       const float* qjl, void* device_buf, size_t device_bytes, tq_tables* t,
+                       void* stream) {
+  const char* fn = "tq_init_tables";
+  if (int rc = check_geom(g, fn)) return rc;
+  if (!k_centroids || !k_boundaries || !v_centroids || !v_boundaries || !rot || !t ||
+      !device_buf || (g->qjl && !qjl)) {
+    set_error("%s: a table, the output or the device buffer is NULL", fn);
+    return TQ_ERR_INVALID;
+  }
+  const TableLayout L = table_layout(g);
+  if (device_bytes < L.total || reinterpret_cast<uintptr_t>(device_buf) % 256) {
+    set_error("%s: device buffer of %zu bytes (256-byte aligned) needed, %zu given", fn, L.total,
+              device_bytes);
+    return TQ_ERR_INVALID;
+  }
+  const int D = g->head_dim;
+  const size_t DD = (size_t)D * D;
+  std::vector<uint8_t> host(L.total, 0);
+  auto put = [&](size_t off, const void* src, size_t bytes) { memcpy(host.data() + off, src, bytes); };
+  put(L.kc, k_centroids, ((size_t)1 << g->key_bits) * 4);
+  put(L.kb, k_boundaries, (((size_t)1 << g->key_bits) - 1) * 4);
+  put(L.vc, v_centroids, ((size_t)1 << g->value_bits) * 4);
+  put(L.vb, v_boundaries, (((size_t)1 << g->value_bits) - 1) * 4);
+  put(L.rot, rot, DD * 4);
+  float* rt = reinterpret_cast<float*>(host.data() + L.rot_t);
+  uint16_t* f16 = reinterpret_cast<uint16_t*>(host.data() + L.f16);
+  for (int i = 0; i < D; ++i)
+    for (int j = 0; j < D; ++j) {
+      rt[(size_t)j * D + i] = rot[(size_t)i * D + j];
+      const __half h = __float2half_rn(rot[(size_t)i * D + j]);
+      memcpy(&f16[(size_t)i * D + j], &h, 2);
+    }
+  if (g->qjl) {
+    put(L.qjl, qjl, DD * 4);
+    float* st = reinterpret_cast<float*>(host.data() + L.qjl_t);
+    for (int i = 0; i < D; ++i)
+      for (int j = 0; j < D; ++j) st[(size_t)j * D + i] = qjl[(size_t)i * D + j];
+  }
+  if (D == 128) {
+    // R = hi + mid + lo in bf16, each rounded to nearest from the fp32
+    // remainder; rows in K quad order ([0]) and V octet order ([1])
+    uint16_t* b3 = reinterpret_cast<uint16_t*>(host.data() + L.bf3);
+    for (int o = 0; o < 2; ++o)
+      for (int p = 0; p < D; ++p) {
+        const int row = o == 0 ? k_coord_at(p, D) : v_coord_at(p, D);
+        for (int c = 0; c < D; ++c) {
+          const float x = rot[(size_t)row * D + c];
+          const uint16_t hi = bf16_bits(x);
+          const float r1 = x - bf16_value(hi);
+          const uint16_t mid = bf16_bits(r1);
+          const uint16_t lo = bf16_bits(r1 - bf16_value(mid));
+          const size_t at = (((size_t)o * 3) * D + p) * D + c;
+          b3[at] = hi;
+          b3[at + DD] = mid;
+          b3[at + 2 * DD] = lo;
+        }
+      }
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(device_buf, host.data(), L.total, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_error("%s: %s", fn, cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  uint8_t* base = static_cast<uint8_t*>(device_buf);
+  t->k_centroids = reinterpret_cast<const float*>(base + L.kc);
+  t->k_boundaries = reinterpret_cast<const float*>(base + L.kb);
+  t->v_centroids = reinterpret_cast<const float*>(base + L.vc);
+  t->v_boundaries = reinterpret_cast<const float*>(base + L.vb);
+  t->rot = reinterpret_cast<const float*>(base + L.rot);
+  t->rot_t = reinterpret_cast<const float*>(base + L.rot_t);
+  t->qjl = g->qjl ? reinterpret_cast<const float*>(base + L.qjl) : nullptr;
+  t->qjl_t = g->qjl ? reinterpret_cast<const float*>(base + L.qjl_t) : nullptr;
+  t->rot_bf16x3 = D == 128 ? reinterpret_cast<const uint16_t*>(base + L.bf3) : nullptr;
+  t->rot_f16 = reinterpret_cast<const uint16_t*>(base + L.f16);
   return TQ_OK;
 }
 

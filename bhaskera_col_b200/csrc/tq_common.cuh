@@ -67,6 +67,14 @@ __device__ __forceinline__ int64_t page_slot(const PageMap& m, int64_t s, int64_
   ok = slot >= 0 && slot < m.nblocks;
   return ok ? slot : 0;
 }
+// page_slot in two halves, so a loop can load the table entry of a later
+// page before it waits: the raw entry, then its check.
+__device__ __forceinline__ int64_t page_entry(const PageMap& m, int64_t s, int64_t pg) {
+  return m.bt == nullptr ? s * m.pps + pg : (int64_t)__ldg(m.bt + s * m.bt_stride + pg);
+}
+__device__ __forceinline__ bool entry_ok(const PageMap& m, int64_t e) {
+  return m.bt == nullptr || (e >= 0 && e < m.nblocks);
+}
 
 // Position of coordinate `coord` in the quad order of a K row.
 __host__ __device__ inline int k_pos_of(int coord, int D) {
@@ -79,6 +87,17 @@ __host__ __device__ inline int k_pos_of(int coord, int D) {
 // Position of coordinate `coord` in the octet order of a V row.
 __host__ __device__ inline int v_pos_of(int coord, int D) {
   return (coord & 7) * (D / 8) + (coord >> 3);
+}
+
+// The coordinates stored at position p of a K row / a V row (inverses of
+// k_pos_of and v_pos_of).
+__host__ __device__ inline int k_coord_at(int p, int D) {
+  const int t = p / (D / 4), e = p % (D / 4);
+  const int j = e >> 2, w = e & 3;           // w: entries 16j+2t, +1, +8, +9
+  return 16 * j + 2 * t + (w & 1) + 8 * (w >> 1);
+}
+__host__ __device__ inline int v_coord_at(int p, int D) {
+  return (p / (D / 8)) + 8 * (p % (D / 8));
 }
 
 // Bit position of quad entry e (k_pos_of) inside a QJL row.

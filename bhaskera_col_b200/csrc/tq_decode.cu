@@ -217,15 +217,16 @@ struct Dec {
   static constexpr int PAGE = OFF_KR + (QJL ? 128 : 0);
   static constexpr int PB = align128(PAGE);
   // static shared memory: the K table (aliased by the combine scratch) and,
-  // when both fit, the V table.  Dynamic: [V table] [stages] [barriers].
+  // when both fit, the V table.  Dynamic: [V table] [stages] [barriers]
+  // (FAST: [table] [stages] [barriers] [combine scratch]).
   // K4 with V2 / V4 at D128: one 64 KB dynamic table region, 256 rows of
   // 256 B (one row per code byte): bytes 0-127 the K pair entry for each of
   // 32 lanes, bytes 128-255 the V entry (V4: pair for 32 lanes; V2: quad of
   // 8 B for 16 lanes).  A lookup address is (byte << 8) | lane offset: one
-  // byte permute.  The combine scratch aliases its first rows.  Such a CTA
-  // owns its SM: 12 consumer warps in three groups of four take every third
-  // page, so one table serves as many warps as three CTAs of the other
-  // variants do.
+  // byte permute.  Such a CTA owns its SM: 12 consumer warps in three groups
+  // of four take every third page, so one table serves as many warps as
+  // three CTAs of the other variants do, and the combine scratch has its own
+  // region (no table rebuild where a stream ends, as ragged batches often do).
   static constexpr bool FAST = D == 128 && KB == 4 && (VB == 2 || VB == 4);
   static constexpr int NCW = FAST ? 12 : 4;            // consumer warps
   static constexpr int NG = NCW / kTileWarps;          // page groups
@@ -235,14 +236,15 @@ struct Dec {
   static constexpr int STAGES = NG * SG;
   static constexpr int COMB = NCW * (16 + 8 * D) * 4;
   static constexpr int FLUT = 65536;
-  static_assert(!FAST || COMB <= FLUT, "combine scratch");
   static constexpr int REGION0 = FAST ? 128 : align128(cmax(Lut<KB>::kBytes, COMB));
   static constexpr bool VSTATIC = FAST || REGION0 + Lut<VB>::kBytes <= 45 * 1024;
   static constexpr int LUTV_STATIC = (VSTATIC && !FAST) ? Lut<VB>::kBytes : 16;
   static constexpr int LUTV = 0;   // offset of the V table in the dynamic region
   static constexpr int STAGE0 = FAST ? FLUT : VSTATIC ? 0 : align128(Lut<VB>::kBytes);
   static constexpr int BARS = STAGE0 + STAGES * PB;
-  static constexpr int SMEM = BARS + 2 * STAGES * 8;
+  static constexpr int COMB_OFF = align128(BARS + 2 * STAGES * 8);
+  static constexpr int SMEM = FAST ? COMB_OFF + COMB : BARS + 2 * STAGES * 8;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 // The K4 / V2|V4 table region (see Dec::FAST): rows [r0, r1) of 256 B, one
@@ -348,9 +350,25 @@ decode_kernel(DecodeParams p) {
     if (lane < G::NG) {
       const int gr = lane;
       int issued = 0;
-      int64_t sp = s_first, sp0 = lay_start(L, sp);   // stream of the lane's page, its start
+      // The lane's pages come in increasing order: walk the streams with the
+      // next stream's start held in a register (a load only when the walk
+      // crosses into the next stream; gpi < total, so it stops before S),
+      // and load each page's table entry one page ahead, before the wait
+      // for its stage, so the lookup latency hides behind that wait.
+      int64_t sp = s_first, sp0 = lay_start(L, sp), nx = lay_start(L, sp + 1);
+      auto entry_of = [&](int64_t gpi) {
+        while (nx <= gpi) {
+          ++sp;
+          sp0 = nx;
+          nx = lay_start(L, sp + 1);
+        }
+        return page_entry(p.pm, sp, gpi - sp0);
+      };
+      int64_t next = gr < npages ? entry_of(gp0 + gr) : 0;
       for (int i = gr, k = 0; i < npages; i += G::NG, ++k) {
         const int st = gr * G::SG + k % G::SG;
+        const int64_t cur = next;
+        if (i + G::NG < npages) next = entry_of(gp0 + i + G::NG);
         if (k >= G::SG && !s_abort) {
           if (!mbar_wait_poll(&empty[st], (uint32_t)(((k / G::SG) - 1) & 1))) {
             atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
@@ -358,14 +376,9 @@ decode_kernel(DecodeParams p) {
           }
         }
         if (s_abort) break;
-        const int64_t gpi = gp0 + i;
-        for (int64_t nx = lay_start(L, sp + 1); nx <= gpi; nx = lay_start(L, sp + 1)) {
-          ++sp;                                  // gpi < total, so this stops before S
-          sp0 = nx;
-        }
-        bool pok;
-        const int64_t ps = page_slot(p.pm, sp, gpi - sp0, pok);
+        const bool pok = entry_ok(p.pm, cur);
         if (!pok) atomicOr(p.status, TQ_DEV_BAD_BLOCK);
+        const int64_t ps = pok ? cur : 0;
         const uint8_t* src = p.pages + ps * (int64_t)G::PAGE;
         mbar_expect_tx(&full[st], (uint32_t)G::PAGE);
         bulk_g2s(smem + G::STAGE0 + st * G::PB, src, (uint32_t)G::PAGE, &full[st]);
@@ -631,8 +644,10 @@ decode_kernel(DecodeParams p) {
         L0 += __shfl_xor_sync(0xffffffffu, L0, o);
         L1 += __shfl_xor_sync(0xffffffffu, L1, o);
       }
-      named_bar(1, NCT);                       // everyone is done with the K table
-      float* comb = reinterpret_cast<float*>(lutk);
+      // everyone is done with the K table (which the scratch aliases), or
+      // with the previous segment's scratch
+      named_bar(1, NCT);
+      float* comb = reinterpret_cast<float*>(G::FAST ? smem + G::COMB_OFF : lutk);
       float* cm = comb + warp * (16 + 8 * D);
       float* cl = cm + 8;
       float* co = cm + 16;
@@ -671,13 +686,12 @@ decode_kernel(DecodeParams p) {
           p.part_l[hrow] = Lsum;
         }
       }
-      named_bar(1, NCT);
-      if (i1 != npages) {                      // restore the table rows the scratch used
-        if constexpr (G::FAST)
-          build_fast_lut<VB>(smem, p.kc, p.vc, 0, (G::COMB + 255) / 256, tid, NCT);
-        else
-          build_lut<KB>(lutk, p.kc, tid, NCT);
+      if constexpr (!G::FAST) {
         named_bar(1, NCT);
+        if (i1 != npages) {                    // restore the table the scratch used
+          build_lut<KB>(lutk, p.kc, tid, NCT);
+          named_bar(1, NCT);
+        }
       }
       reset_state();
     }

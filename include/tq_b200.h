@@ -5,7 +5,8 @@
  * and a cudaStream_t passed as `void*`.  Nothing here allocates device
  * memory: scratch ("workspace") is supplied by the caller and sized with the
  * matching *_workspace_bytes() query.  Work is stream-ordered and no entry
- * point synchronises the host.  Every function returns TQ_OK (0) or a
+ * point synchronises the host, except the init-time tq_init_tables and the
+ * status reads.  Every function returns TQ_OK (0) or a
  * negative status; tq_last_error() gives a thread-local message for the last
  * failure on the calling thread.
  *
@@ -118,6 +119,22 @@ typedef struct tq_tensor4 {
 const char* tq_last_error(void);
 int32_t tq_version(void);
 int64_t tq_page_bytes(const tq_geom* g);
+
+/* One layer's tables from host arrays, for callers without PyTorch.
+ * tq_tables_bytes(g): device bytes the tables need (0 on a bad geometry).
+ * tq_init_tables copies the codebooks (fp32: centroids [2^bits], boundaries
+ * [2^bits - 1]), R and, with g->qjl, S ([D][D] row-major fp32) into
+ * `device_buf` (>= tq_tables_bytes(g) bytes, 256-byte aligned), derives R^T,
+ * S^T, R in fp16 and, for head_dim 128, the three bf16 terms of R in packed
+ * row order, and points *t into the buffer.  It synchronises `stream` once
+ * (an init-time call; the host arrays may be freed on return).  Replaces the
+ * table set-up of _LayerKVStore.__init__ (kv_cache.py:270-311): R from
+ * _generate_rotation_matrix, codebooks from FastLloydMaxCodebook.get. */
+size_t tq_tables_bytes(const tq_geom* g);
+int32_t tq_init_tables(const tq_geom* g, const float* k_centroids, const float* k_boundaries,
+                       const float* v_centroids, const float* v_boundaries, const float* rot,
+                       const float* qjl, void* device_buf, size_t device_bytes, tq_tables* t,
+                       void* stream);
 
 /* Bit-exact scalar quantiser: codes[i] = #{ j : boundaries[j] < y[i] }
  * (torch.bucketize, right=False) for n fp32 values, int16 output.

@@ -27,6 +27,11 @@ from test_gpu_parity import DEV, cosine, rand_kv
 pytestmark = pytest.mark.gpu
 
 
+def _tokens(n, heads, D, seed, outliers=2):
+    """(n, heads, D) token-major bf16 rows (the seeded generator works on (B, H, T, D))."""
+    return rand_kv((1, heads, n, D), seed, outliers=outliers)[0].transpose(0, 1).contiguous()
+
+
 class _Sched:
     """Requests with block lists, like vLLM's KV cache manager."""
 
@@ -58,8 +63,8 @@ class _Sched:
                 self.blocks[r].append(self.free.pop())
             qsl.append(qsl[-1] + n)
             sl.append(self.length[r])
-            k = rand_kv((n, H, D), seed + 2 * i)
-            v = rand_kv((n, H, D), seed + 2 * i + 1)
+            k = _tokens(n, H, D, seed + 2 * i)
+            v = _tokens(n, H, D, seed + 2 * i + 1)
             self.k[r] = torch.cat([self.k[r], k])
             self.v[r] = torch.cat([self.v[r], v])
             toks_k.append(k)
@@ -72,7 +77,7 @@ class _Sched:
         batch = VLLMBatch(torch.tensor(qsl, dtype=torch.int32, device=DEV),
                           torch.tensor(sl, dtype=torch.int32, device=DEV), bt.to(DEV), N,
                           max(n for _, n in work))
-        q = rand_kv((N, Hq, D), seed + 999, outliers=0).to(DEV)
+        q = _tokens(N, Hq, D, seed + 999, outliers=0).to(DEV)
         key = torch.cat(toks_k).to(DEV)
         val = torch.cat(toks_v).to(DEV)
         out = L.forward(q, key, val, batch)

@@ -131,3 +131,24 @@ def test_paged_pages_holder():
         ops.PagedPages(pool, torch.zeros((4, 3), dtype=torch.int32).t())
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.append(None, pp, torch.zeros(1), torch.zeros(1), 0)
+
+
+def test_init_tables_sizes_and_validation():
+    lib = _lib.load()
+    g = _geom(D=128, kb=4, vb=2, q=1)
+    n = lib.tq_tables_bytes(ctypes.byref(g))
+    # kc 64 B, kb 60, vc 16, vb 12 (each in a 256-byte slot), R, R^T, S, S^T
+    # (64 KiB each), three bf16 terms x 2 orders (192 KiB), R fp16 (32 KiB)
+    assert n == 4 * 256 + 4 * 65536 + 196608 + 32768
+    assert lib.tq_tables_bytes(ctypes.byref(_geom(D=48))) == 0
+    t = _lib.Tables()
+    host = (ctypes.c_float * (128 * 128))()
+    rc = lib.tq_init_tables(ctypes.byref(g), host, host, host, host, host, None, 256, n,
+                            ctypes.byref(t), None)
+    assert rc == _lib.TQ_ERR_INVALID and "NULL" in _lib.last_error()     # qjl needs S
+    rc = lib.tq_init_tables(ctypes.byref(g), host, host, host, host, host, host, 256, n - 1,
+                            ctypes.byref(t), None)
+    assert rc == _lib.TQ_ERR_INVALID and "device buffer" in _lib.last_error()
+    rc = lib.tq_init_tables(ctypes.byref(g), host, host, host, host, host, host, 264, n,
+                            ctypes.byref(t), None)
+    assert rc == _lib.TQ_ERR_INVALID and "aligned" in _lib.last_error()
