@@ -41,14 +41,15 @@ constexpr float kNegInf = -INFINITY;
 // Which pages a decode walks.  Stream s owns the compacted page range
 // [start(s), start(s + 1)): s * Pv for a uniform batch, and for a ragged one
 // (per-row token counts) the prefix sums the query preparation lays out.
-// CTA c takes compacted pages [c * Q, (c + 1) * Q).
+// Work unit u (a page group of a decode CTA) takes compacted pages
+// [u * Q, (u + 1) * Q).
 struct PageLayout {
-  int64_t S, Pv, T, Q;    // streams, pages and tokens per stream (bounds), pages per CTA
+  int64_t S, Pv, T, Q;    // streams, pages and tokens per stream (bounds), pages per unit
   int hkv;                // streams per batch row
-  int64_t nid;            // partial-result ids per head chunk: CTAs + S
+  int64_t nid;            // partial-result ids per head chunk: work units + S
   const int32_t* lens;    // [B] tokens of each batch row; NULL: uniform (T each)
   int32_t* cum;           // [S + 1] ragged: first compacted page of each stream
-  int32_t* rq;            // ragged: pages per CTA
+  int32_t* rq;            // ragged: pages per unit
 };
 
 __device__ __forceinline__ int64_t lay_start(const PageLayout& L, int64_t s) {
@@ -86,9 +87,9 @@ struct DecodeParams {
   const uint32_t* sqf;   // [S][nch][8][D/2] half2
   const float* kc;
   const float* vc;
-  // partial results of segment (CTA c, stream s) under id c + s: the id
-  // grows along every CTA's walk and from one CTA to the next, so ids of
-  // different segments never meet
+  // partial results of segment (work unit u, stream s) under id u + s: the
+  // id grows along every unit's walk and from one unit to the next, so ids
+  // of different segments never meet
   float* part_m;         // [nch][nid][8]
   float* part_l;
   float* part_o;         // [nch][nid][8][D]
@@ -199,6 +200,20 @@ __device__ __forceinline__ uint32_t sign_pair(uint32_t w, int pe, int po) {
 
 __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// The named barrier of page group `grp` (ids 1..NG, constant in each branch
+// so the kernel reserves NG + 1 barriers, not all sixteen).
+template <int NG>
+__device__ __forceinline__ void group_bar(int grp, int count) {
+  static_assert(NG >= 1 && NG <= 3, "page groups");
+  if constexpr (NG == 1) {
+    named_bar(1, count);
+  } else {
+    if (grp == 0) named_bar(1, count);
+    else if (NG == 2 || grp == 1) named_bar(2, count);
+    else named_bar(3, count);
+  }
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -336,17 +351,35 @@ decode_kernel(DecodeParams p) {
   __syncthreads();
   pdl_wait();   // pages, query fragments and a ragged layout come from the preceding kernels
 
+  // Work unit u = blockIdx.x * NG + g, served by page group g (its four
+  // consumer warps and producer lane g), takes compacted pages
+  // [u * Q, (u + 1) * Q).  Each group walks and combines its own streams, so
+  // where one group's stream ends the other groups keep working (a CTA over
+  // many short requests of a ragged batch would otherwise stop all twelve
+  // warps at every stream boundary).  unit_range runs on whole warps (the
+  // stream search is warp-cooperative) and is warp-uniform.
   const int64_t Q = L.lens ? (int64_t)__ldcg(L.rq) : L.Q;
   const int64_t total = L.lens ? (int64_t)__ldcg(L.cum + L.S) : L.S * L.Pv;
-  const int64_t gp0 = (int64_t)blockIdx.x * Q;
-  const int npages = (int)tmax<int64_t>(0, tmin<int64_t>(gp0 + Q, total) - gp0);
-  int64_t s_first = 0;                           // the stream of page gp0 (warp-uniform)
-  if (npages > 0) s_first = L.lens ? find_stream(L.cum, L.S, gp0, lane) : gp0 / L.Pv;
+  auto unit_range = [&](int g, int64_t& u0, int& n, int64_t& sf) {
+    const int64_t u = (int64_t)blockIdx.x * G::NG + g;
+    u0 = u * Q;
+    n = (int)tmax<int64_t>(0, tmin<int64_t>(u0 + Q, total) - u0);
+    sf = 0;                                      // the stream of page u0
+    if (n > 0) sf = L.lens ? find_stream(L.cum, L.S, u0, lane) : u0 / L.Pv;
+  };
 
   // ------------------------------------------------------------ producer
-  // Lane g feeds page group g (pages i = g, g + NG, ...) through its own ring
-  // of SG stages, so a slow group never holds back the others' pages.
+  // Lane g feeds page group g (its unit's pages in order) through its own
+  // ring of SG stages, so a slow group never holds back the others' pages.
   if (warp == kConsumerWarps) {
+    int64_t gp0 = 0, s_first = 0;
+    int npages = 0;
+    for (int g = 0; g < G::NG; ++g) {
+      int64_t a, sf;
+      int n;
+      unit_range(g, a, n, sf);
+      if (lane == g) { gp0 = a; npages = n; s_first = sf; }
+    }
     if (lane < G::NG) {
       const int gr = lane;
       int issued = 0;
@@ -364,11 +397,11 @@ decode_kernel(DecodeParams p) {
         }
         return page_entry(p.pm, sp, gpi - sp0);
       };
-      int64_t next = gr < npages ? entry_of(gp0 + gr) : 0;
-      for (int i = gr, k = 0; i < npages; i += G::NG, ++k) {
+      int64_t next = npages > 0 ? entry_of(gp0) : 0;
+      for (int k = 0; k < npages; ++k) {
         const int st = gr * G::SG + k % G::SG;
         const int64_t cur = next;
-        if (i + G::NG < npages) next = entry_of(gp0 + i + G::NG);
+        if (k + 1 < npages) next = entry_of(gp0 + k + 1);
         if (k >= G::SG && !s_abort) {
           if (!mbar_wait_poll(&empty[st], (uint32_t)(((k / G::SG) - 1) & 1))) {
             atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
@@ -420,15 +453,21 @@ decode_kernel(DecodeParams p) {
   reset_state();
 
   const int tw = warp % kTileWarps;             // 16-token tile of a page
-  const int grp = warp / kTileWarps;             // pages i with i % NG == grp
-  // Segments are the runs of one stream's pages in this CTA's range; each
-  // warp takes its group's pages of a segment, then all consumer warps
-  // combine their partial results for the segment.
+  const int grp = warp / kTileWarps;             // page group: serves unit blockIdx.x * NG + grp
+  constexpr int GT = 32 * kTileWarps;            // threads of a page group
+  const int gtid = tid - grp * GT;
+  const int64_t unit = (int64_t)blockIdx.x * G::NG + grp;
+  int64_t gp0, s_first;
+  int npages;
+  unit_range(grp, gp0, npages, s_first);
+  // Segments are the runs of one stream's pages in the unit's range; the
+  // group's four warps take one 16-token tile of every page, then combine
+  // their partial results for the segment.
   int64_t s = s_first;                          // stream of the segment
   int64_t st0 = lay_start(L, s);                // its first compacted page
   int pg0 = (int)(gp0 - st0);                   // the segment's first page in the stream
-  int i0 = 0;                                   // CTA-relative index of that page
-  int inext = grp;                              // next page of this warp's group
+  int i0 = 0;                                   // unit-relative index of that page
+  int inext = 0;                                // next page of the unit
   int ring = 0;                                 // position in the group's stage ring
   uint32_t phase = 0;
   while (i0 < npages) {
@@ -436,7 +475,7 @@ decode_kernel(DecodeParams p) {
     const int i1 = (int)tmin<int64_t>(npages, i0 + (st1 - st0 - pg0));   // pages [i0, i1)
     const int Ts = lay_tokens(L, s);            // valid tokens of the stream
     if (inext < i1) load_q(s);
-    for (; inext < i1; inext += G::NG) {
+    for (; inext < i1; ++inext) {
       const int st = grp * G::SG + ring;
       const int pg = pg0 + (inext - i0);
       if (!s_abort && !mbar_wait_poll(&full[st], phase)) {
@@ -644,9 +683,9 @@ decode_kernel(DecodeParams p) {
         L0 += __shfl_xor_sync(0xffffffffu, L0, o);
         L1 += __shfl_xor_sync(0xffffffffu, L1, o);
       }
-      // everyone is done with the K table (which the scratch aliases), or
-      // with the previous segment's scratch
-      named_bar(1, NCT);
+      // the group is done with the K table (which the scratch aliases when
+      // NG == 1), or with its previous segment's scratch
+      group_bar<G::NG>(grp, GT);
       float* comb = reinterpret_cast<float*>(G::FAST ? smem + G::COMB_OFF : lutk);
       float* cm = comb + warp * (16 + 8 * D);
       float* cl = cm + 8;
@@ -662,18 +701,19 @@ decode_kernel(DecodeParams p) {
         co[(2 * tq) * D + 16 * i2 + gq + 8] = O[i2][2];
         co[(2 * tq + 1) * D + 16 * i2 + gq + 8] = O[i2][3];
       }
-      named_bar(1, NCT);
-      const int64_t hrow0 = ((int64_t)hc * L.nid + blockIdx.x + s) * 8;
-      for (int idx = tid; idx < 8 * D; idx += NCT) {
+      group_bar<G::NG>(grp, GT);
+      const int64_t hrow0 = ((int64_t)hc * L.nid + unit + s) * 8;
+      const float* gcomb = comb + grp * kTileWarps * (16 + 8 * D);
+      for (int idx = gtid; idx < 8 * D; idx += GT) {
         const int h = idx / D, d = idx % D;
         float M = kNegInf;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, comb[w * (16 + 8 * D) + h]);
+        for (int w = 0; w < kTileWarps; ++w) M = fmaxf(M, gcomb[w * (16 + 8 * D) + h]);
         float Lsum = 0.f, Osum = 0.f;
         if (M != kNegInf) {
 #pragma unroll
-          for (int w = 0; w < kConsumerWarps; ++w) {
-            const float* cw = comb + w * (16 + 8 * D);
+          for (int w = 0; w < kTileWarps; ++w) {
+            const float* cw = gcomb + w * (16 + 8 * D);
             const float wt = fast_exp2(cw[h] - M);
             Lsum = fmaf(wt, cw[8 + h], Lsum);
             Osum = fmaf(wt, cw[16 + h * D + d], Osum);
@@ -686,11 +726,11 @@ decode_kernel(DecodeParams p) {
           p.part_l[hrow] = Lsum;
         }
       }
-      if constexpr (!G::FAST) {
-        named_bar(1, NCT);
+      if constexpr (!G::FAST) {                // NG == 1: the group is the CTA
+        group_bar<G::NG>(grp, GT);
         if (i1 != npages) {                    // restore the table the scratch used
-          build_lut<KB>(lutk, p.kc, tid, NCT);
-          named_bar(1, NCT);
+          build_lut<KB>(lutk, p.kc, gtid, GT);
+          group_bar<G::NG>(grp, GT);
         }
       }
       reset_state();
@@ -732,19 +772,19 @@ struct PrepParams {
   uint8_t* pages; PageMap pm; int64_t pos;
   uint32_t* status;
   PageLayout lay;        // ragged (lay.lens set): store at row length - 1, lay out the pages
-  int ctas;              // the decode's grid
+  int units;             // the decode's work units (CTAs x page groups)
 };
 
 constexpr int kPrepThreads = 256;
 
 // Ragged page layout, by all threads of one CTA: cum[s] = compacted pages of
-// the streams before s, cum[S] = all pages, *rq = pages per CTA (at least
+// the streams before s, cum[S] = all pages, *rq = pages per unit (at least
 // Pv / (kMaxSlots - 1), so no stream has more segments than the merge's slot
 // table).  Each thread sums a run of rows; the run totals are scanned by warp
 // shuffles.
 constexpr int kMaxSlots = 64;
 
-__device__ __noinline__ void ragged_layout(const PageLayout L, int ctas, int tid) {
+__device__ __noinline__ void ragged_layout(const PageLayout L, int units, int tid) {
   __shared__ int64_t s_warp[kPrepThreads / 32];
   const int lane = tid & 31, warp = tid >> 5;
   const int64_t B = L.S / L.hkv;
@@ -775,7 +815,7 @@ __device__ __noinline__ void ragged_layout(const PageLayout L, int ctas, int tid
   }
   if (tid == 0) {
     L.cum[L.S] = (int32_t)all;
-    const int64_t q = tmax<int64_t>(tmax<int64_t>((all + ctas - 1) / tmax(ctas, 1), 1),
+    const int64_t q = tmax<int64_t>(tmax<int64_t>((all + units - 1) / tmax(units, 1), 1),
                                     (L.Pv + kMaxSlots - 2) / (kMaxSlots - 1));
     *L.rq = (int32_t)q;
   }
@@ -932,7 +972,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
       if (qjl) reinterpret_cast<__half*>(page + g.off_kr)[slot] = __float2half_rn(nrm[2]);
     }
   }
-  if (pp.lay.lens && blockIdx.x == 0 && blockIdx.y == 0) ragged_layout(pp.lay, pp.ctas, tid);
+  if (pp.lay.lens && blockIdx.x == 0 && blockIdx.y == 0) ragged_layout(pp.lay, pp.units, tid);
 }
 
 // ---------------------------------------------------------------------------
@@ -1154,11 +1194,11 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
 namespace {
 
 // Workspace: [0, 4) the status word, [64, 68) a ragged batch's pages per
-// CTA, then the query fragments, the partials and a ragged page layout.
+// work unit, then the query fragments, the partials and a ragged page layout.
 constexpr size_t kWsRaggedQ = 64;
 
 struct Plan {
-  int D, g, nch, ctas;
+  int D, g, nch, ctas, units;
   int64_t S, Pv, T, Q, nid;
   size_t off_qf, off_sqf, off_m, off_l, off_o, off_cum, total;
 };
@@ -1173,11 +1213,12 @@ struct Variant {
   DecodeFn fn;
   size_t (*smem)();
   int threads;
+  int ng;                 // page groups (work units) per CTA
 };
 
 #define TQ_VARIANT(D_, KB_, VB_, Q_) \
   {D_, KB_, VB_, Q_, decode_kernel<D_, KB_, VB_, (Q_ != 0)>, dec_smem_bytes<D_, KB_, VB_, (Q_ != 0)>, \
-   Dec<D_, KB_, VB_, (Q_ != 0)>::THREADS}
+   Dec<D_, KB_, VB_, (Q_ != 0)>::THREADS, Dec<D_, KB_, VB_, (Q_ != 0)>::NG}
 #define TQ_VARIANT2(D_, KB_, VB_) TQ_VARIANT(D_, KB_, VB_, 0), TQ_VARIANT(D_, KB_, VB_, 1)
 
 const Variant kVariants[] = {
@@ -1197,7 +1238,7 @@ const Variant* find_variant(const tq_geom* g) {
   return nullptr;
 }
 
-Plan make_plan(const tq_geom* G, const tq_cache* c, const tq_decode_args* a, int occ) {
+Plan make_plan(const tq_geom* G, const tq_cache* c, const tq_decode_args* a, int occ, int ng) {
   Plan pl;
   pl.D = G->head_dim;
   const int64_t Hkv = c->streams / a->q->shape[0];
@@ -1209,13 +1250,16 @@ Plan make_plan(const tq_geom* G, const tq_cache* c, const tq_decode_args* a, int
   const int64_t TP = pl.S * pl.Pv;
   int64_t slots = a->num_ctas > 0 ? a->num_ctas : (int64_t)device_sm_count() * tmax(occ, 1);
   slots = tmax<int64_t>(1, slots / tmax(pl.nch, 1));
-  pl.Q = TP > 0 ? (TP + slots - 1) / slots : 1;
+  const int64_t want = slots * ng;               // work units: CTAs x page groups
+  pl.Q = TP > 0 ? (TP + want - 1) / want : 1;    // pages per unit
   // every stream's partials must fit the merge kernel's slot table
   if (pl.Pv > 0) pl.Q = tmax<int64_t>(pl.Q, (pl.Pv + kMaxSlots - 2) / (kMaxSlots - 1));
-  pl.ctas = TP > 0 ? (int)((TP + pl.Q - 1) / pl.Q) : 0;
+  const int64_t used = TP > 0 ? (TP + pl.Q - 1) / pl.Q : 0;
+  pl.ctas = (int)((used + ng - 1) / ng);
+  pl.units = pl.ctas * ng;
   // a ragged batch has at most TP pages, so it keeps this grid and takes
-  // fewer pages per CTA; its segment ids stay below ctas + S as well
-  pl.nid = pl.ctas + pl.S;
+  // fewer pages per unit; its segment ids stay below units + S as well
+  pl.nid = pl.units + pl.S;
   size_t off = 256;
   const size_t heads = (size_t)pl.S * pl.nch * 8;
   const size_t rows = (size_t)pl.nch * pl.nid * 8;
@@ -1242,7 +1286,7 @@ size_t decode_workspace_bytes(const tq_geom* g, const tq_cache* c, const tq_deco
   if (!v) return 0;
   const size_t smem = v->smem();
   if (set_smem_attr((const void*)v->fn, smem) != TQ_OK) return 0;
-  return make_plan(g, c, a, occupancy_of(v, smem)).total;
+  return make_plan(g, c, a, occupancy_of(v, smem), v->ng).total;
 }
 
 using PrepFn = void (*)(PrepParams);
@@ -1267,7 +1311,7 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   }
   const size_t smem = v->smem();
   if (set_smem_attr((const void*)v->fn, smem) != TQ_OK) return TQ_ERR_CUDA;
-  const Plan pl = make_plan(G, c, a, occupancy_of(v, smem));
+  const Plan pl = make_plan(G, c, a, occupancy_of(v, smem), v->ng);
   if (ws == nullptr || ws_bytes < pl.total) {
     set_error("tq_decode_attn: workspace of %zu bytes needed, %zu given", pl.total, ws_bytes);
     return TQ_ERR_WORKSPACE;
@@ -1299,7 +1343,7 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   if (pl.S > 0 && (step || (phases & TQ_PHASE_QPREP))) {
     PrepParams pp;
     pp.lay = lay;
-    pp.ctas = pl.ctas;
+    pp.units = pl.units;
     pp.q = qp;
     pp.append = step != nullptr;
     pp.g = make_geom(G->head_dim, G->key_bits, G->value_bits, G->qjl);
