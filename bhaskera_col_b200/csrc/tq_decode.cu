@@ -861,6 +861,17 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
 
   stage_async(rt, p.RT, D * D * 4, tid, kPrepThreads);
   if (qjl) stage_async(stt, p.ST, D * D * 4, tid, kPrepThreads);
+  if (app) {
+    // the layer's constant tables: read before the dependency wait, so their
+    // latency overlaps the previous kernel
+    for (int i = tid; i < 256; i += kPrepThreads) {
+      if (i <= nbk) cb[i] = pp.kc[i];
+      if (i < nbk) cb[256 + i] = pp.kb[i];
+      if (i <= nbv) cb[512 + i] = pp.vc[i];
+      if (i < nbv) cb[768 + i] = pp.vb[i];
+    }
+    build_orders(ordk, ordv, qinv, D, tid, kPrepThreads);
+  }
   pdl_launch_dependents();
   pdl_wait();
   for (int i = tid; i < 8 * D; i += kPrepThreads) {
@@ -868,6 +879,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
     xs[i] = hl < nh ? load_elem(p.q, p.q_dtype, b * p.q_stride[0] +
                                 (kvh * p.g + hc * 8 + hl) * p.q_stride[1] + c * p.q_stride[3])
                     : 0.f;
+    if (hl >= nh) ys[i] = 0.f;                   // padded heads: zero fragments, not computed
   }
   if (app) {
     if (warp == 0) {
@@ -879,26 +891,28 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
                                      xs + 9 * D, D, lane);
       if (lane == 0) nrm[1] = n;
     }
-    for (int i = tid; i < 256; i += kPrepThreads) {
-      if (i <= nbk) cb[i] = pp.kc[i];
-      if (i < nbk) cb[256 + i] = pp.kb[i];
-      if (i <= nbv) cb[512 + i] = pp.vc[i];
-      if (i < nbv) cb[768 + i] = pp.vb[i];
-    }
-    build_orders(ordk, ordv, qinv, D, tid, kPrepThreads);
   }
   cp_async_wait_all();
   __syncthreads();
 
-  // phase A: rotate the query heads (and u_k, u_v)
+  // phase A: rotate the nh real query heads (and u_k, u_v); vector a of the
+  // active list sits at row a (a head) or 8 + a - nh (u_k, u_v).  The loop
+  // is bound by shared-memory wavefronts, one per (vector, i) and warp, so
+  // the heads a GQA group pads to 8 are not computed.
   {
-    const int nvec = app ? 10 : 8;
+    const int nvec = nh + (app ? 2 : 0);
     const int mine = (grp < G && nvec > grp) ? (nvec - grp + G - 1) / G : 0;
-    float acc[NA];
-    rot_multi<D, NA>(xs + grp * D, G * D, mine, rt, j, acc);
+    int row[NA];
 #pragma unroll
     for (int k = 0; k < NA; ++k) {
-      const int v = grp + k * G;
+      const int a = grp + k * G;
+      row[k] = a < nh ? a : tmin(8 + a - nh, 9);
+    }
+    float acc[NA];
+    rot_rows<D, NA>(xs, row, mine, rt, j, acc);
+#pragma unroll
+    for (int k = 0; k < NA; ++k) {
+      const int v = row[k];
       if (k < mine) {
         ys[v * D + j] = acc[k];
         if (v == 8) code[j] = (uint8_t)bucketize_lt(cb + 256, nbk, acc[k]);
@@ -910,14 +924,20 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   if (qjl) {
     if (app && tid < D) ys[8 * D + tid] -= cb[code[tid]];   // K residual y - c[idx]
     __syncthreads();
-    // phase B: S q_rot for the heads, S r for the K residual
-    const int nvec = app ? 9 : 8;
+    // phase B: S q_rot for the nh heads, S r for the K residual (row 8)
+    const int nvec = nh + (app ? 1 : 0);
     const int mine = (grp < G && nvec > grp) ? (nvec - grp + G - 1) / G : 0;
-    float acc[NB];
-    rot_multi<D, NB>(ys + grp * D, G * D, mine, stt, j, acc);
+    int row[NB];
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
-      const int v = grp + k * G;
+      const int a = grp + k * G;
+      row[k] = a < nh ? a : 8;
+    }
+    float acc[NB];
+    rot_rows<D, NB>(ys, row, mine, stt, j, acc);
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const int v = row[k];
       if (k < mine) {
         if (v < 8) xs[v * D + j] = acc[k];
         else qb[j] = acc[k] >= 0.f ? 1 : 0;
@@ -955,16 +975,23 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
     uint8_t* page = pp.pages + pslot * (int64_t)g.page_bytes;
     const int slot = (int)(t % kPageTokens);
     const int kw = g.krow / 4, vw = g.vrow / 4, qw = qjl ? D / 32 : 0;
-    for (int i = tid; i < kw + vw + qw; i += kPrepThreads) {
+    // every word of the token's K, V and QJL rows is one warp ballot (lane b
+    // holds bit b; the bit order of pack_word and pack_qjl_word), the words
+    // spread over the CTA's warps
+    for (int i = warp; i < kw + vw + qw; i += kPrepThreads / 32) {
+      uint32_t word;
+      uint32_t* dst;
       if (i < kw) {
-        reinterpret_cast<uint32_t*>(page + g.off_k + slot * g.krow)[i] = pack_word(code, ordk, g.kb, i, D);
+        word = ballot_word(code, ordk, g.kb, i, D, lane);
+        dst = reinterpret_cast<uint32_t*>(page + g.off_k + slot * g.krow) + i;
       } else if (i < kw + vw) {
-        reinterpret_cast<uint32_t*>(page + g.off_v + slot * g.vrow)[i - kw] =
-            pack_word(code + D, ordv, g.vb, i - kw, D);
+        word = ballot_word(code + D, ordv, g.vb, i - kw, D, lane);
+        dst = reinterpret_cast<uint32_t*>(page + g.off_v + slot * g.vrow) + (i - kw);
       } else {
-        reinterpret_cast<uint32_t*>(page + g.off_q + slot * g.qrow)[i - kw - vw] =
-            pack_qjl_word(qb, qinv, i - kw - vw);
+        word = __ballot_sync(0xffffffffu, qb[qinv[32 * (i - kw - vw) + lane]] != 0);
+        dst = reinterpret_cast<uint32_t*>(page + g.off_q + slot * g.qrow) + (i - kw - vw);
       }
+      if (lane == 0) *dst = word;
     }
     if (tid == 0) {
       reinterpret_cast<__half*>(page + g.off_kn)[slot] = __float2half_rn(nrm[0]);
@@ -1122,6 +1149,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   constexpr int hpg = 8 / groups;                 // heads per group
   for (int x = tid; x < D * groups; x += kMergeThreads) {
     const int j = x % D, h0 = (x / D) * hpg;
+    if (h0 >= nh) continue;                       // only heads a GQA group pads to 8
     float o[hpg];
 #pragma unroll
     for (int h = 0; h < hpg; ++h) o[h] = 0.f;

@@ -52,6 +52,43 @@ __device__ __forceinline__ void rot_multi(const float* x, int ldx, int nv, const
   }
 }
 
+// acc[v] = sum_i x[row[v] * D + i] T[i][j] for the first N vectors, i
+// ascending with one fmaf per term (rot_coord's order, so each result is
+// bit-identical to it).  N is a compile-time count and every load is
+// unconditional, so the loads of an unrolled block issue together instead
+// of one latency at a time.
+template <int D, int N, int NA>
+__device__ __forceinline__ void rot_rows_n(const float* x, const int (&row)[NA], const float* T,
+                                           int j, float (&acc)[NA]) {
+  const float* xp[N];
+#pragma unroll
+  for (int v = 0; v < N; ++v) {
+    acc[v] = 0.f;
+    xp[v] = x + row[v] * D;
+  }
+#pragma unroll 4
+  for (int i = 0; i < D; ++i) {
+    const float t = T[i * D + j];
+#pragma unroll
+    for (int v = 0; v < N; ++v) acc[v] = fmaf(xp[v][i], t, acc[v]);
+  }
+}
+
+// rot_rows_n for nv (<= NA, uniform across the warp) vectors at rows row[v].
+template <int D, int NA>
+__device__ __forceinline__ void rot_rows(const float* x, const int (&row)[NA], int nv,
+                                         const float* T, int j, float (&acc)[NA]) {
+  static_assert(NA >= 1 && NA <= 5, "vectors per thread");
+  switch (nv) {
+    case 1: rot_rows_n<D, 1, NA>(x, row, T, j, acc); break;
+    case 2: if constexpr (NA >= 2) rot_rows_n<D, 2, NA>(x, row, T, j, acc); break;
+    case 3: if constexpr (NA >= 3) rot_rows_n<D, 3, NA>(x, row, T, j, acc); break;
+    case 4: if constexpr (NA >= 4) rot_rows_n<D, 4, NA>(x, row, T, j, acc); break;
+    case 5: if constexpr (NA >= 5) rot_rows_n<D, 5, NA>(x, row, T, j, acc); break;
+    default: break;
+  }
+}
+
 // Word w of a packed row: LSB-first stream of `bits`-bit codes taken in the
 // order ord[position] -> coordinate.
 __device__ __forceinline__ uint32_t pack_word(const uint8_t* code, const int16_t* ord, int bits,
@@ -72,6 +109,17 @@ __device__ __forceinline__ uint32_t pack_qjl_word(const uint8_t* qb, const int16
   uint32_t word = 0;
   for (int bit = 0; bit < 32; ++bit) word |= (uint32_t)qb[qinv[32 * w + bit]] << bit;
   return word;
+}
+
+// pack_word by one warp: lane l holds bit 32w + l of the row (bit b of the
+// code at position n, 32w + l = n * bits + b), and the ballot is the word.
+// Same bits as pack_word; every lane gets the word.
+__device__ __forceinline__ uint32_t ballot_word(const uint8_t* code, const int16_t* ord,
+                                                int bits, int w, int D, int lane) {
+  const int bit = 32 * w + lane;
+  const int n = bit / bits, b = bit - n * bits;
+  const bool v = n < D && ((code[ord[n]] >> b) & 1);
+  return __ballot_sync(0xffffffffu, v);
 }
 
 // Position -> coordinate tables of the K (quad) and V (octet) row orders and
