@@ -1064,6 +1064,10 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
       hrow0 = ((int64_t)hc * L.nid + first + s) * 8;
     }
   }
+  // the first chunk of partials starts copying now, behind the window and
+  // per-head passes
+  if (nslot > 0)
+    stage_async(po, p.part_o + hrow0 * D, tmin(kSlotChunk, nslot) * 8 * D * 4, tid, kMergeThreads);
 
   // --- window scores (unrotated), all heads --------------------------------
   if (W > 0) {
@@ -1094,19 +1098,33 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   if (warp < 8) {
     const int h = warp;
     float M = kNegInf;
+    // slots lane and lane + 32 (kMaxSlots = 64): m and l loaded together
+    static_assert(kMaxSlots <= 64, "two slots per lane");
+    float mk[2] = {kNegInf, kNegInf}, lk[2] = {0.f, 0.f};
     if (h < nh) {
-      for (int k = lane; k < nslot; k += 32) M = fmaxf(M, p.part_m[hrow0 + 8 * k + h]);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int k = lane + 32 * u;
+        if (k < nslot) {
+          mk[u] = p.part_m[hrow0 + 8 * k + h];
+          lk[u] = p.part_l[hrow0 + 8 * k + h];
+        }
+      }
+      M = fmaxf(mk[0], mk[1]);
       for (int64_t t = lane; t < W; t += 32) M = fmaxf(M, sc[h * W + t]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     const float Ms = M == kNegInf ? 0.f : M;
     float L = 0.f;
-    for (int k = lane; k < nslot; k += 32) {
-      const float mk = p.part_m[hrow0 + 8 * k + h];
-      const float wt = (h < nh && mk != kNegInf) ? exp2f(mk - Ms) : 0.f;
-      s_wt[h][k] = wt;
-      L = fmaf(wt, p.part_l[hrow0 + 8 * k + h], L);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int k = lane + 32 * u;
+      if (k < nslot) {
+        const float wt = (h < nh && mk[u] != kNegInf) ? exp2f(mk[u] - Ms) : 0.f;
+        s_wt[h][k] = wt;
+        L = fmaf(wt, lk[u], L);
+      }
     }
     for (int64_t t = lane; t < W; t += 32) {
       const float e = h < nh ? exp2f(sc[h * W + t] - Ms) : 0.f;
@@ -1123,7 +1141,9 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   for (int k0 = 0; k0 < nslot; k0 += kSlotChunk) {
     const int kn = tmin(kSlotChunk, nslot - k0);
     // slots k0 .. k0 + kn - 1 of all 8 heads are one run: po[k][h][D]
-    stage_async(po, p.part_o + (hrow0 + 8 * k0) * D, kn * 8 * D * 4, tid, kMergeThreads);
+    // (the first chunk was issued after the dependency wait)
+    if (k0 > 0)
+      stage_async(po, p.part_o + (hrow0 + 8 * k0) * D, kn * 8 * D * 4, tid, kMergeThreads);
     cp_async_wait_all();
     __syncthreads();
 #pragma unroll
@@ -1144,21 +1164,39 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   cp_async_wait_all();
   __syncthreads();
   // --- un-rotate (o = O_rot R), add the window, normalise, store --------------
-  // thread (j, half) handles heads half*4 .. half*4+3 of coordinate j
+  // thread (j, grp) handles heads grp*hpg .. grp*hpg + hpg-1 of coordinate
+  // j.  A group of at most hpg heads (GQA 4 at D128) would leave the other
+  // thread groups idle, so there every group sums its own part of the
+  // d-range for heads 0 .. hpg-1 and group 0 adds the parts, in order,
+  // through the partial buffer (consumed by now).
   constexpr int groups = kMergeThreads / D;       // 2 for D = 128
   constexpr int hpg = 8 / groups;                 // heads per group
-  for (int x = tid; x < D * groups; x += kMergeThreads) {
-    const int j = x % D, h0 = (x / D) * hpg;
-    if (h0 >= nh) continue;                       // only heads a GQA group pads to 8
-    float o[hpg];
+  static_assert(D * groups == kMergeThreads && groups * hpg * D <= 8 * kSlotChunk * D, "merge");
+  const bool split = groups > 1 && nh <= hpg;     // block-uniform
+  const int j = tid % D, grp = tid / D;
+  const int h0 = split ? 0 : grp * hpg;
+  const int d0 = split ? grp * (D / groups) : 0, d1 = split ? d0 + D / groups : D;
+  float o[hpg];
 #pragma unroll
-    for (int h = 0; h < hpg; ++h) o[h] = 0.f;
+  for (int h = 0; h < hpg; ++h) o[h] = 0.f;
+  if (h0 < nh) {
 #pragma unroll 4
-    for (int d = 0; d < D; ++d) {
+    for (int d = d0; d < d1; ++d) {
       const float r = rs[d * D + j];
 #pragma unroll
       for (int h = 0; h < hpg; ++h) o[h] = fmaf(orot[(h0 + h) * D + d], r, o[h]);
     }
+  }
+  if (split) {
+#pragma unroll
+    for (int h = 0; h < hpg; ++h) po[(grp * hpg + h) * D + j] = o[h];
+    __syncthreads();
+    if (grp == 0)
+      for (int q = 1; q < groups; ++q)
+#pragma unroll
+        for (int h = 0; h < hpg; ++h) o[h] += po[(q * hpg + h) * D + j];
+  }
+  if (split ? grp == 0 : h0 < nh) {
     for (int64_t t = 0; t < W; ++t) {
       const float vx = load_elem(p.wv, p.w_dtype, b * p.wv_stride[0] + kvh * p.wv_stride[1] +
                                                       t * p.wv_stride[2] + j * p.wv_stride[3]);
