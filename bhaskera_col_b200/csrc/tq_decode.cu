@@ -52,6 +52,13 @@ struct PageLayout {
   int32_t* rq;            // ragged: pages per unit
 };
 
+// A ragged layout opens every non-empty stream with this many placeholder
+// pages: the cost of a stream boundary (the group drains, combines and
+// starts the next stream, ~3.5 us, about four pages) counted as work, so the
+// units over many short requests take fewer real pages.  Placeholders are
+// never fetched or computed; producer and consumers skip them alike.
+constexpr int kSegPages = 4;
+
 __device__ __forceinline__ int64_t lay_start(const PageLayout& L, int64_t s) {
   return L.lens ? (int64_t)__ldcg(L.cum + s) : s * L.Pv;
 }
@@ -389,21 +396,30 @@ decode_kernel(DecodeParams p) {
       // and load each page's table entry one page ahead, before the wait
       // for its stage, so the lookup latency hides behind that wait.
       int64_t sp = s_first, sp0 = lay_start(L, sp), nx = lay_start(L, sp + 1);
-      auto entry_of = [&](int64_t gpi) {
+      const int cph = L.lens ? kSegPages : 0;
+      // false for a placeholder page; else the page's table entry in e
+      auto locate = [&](int64_t gpi, int64_t& e) {
         while (nx <= gpi) {
           ++sp;
           sp0 = nx;
           nx = lay_start(L, sp + 1);
         }
-        return page_entry(p.pm, sp, gpi - sp0);
+        const int64_t pg = gpi - sp0 - cph;
+        if (pg < 0) return false;
+        e = page_entry(p.pm, sp, pg);
+        return true;
       };
-      int64_t next = npages > 0 ? entry_of(gp0) : 0;
+      int64_t next = 0;
+      bool next_real = npages > 0 && locate(gp0, next);
+      int kr = 0;                                // real pages issued: the ring position
       for (int k = 0; k < npages; ++k) {
-        const int st = gr * G::SG + k % G::SG;
         const int64_t cur = next;
-        if (k + 1 < npages) next = entry_of(gp0 + k + 1);
-        if (k >= G::SG && !s_abort) {
-          if (!mbar_wait_poll(&empty[st], (uint32_t)(((k / G::SG) - 1) & 1))) {
+        const bool real = next_real;
+        if (k + 1 < npages) next_real = locate(gp0 + k + 1, next);
+        if (!real) continue;
+        const int st = gr * G::SG + kr % G::SG;
+        if (kr >= G::SG && !s_abort) {
+          if (!mbar_wait_poll(&empty[st], (uint32_t)(((kr / G::SG) - 1) & 1))) {
             atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
             s_abort = 1;
           }
@@ -415,7 +431,7 @@ decode_kernel(DecodeParams p) {
         const uint8_t* src = p.pages + ps * (int64_t)G::PAGE;
         mbar_expect_tx(&full[st], (uint32_t)G::PAGE);
         bulk_g2s(smem + G::STAGE0 + st * G::PB, src, (uint32_t)G::PAGE, &full[st]);
-        issued = k + 1;
+        issued = ++kr;
       }
       if (s_abort) {   // never leave with a copy still writing shared memory
         for (int k = tmax(0, issued - G::SG); k < issued; ++k)
@@ -463,6 +479,7 @@ decode_kernel(DecodeParams p) {
   // Segments are the runs of one stream's pages in the unit's range; the
   // group's four warps take one 16-token tile of every page, then combine
   // their partial results for the segment.
+  const int cph = L.lens ? kSegPages : 0;       // placeholder pages opening a ragged stream
   int64_t s = s_first;                          // stream of the segment
   int64_t st0 = lay_start(L, s);                // its first compacted page
   int pg0 = (int)(gp0 - st0);                   // the segment's first page in the stream
@@ -476,8 +493,9 @@ decode_kernel(DecodeParams p) {
     const int Ts = lay_tokens(L, s);            // valid tokens of the stream
     if (inext < i1) load_q(s);
     for (; inext < i1; ++inext) {
+      const int pg = pg0 + (inext - i0) - cph;  // page in the stream; < 0: a placeholder
+      if (pg < 0) continue;
       const int st = grp * G::SG + ring;
-      const int pg = pg0 + (inext - i0);
       if (!s_abort && !mbar_wait_poll(&full[st], phase)) {
         atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
         s_abort = 1;
@@ -790,8 +808,9 @@ __device__ __noinline__ void ragged_layout(const PageLayout L, int units, int ti
   const int64_t B = L.S / L.hkv;
   const int64_t run = (B + kPrepThreads - 1) / kPrepThreads;
   const int64_t b0 = tmin<int64_t>(B, tid * run), b1 = tmin<int64_t>(B, b0 + run);
-  auto row_pages = [&](int64_t b) {
-    return ((int64_t)lay_tokens(L, b * L.hkv) + kPageTokens - 1) / kPageTokens;
+  auto row_pages = [&](int64_t b) {            // real pages + placeholders per stream
+    const int64_t n = ((int64_t)lay_tokens(L, b * L.hkv) + kPageTokens - 1) / kPageTokens;
+    return n > 0 ? n + kSegPages : 0;
   };
   int64_t mine = 0;
   for (int64_t b = b0; b < b1; ++b) mine += row_pages(b) * L.hkv;
@@ -816,7 +835,7 @@ __device__ __noinline__ void ragged_layout(const PageLayout L, int units, int ti
   if (tid == 0) {
     L.cum[L.S] = (int32_t)all;
     const int64_t q = tmax<int64_t>(tmax<int64_t>((all + units - 1) / tmax(units, 1), 1),
-                                    (L.Pv + kMaxSlots - 2) / (kMaxSlots - 1));
+                                    (L.Pv + kSegPages + kMaxSlots - 2) / (kMaxSlots - 1));
     *L.rq = (int32_t)q;
   }
 }
@@ -1386,8 +1405,8 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   const int64_t Hkv = c->streams / a->q->shape[0];
   const float alpha = sqrtf(3.14159265358979f / 2.f) / (float)pl.D;
   const int phases = a->phases ? a->phases : (TQ_PHASE_QPREP | TQ_PHASE_DECODE | TQ_PHASE_MERGE);
-  if (a->seq_lens && pl.S * pl.Pv >= ((int64_t)1 << 31)) {
-    set_error("tq_decode_attn: a ragged batch needs streams x pages < 2^31");
+  if (a->seq_lens && pl.S * (pl.Pv + kSegPages) >= ((int64_t)1 << 31)) {
+    set_error("tq_decode_attn: a ragged batch needs streams x (pages + %d) < 2^31", kSegPages);
     return TQ_ERR_INVALID;
   }
   PageLayout lay;
