@@ -152,3 +152,36 @@ def test_init_tables_sizes_and_validation():
     rc = lib.tq_init_tables(ctypes.byref(g), host, host, host, host, host, host, 264, n,
                             ctypes.byref(t), None)
     assert rc == _lib.TQ_ERR_INVALID and "aligned" in _lib.last_error()
+
+
+def test_seq_lens_validation():
+    """Ragged decode arguments are checked on the host before any launch."""
+    import torch
+    from bhaskera_col_b200.inference import ops
+    q = torch.zeros((3, 8, 1, 128), dtype=torch.bfloat16)
+    for bad in (torch.zeros(3, dtype=torch.int64), torch.zeros((3, 1), dtype=torch.int32),
+                torch.zeros(4, dtype=torch.int32)):
+        with pytest.raises(ValueError, match="seq_lens"):
+            ops._seq_lens_ptr(bad, q)
+    assert ops._seq_lens_ptr(None, q) is None
+    lib = _lib.load()
+    g = _geom()
+    t = _lib.Tables(*([16] * 10))
+    c = _lib.Cache(1024, 8, 4)
+    qt = _lib.Tensor4(16, _lib.TQ_BF16, (ctypes.c_int64 * 4)(2, 8, 1, 128),
+                      (ctypes.c_int64 * 4)(1024, 128, 128, 1))
+    a = _lib.DecodeArgs()
+    a.q = ctypes.pointer(qt)
+    a.out = ctypes.pointer(qt)
+    a.n_tokens = 10
+    a.num_q_heads = 8
+    a.scale = 0.1
+    a.seq_lens = 1026                        # not 4-byte aligned
+    rc = lib.tq_decode_attn(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c),
+                            ctypes.byref(a), None, 0, None)
+    assert rc == _lib.TQ_ERR_INVALID and "aligned" in _lib.last_error()
+    a.seq_lens = 1024
+    a.phases = _lib.PHASE_DECODE             # the page layout needs the prep phase
+    rc = lib.tq_decode_attn(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c),
+                            ctypes.byref(a), None, 0, None)
+    assert rc == _lib.TQ_ERR_INVALID and "query-preparation" in _lib.last_error()
