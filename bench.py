@@ -12,7 +12,17 @@ K/V ~ N(0,1) with 1% of channels (2 of 128, fixed per head) scaled x8.
 Multi-GPU (torchrun, one rank per GPU): KV heads are sharded over N ranks
 (8/N heads per rank) and the global batch is 16*N sequences, so every rank
 holds the same 128 (sequence, kv-head) streams as the 1-GPU run (weak
-scaling); each layer ends with an NCCL all-gather of the attention outputs.
+scaling).  Each layer's attention outputs are all-gathered inside the decode
+itself (the merge kernel stores every output block into every rank's buffer
+over NVLink); `--gather nccl` runs NCCL's all-gather after each layer
+instead.  Before timing, one pass over all layers checks the fused gather
+bitwise against NCCL's (`gather_exact`).
+
+Extra keys of the same JSON line: `serving` (256 sequences x 4096 context,
+K3+QJL/V3, KV heads split over the N ranks: strong scaling), `long_context`
+(1 GPU: Qwen2.5-14B shapes, B1/B4 x 32K/128K, bit widths 2/3/4), `append`
+(prefill append GB/s), `prefill_attention` (TFLOP/s) and `ragged_decode`
+(continuous batching).
 
 The JSON line's `value` is decode tokens/s over all ranks (global batch /
 step time, max over ranks), timed on the device with CUDA events around K
@@ -152,6 +162,7 @@ def run_reference(args, rank, world):
         return
     import torch
     from oracle import cpu_baseline as C
+    C.use_all_host_threads()        # torchrun sets OMP_NUM_THREADS=1; the arm uses every core
     W = _workload(args)
     LAYERS, HQ, HKV, D, T_CTX, KEY_BITS, VALUE_BITS = (W.layers, W.hq, W.hkv, W.d, W.t_ctx,
                                                        W.kb, W.vb)
@@ -212,193 +223,264 @@ def _config(W, world, gather="fused"):
 
 
 # ---------------------------------------------------------------------------
-def run_ours(args, rank, world, local_rank):
-    import torch
-    import torch.distributed as dist
-    from bhaskera_col_b200 import _lib
-    from bhaskera_col_b200.inference import TurboQuantKVCache, ops
-    from bhaskera_col_b200.inference.head_parallel import (HeadParallelDecoder, HeadShard,
-                                                           SharedGather)
+class DecodeRig:
+    """One decode-step workload on this rank: the packed cache of the rank's
+    KV heads for every layer, filled with `t_ctx` synthetic tokens, plus the
+    step's inputs (q, the new K/V token) and outputs."""
 
-    W = _workload(args)
-    LAYERS, HQ, HKV, D, T_CTX, KEY_BITS, VALUE_BITS, QJL = (W.layers, W.hq, W.hkv, W.d, W.t_ctx,
-                                                            W.kb, W.vb, W.qjl)
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    shard = HeadShard(HQ, HKV, rank, world)
-    hkv = shard.kv_heads
-    hq = shard.q_heads
-    B = W.batch * world if W.scaling == "weak" else W.batch
-    S = B * hkv
-    bpt = ops.page_bytes(D, KEY_BITS, VALUE_BITS, QJL) // 64
+    def __init__(self, W: Workload, rank: int, world: int, local_rank: int, extra_tokens: int,
+                 gather: str = "fused"):
+        import torch
+        from bhaskera_col_b200.inference import TurboQuantKVCache, ops
+        from bhaskera_col_b200.inference.head_parallel import HeadShard, SharedGather
+        self.W, self.rank, self.world = W, rank, world
+        dev = torch.device("cuda", local_rank)
+        self.dev = dev
+        self.shard = HeadShard(W.hq, W.hkv, rank, world)
+        self.hkv, self.hq = self.shard.kv_heads, self.shard.q_heads
+        self.B = W.batch * world if W.scaling == "weak" else W.batch
+        self.S = self.B * self.hkv
+        self.bpt = ops.page_bytes(W.d, W.kb, W.vb, W.qjl) // 64
+        self.cache = TurboQuantKVCache(
+            num_layers=W.layers, batch_size=self.B, num_heads=self.hkv, head_dim=W.d,
+            key_bits=W.kb, value_bits=W.vb, residual_window=0, protected_layers=0,
+            dtype=torch.bfloat16, device=dev, max_seq_len=W.t_ctx + 64 + extra_tokens, qjl=W.qjl)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1234 + rank)
+        out_ch = torch.randperm(W.d, generator=torch.Generator().manual_seed(7))[:2].to(dev)
+        scale = torch.ones(W.d, device=dev)
+        scale[out_ch] = 8.0
+        student = torch.distributions.StudentT(torch.tensor(4.0, device=dev))
+        torch.cuda.manual_seed(1234 + rank)
 
-    # ---- cache: 32 layers, filled with T_CTX synthetic tokens -------------
-    cache = TurboQuantKVCache(num_layers=LAYERS, batch_size=B, num_heads=hkv, head_dim=D,
-                              key_bits=KEY_BITS, value_bits=VALUE_BITS, residual_window=0,
-                              protected_layers=0, dtype=torch.bfloat16, device=dev,
-                              max_seq_len=T_CTX + 64 + args.steps + args.warmup, qjl=QJL)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1234 + rank)
-    out_ch = torch.randperm(D, generator=torch.Generator().manual_seed(7))[:2].to(dev)
-    scale = torch.ones(D, device=dev)
-    scale[out_ch] = 8.0
+        def synth(shape):
+            if W.data == "student-t":
+                return (student.sample(shape) * (0.5 ** 0.5)).to(torch.bfloat16)
+            return (torch.randn(shape, device=dev, generator=gen) * scale).to(torch.bfloat16)
 
-    student = torch.distributions.StudentT(torch.tensor(4.0, device=dev))
-    torch.cuda.manual_seed(1234 + rank)
+        # four distinct chunks of synthetic K/V, appended round-robin: every
+        # layer's pages are its own memory, so a step reads them all from HBM
+        ch = min(2048, W.t_ctx)
+        chunks = [(synth((self.B, self.hkv, ch, W.d)), synth((self.B, self.hkv, ch, W.d)))
+                  for _ in range(4)]
+        i = 0
+        for layer in range(W.layers):
+            for c0 in range(0, W.t_ctx, ch):
+                n = min(ch, W.t_ctx - c0)
+                k, v = chunks[i % 4]
+                self.cache.append(k[:, :, :n], v[:, :, :n], layer)
+                i += 1
+        del chunks
+        torch.cuda.synchronize()
+        self.stores = self.cache._stores
+        L = W.layers
+        self.q = [synth((self.B, self.hq, 1, W.d)) for _ in range(min(L, 4))]
+        self.k_new = [synth((self.B, self.hkv, 1, W.d)) for _ in range(min(L, 4))]
+        self.v_new = [synth((self.B, self.hkv, 1, W.d)) for _ in range(min(L, 4))]
+        self.o_loc = [torch.empty((self.B, self.hq, 1, W.d), dtype=torch.bfloat16, device=dev)
+                      for _ in range(L)]
+        self.fused = (SharedGather(self.shard, L, self.B, W.d, dev)
+                      if world > 1 and gather == "fused" else None)
+        self.o_all = (self.fused.out if self.fused is not None else
+                      torch.empty((L, world * self.B, self.hq, 1, W.d), dtype=torch.bfloat16,
+                                  device=dev))
+        self.ws = ops.DecodeWorkspace()
 
-    def synth(shape):
-        if W.data == "student-t":
-            return (student.sample(shape) * (0.5 ** 0.5)).to(torch.bfloat16)
-        return (torch.randn(shape, device=dev, generator=gen) * scale).to(torch.bfloat16)
+    def inputs(self, layer):
+        i = layer % len(self.q)
+        return self.q[i], self.k_new[i], self.v_new[i]
 
-    CH = 2048
-    for layer in range(LAYERS):
-        for c0 in range(0, T_CTX, CH):
-            cache.append(synth((B, hkv, CH, D)), synth((B, hkv, CH, D)), layer)
-    torch.cuda.synchronize()
-
-    stores = cache._stores
-    q_dev = [synth((B, hq, 1, D)) for _ in range(LAYERS)]
-    k_new = [synth((B, hkv, 1, D)) for _ in range(LAYERS)]
-    v_new = [synth((B, hkv, 1, D)) for _ in range(LAYERS)]
-    o_loc = [torch.empty((B, hq, 1, D), dtype=torch.bfloat16, device=dev) for _ in range(LAYERS)]
-    # the gathered outputs: for world > 1 by default in peer-mapped buffers
-    # that the decode itself fills (fused all-gather), else NCCL into o_all
-    fused = (SharedGather(shard, LAYERS, B, D, dev)
-             if world > 1 and args.gather == "fused" else None)
-    o_all = (fused.out if fused is not None else
-             torch.empty((LAYERS, world * B, hq, 1, D), dtype=torch.bfloat16, device=dev))
-    ws = ops.DecodeWorkspace()
-    n_tok = T_CTX + 1
-
-    def step(phased_events=None):
-        for layer in range(LAYERS):
-            st = stores[layer]
-            if phased_events is None and fused is not None:
-                ops.decode_step(st.tables, st._pages, k_new[layer], v_new[layer], T_CTX,
-                                q_dev[layer], out=fused.block_view(layer), workspace=ws,
-                                gather=fused.args(layer))
+    def step(self, phased_events=None):
+        """One decode step over all layers (the new token stored at t_ctx)."""
+        from bhaskera_col_b200 import _lib
+        from bhaskera_col_b200.inference import ops
+        T = self.W.t_ctx
+        for layer in range(self.W.layers):
+            st = self.stores[layer]
+            q, k, v = self.inputs(layer)
+            if phased_events is None and self.fused is not None:
+                ops.decode_step(st.tables, st._pages, k, v, T, q,
+                                out=self.fused.block_view(layer), workspace=self.ws,
+                                gather=self.fused.args(layer))
                 continue
             if phased_events is None:
-                ops.decode_step(st.tables, st._pages, k_new[layer], v_new[layer], T_CTX,
-                                q_dev[layer], out=o_loc[layer], workspace=ws)
+                ops.decode_step(st.tables, st._pages, k, v, T, q, out=self.o_loc[layer],
+                                workspace=self.ws)
             else:
-                ops.append(st.tables, st._pages, k_new[layer], v_new[layer], T_CTX)
-                ops.decode_attention(st.tables, st._pages, q_dev[layer], n_tok,
-                                     out=o_loc[layer], workspace=ws,
-                                     phases=_lib.PHASE_QPREP)
+                ops.append(st.tables, st._pages, k, v, T)
+                ops.decode_attention(st.tables, st._pages, q, T + 1, out=self.o_loc[layer],
+                                     workspace=self.ws, phases=_lib.PHASE_QPREP)
                 e0, e1 = phased_events[layer]
                 e0.record()
-                ops.decode_attention(st.tables, st._pages, q_dev[layer], n_tok,
-                                     out=o_loc[layer], workspace=ws,
-                                     phases=_lib.PHASE_DECODE)
+                ops.decode_attention(st.tables, st._pages, q, T + 1, out=self.o_loc[layer],
+                                     workspace=self.ws, phases=_lib.PHASE_DECODE)
                 e1.record()
-                ops.decode_attention(st.tables, st._pages, q_dev[layer], n_tok,
-                                     out=o_loc[layer], workspace=ws,
-                                     phases=_lib.PHASE_MERGE)
-            if world > 1:
-                shard.gather(o_loc[layer], buf=o_all[layer], layer=layer)
+                ops.decode_attention(st.tables, st._pages, q, T + 1, out=self.o_loc[layer],
+                                     workspace=self.ws, phases=_lib.PHASE_MERGE)
+            if self.world > 1:
+                self.shard.gather(self.o_loc[layer], buf=self.o_all[layer], layer=layer)
 
-    # eager warm-up (sets kernel attributes, sizes the workspace)
-    for _ in range(max(1, args.warmup)):
-        step()
+    def check_gather(self):
+        """Every layer once through the fused gather and once through NCCL's
+        all_gather_into_tensor of the same per-rank outputs: the gathered
+        buffers must be bitwise equal on every rank.  Returns (exact, status)."""
+        import torch
+        import torch.distributed as dist
+        from bhaskera_col_b200.inference import ops
+        T = self.W.t_ctx
+        exact = True
+        ref = torch.empty_like(self.o_all[0])
+        for layer in range(self.W.layers):
+            st = self.stores[layer]
+            q, k, v = self.inputs(layer)
+            ops.decode_step(st.tables, st._pages, k, v, T, q, out=self.fused.block_view(layer),
+                            workspace=self.ws, gather=self.fused.args(layer))
+            ops.decode_step(st.tables, st._pages, k, v, T, q, out=self.o_loc[layer],
+                            workspace=self.ws)
+            dist.all_gather_into_tensor(ref, self.o_loc[layer])
+            exact &= bool(torch.equal(self.fused.gathered(layer), ref))
+        flag = torch.tensor([1 if exact else 0], device=self.dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        status = self.ws.status()
+        return bool(flag.item()), status
+
+    def close(self):
+        if self.fused is not None:
+            self.fused.close()
+            self.fused = None
+
+
+def _max_over_ranks(ms, world, dev):
+    if world == 1:
+        return ms
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world, local_rank):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[local_rank])
+
+
+def measure_decode(W: Workload, args, rank, world, local_rank, *, e2e=True, check_gather=False,
+                   clocks=False):
+    """Time one decode-step workload: K CUDA-graph replays of the whole step
+    (CUDA events, max over ranks), the decode kernel alone (roofline pass),
+    and optionally the end-to-end step through the public API with host
+    buffers.  Every rank takes the same collective steps."""
+    import torch
+    rig = DecodeRig(W, rank, world, local_rank, args.steps + args.warmup + 8, args.gather)
+    dev = rig.dev
+    L, T = W.layers, W.t_ctx
+    res = {}
+    if check_gather and rig.fused is not None:
+        res["gather_exact"], res["gather_check_status"] = rig.check_gather()
+
+    for _ in range(max(1, args.warmup)):       # eager warm-up (attributes, workspace)
+        rig.step()
     torch.cuda.synchronize()
-    if ws.status() != 0:
+    if rig.ws.status() != 0:
         raise RuntimeError("device status error after warm-up")
 
-    # ---- CUDA graph of one step -------------------------------------------
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(s):
-        step()
+        rig.step()
     torch.cuda.current_stream(dev).wait_stream(s)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=s):
-        step()
+        rig.step()
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
 
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local_rank])
+    sampler = None
+    if clocks:
+        phys = local_rank
+        cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if cvd:
+            try:
+                phys = int(cvd.split(",")[local_rank])
+            except ValueError:
+                pass
+        sampler = ClockSampler(phys)
 
-    phys = local_rank
-    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
-    if cvd:
-        try:
-            phys = int(cvd.split(",")[local_rank])
-        except ValueError:
-            pass
-    sampler = ClockSampler(phys)
-
-    # ---- timed region: K graph replays --------------------------------------
-    barrier()
+    _barrier(world, local_rank)
     torch.cuda.synchronize()
-    sampler.start()
-    time.sleep(0.3)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(args.steps):
         graph.replay()
     ev1.record()
     torch.cuda.synchronize()
-    clocks = sampler.stop()
-    barrier()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / args.steps
-    value = B / (ms_step / 1e3)
+    res["clocks"] = sampler.stop() if sampler else None
+    _barrier(world, local_rank)
+    ms = _max_over_ranks(ev0.elapsed_time(ev1), world, dev)
+    res["ms_step"] = ms / args.steps
+    res["value"] = rig.B / (res["ms_step"] / 1e3)
+    del graph
 
-    # ---- roofline pass: decode kernel timed alone with events ---------------
+    # roofline pass: the decode kernel alone, timed with events on its stream
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            for _ in range(LAYERS)] for _ in range(args.steps)]
+            for _ in range(L)] for _ in range(args.steps)]
     torch.cuda.synchronize()
     torch.cuda._sleep(int(2e8))          # let the host queue the whole pass first
     for k in range(args.steps):
-        step(phased_events=evs[k])
+        rig.step(phased_events=evs[k])
     torch.cuda.synchronize()
     dec_ms = [e0.elapsed_time(e1) for row in evs for (e0, e1) in row]
-    dec_avg = sum(dec_ms) / len(dec_ms)
-    alg_bytes = S * n_tok * bpt
-    hbm_peak, peak_kind = _peaks()
-    achieved = alg_bytes / (dec_avg / 1e3) / 1e9
+    res["dec_avg_ms"] = sum(dec_ms) / len(dec_ms)
+    res["alg_bytes"] = rig.S * (T + 1) * rig.bpt
+    res["achieved_gbs"] = res["alg_bytes"] / (res["dec_avg_ms"] / 1e3) / 1e9
+    res["packed_kv_gbs_per_gpu"] = L * res["alg_bytes"] / (res["ms_step"] / 1e3) / 1e9
 
-    # ---- e2e through the public API with host buffers -----------------------
-    # each rank receives the full step inputs (all heads) from the host, keeps
-    # its own heads, and reads back the gathered (B, Hq, 1, D) output
-    full_q = [torch.cat([q] * world, 1) for q in q_dev[:4]]
-    full_k = [torch.cat([k] * world, 1) for k in k_new[:4]]
-    full_v = [torch.cat([v] * world, 1) for v in v_new[:4]]
-    # every step copies all 32 layers' q/k/v from one pinned host buffer (in
-    # three chunks: layer 0, layers 1-3, the rest, so layer 0 starts after a
-    # 200 KB copy and later chunks land while earlier layers compute) and reads
-    # all 32 gathered outputs back (layers 0-30 behind the last layer's
-    # compute, then layer 31); copies run on their own stream
-    qn, kn = full_q[0].numel(), full_k[0].numel()
+    if e2e:
+        res.update(_e2e(rig, args, rank, world, local_rank))
+    res["status"] = rig.cache.device_status() | rig.ws.status()
+    res["B"] = rig.B
+    rig.close()
+    del rig
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return res
+
+
+def _e2e(rig, args, rank, world, local_rank):
+    """The step through the public API (TurboQuantKVCache.decode, one call per
+    layer, with the fused all-gather at N > 1) with host buffers: every step
+    each rank copies its own heads' q / k / v in from pinned host memory (the
+    per-rank slices a head-sharded model computes), and rank 0 reads the
+    step's gathered outputs (all layers, all heads) back.  Copies run on their
+    own stream, overlapped with the layers they do not feed."""
+    import torch
+    W, dev, L = rig.W, rig.dev, rig.W.layers
+    qn, kn = rig.q[0].numel(), rig.k_new[0].numel()
     per = qn + 2 * kn
-    in_h = torch.empty((LAYERS, per), dtype=torch.bfloat16).pin_memory()
-    for layer in range(LAYERS):
-        in_h[layer, :qn] = full_q[layer % 4].flatten().cpu()
-        in_h[layer, qn:qn + kn] = full_k[layer % 4].flatten().cpu()
-        in_h[layer, qn + kn:] = full_v[layer % 4].flatten().cpu()
-    in_d = torch.empty((LAYERS, per), dtype=torch.bfloat16, device=dev)
-    q_in = [in_d[l, :qn].view(full_q[0].shape) for l in range(LAYERS)]
-    k_in = [in_d[l, qn:qn + kn].view(full_k[0].shape) for l in range(LAYERS)]
-    v_in = [in_d[l, qn + kn:].view(full_v[0].shape) for l in range(LAYERS)]
-    o_h = torch.empty(o_all.shape, dtype=torch.bfloat16).pin_memory()
-    h2d = in_h.numel() * 2
-    d2h = o_h.numel() * 2
-    decoder = HeadParallelDecoder(cache, shard, fused=fused)
+    in_h = torch.empty((L, per), dtype=torch.bfloat16).pin_memory()
+    for layer in range(L):
+        q, k, v = rig.inputs(layer)
+        in_h[layer, :qn] = q.flatten().cpu()
+        in_h[layer, qn:qn + kn] = k.flatten().cpu()
+        in_h[layer, qn + kn:] = v.flatten().cpu()
+    in_d = torch.empty((L, per), dtype=torch.bfloat16, device=dev)
+    q_in = [in_d[l, :qn].view(rig.q[0].shape) for l in range(L)]
+    k_in = [in_d[l, qn:qn + kn].view(rig.k_new[0].shape) for l in range(L)]
+    v_in = [in_d[l, qn + kn:].view(rig.v_new[0].shape) for l in range(L)]
+    reader = rank == 0
+    o_h = torch.empty(rig.o_all.shape, dtype=torch.bfloat16).pin_memory() if reader else None
     main = torch.cuda.current_stream(dev)
     copy_stream = torch.cuda.Stream(dev)
-    chunks = [(0, 1), (1, min(4, LAYERS)), (min(4, LAYERS), LAYERS)]
+    chunks = [(0, 1), (1, min(4, L)), (min(4, L), L)]
     ev_in = [torch.cuda.Event() for _ in chunks]
     ev_out = [torch.cuda.Event() for _ in range(2)]
+    cache, fused, shard = rig.cache, rig.fused, rig.shard
 
     def e2e_step():
         with torch.cuda.stream(copy_stream):
@@ -406,29 +488,38 @@ def run_ours(args, rank, world, local_rank):
                 if b > a:
                     in_d[a:b].copy_(in_h[a:b], non_blocking=True)
                 ev.record(copy_stream)
-        for layer in range(LAYERS):
+        for layer in range(L):
             for (a, _), ev in zip(chunks, ev_in):
                 if layer == a:
                     main.wait_event(ev)
-            decoder.decode(q_in[layer], k_in[layer], v_in[layer], layer, buf=o_all[layer])
-            if layer == LAYERS - 2:
+            if fused is not None:
+                cache.decode(q_in[layer], k_in[layer], v_in[layer], layer,
+                             out=fused.block_view(layer), gather=fused.args(layer))
+            else:
+                out = cache.decode(q_in[layer], k_in[layer], v_in[layer], layer,
+                                   out=rig.o_loc[layer] if rig.world > 1 else rig.o_all[layer])
+                if rig.world > 1:
+                    shard.gather(out, buf=rig.o_all[layer], layer=layer)
+            if layer == L - 2:
                 ev_out[0].record(main)
         ev_out[1].record(main)
-        with torch.cuda.stream(copy_stream):
-            copy_stream.wait_event(ev_out[0])
-            o_h[:LAYERS - 1].copy_(o_all[:LAYERS - 1], non_blocking=True)
-            copy_stream.wait_event(ev_out[1])
-            o_h[LAYERS - 1:].copy_(o_all[LAYERS - 1:], non_blocking=True)
+        if reader:
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(ev_out[0])
+                o_h[:L - 1].copy_(rig.o_all[:L - 1], non_blocking=True)
+                copy_stream.wait_event(ev_out[1])
+                o_h[L - 1:].copy_(rig.o_all[L - 1:], non_blocking=True)
         copy_stream.synchronize()
         main.synchronize()
 
-    for st in stores:      # the e2e leg appends for real: start from T_CTX tokens
-        st._comp_ptr = T_CTX
+    T = W.t_ctx
+    for st in rig.stores:      # the e2e leg appends for real: start from t_ctx tokens
+        st._comp_ptr = T
     for _ in range(args.warmup):
         e2e_step()
-    for st in stores:
-        st._comp_ptr = T_CTX
-    barrier()
+    for st in rig.stores:
+        st._comp_ptr = T
+    _barrier(world, local_rank)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -436,22 +527,43 @@ def run_ours(args, rank, world, local_rank):
         e2e_step()
     e1.record()
     torch.cuda.synchronize()
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_val = B / (e2e_ms / args.steps / 1e3)
-    status = cache.device_status() | ws.status()
-    del graph
-    if fused is not None:
-        fused.close()
+    _barrier(world, local_rank)
+    ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
+    return {"e2e_value": rig.B / (ms / args.steps / 1e3),
+            "h2d_bytes_per_step": in_h.numel() * 2 * world,
+            "d2h_bytes_per_step": rig.o_all.numel() * 2}
 
-    # ---- prefill append throughput (48 layers x B8 x Hkv8 x 4096, 4-bit) ----
-    append_line = None
-    prefill_line = None
-    ragged_line = None
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    W = _workload(args)
+    hbm_peak, peak_kind = _peaks()
+
+    # ---- the headline workload ----------------------------------------------
+    main = measure_decode(W, args, rank, world, local_rank, e2e=True,
+                          check_gather=world > 1 and args.gather == "fused", clocks=True)
+
+    # ---- config 5: head-sharded serving, strong scaling over the ranks ------
+    serving = None
+    if args.workload == "mixtral" and not args.skip_serving:
+        SW = WORKLOADS["serving"]
+        r = measure_decode(SW, args, rank, world, local_rank, e2e=True,
+                           check_gather=world > 1 and args.gather == "fused")
+        serving = _summary(SW, r, world, hbm_peak, args)
+
+    # ---- config 3: long context (1 GPU) -------------------------------------
+    long_ctx = None
+    if args.workload == "mixtral" and world == 1 and not args.skip_long:
+        long_ctx = []
+        base = WORKLOADS["qwen-long"]
+        for b, t, bits in LONG_CASES:
+            LW = replace(base, batch=b, t_ctx=t, kb=bits, vb=bits)
+            r = measure_decode(LW, args, rank, world, local_rank, e2e=False)
+            long_ctx.append(_summary(LW, r, world, hbm_peak, args))
+
+    append_line = prefill_line = ragged_line = None
     if rank == 0 and not args.skip_append and args.workload == "mixtral":
         append_line = bench_append(dev, args)
         prefill_line = bench_prefill(dev, args)
@@ -460,40 +572,72 @@ def run_ours(args, rank, world, local_rank):
     cpu_line = None
     if rank == 0 and world == 1 and not args.skip_cpu and args.workload == "mixtral":
         from oracle import cpu_baseline as C
-        t_layer = C.time_decode(B, HQ, HKV, D, T_CTX, KEY_BITS, VALUE_BITS, steps=2)
-        cpu_line = {"value": B / (t_layer * LAYERS), "unit": "tokens/s",
+        C.use_all_host_threads()
+        t_layer = C.time_decode(main["B"], W.hq, W.hkv, W.d, W.t_ctx, W.kb, W.vb, steps=2)
+        cpu_line = {"value": main["B"] / (t_layer * W.layers), "unit": "tokens/s",
                     "cores": C.host_threads(), "kind": "port",
-                    "sample": f"reference update()+SDPA, 1 of {LAYERS} layers x 2 steps "
-                              f"timed and scaled x{LAYERS}; B{B} Hkv{HKV} T{T_CTX}, no QJL"}
+                    "sample": f"reference update()+SDPA, 1 of {W.layers} layers x 2 steps "
+                              f"timed and scaled x{W.layers}; B{main['B']} Hkv{W.hkv} "
+                              f"T{W.t_ctx}, no QJL"}
 
     if rank == 0:
+        alg, dec_avg = main["alg_bytes"], main["dec_avg_ms"]
         line = {
-            "metric": "decode-attn tokens/s", "value": value, "unit": "tokens/s",
+            "metric": "decode-attn tokens/s", "value": main["value"], "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_step, "higher_is_better": True, "scaling": W.scaling,
+            "ms_per_step": main["ms_step"], "higher_is_better": True, "scaling": W.scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": _config(W, world, args.gather),
-            "packed_kv_gbs_per_gpu": LAYERS * alg_bytes / (ms_step / 1e3) / 1e9,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
-                         "unit": "GB/s", "frac": achieved / hbm_peak,
+            "packed_kv_gbs_per_gpu": main["packed_kv_gbs_per_gpu"],
+            "roofline": {"bound": "hbm", "achieved": main["achieved_gbs"], "peak": hbm_peak,
+                         "unit": "GB/s", "frac": main["achieved_gbs"] / hbm_peak,
                          "traffic": _traffic_per_launch() if args.workload == "mixtral" else None,
-                         "kernel": f"decode_kernel<{D},{KEY_BITS},{VALUE_BITS},"
-                                   f"{'qjl' if QJL else 'mse'}>",
-                         "algorithmic_bytes_per_launch": alg_bytes,
+                         "kernel": f"decode_kernel<{W.d},{W.kb},{W.vb},"
+                                   f"{'qjl' if W.qjl else 'mse'}>",
+                         "algorithmic_bytes_per_launch": alg,
                          "avg_launch_ms": dec_avg, "peak_kind": peak_kind},
             "cpu_baseline": cpu_line,
-            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h,
-                    "path": "TurboQuantKVCache.decode per layer (fused store + attend), "
-                            "pinned host q/k/v in, output out"},
-            "gpu_launches": args.steps * LAYERS * 3,
-            "clocks": clocks,
+            "e2e": {"value": main["e2e_value"], "unit": "tokens/s",
+                    "h2d_bytes_per_step": main["h2d_bytes_per_step"],
+                    "d2h_bytes_per_step": main["d2h_bytes_per_step"],
+                    "path": "TurboQuantKVCache.decode per layer (fused store + attend"
+                            + (", fused all-gather" if world > 1 else "") + "); each rank "
+                            "copies its heads' q/k/v in from pinned host memory, rank 0 "
+                            "reads the gathered outputs back (byte counts: all ranks)"},
+            "gpu_launches": args.steps * W.layers * 3,
+            "clocks": main["clocks"],
+            "gather_exact": main.get("gather_exact"),
+            "serving": serving,
+            "long_context": long_ctx,
             "append": append_line,
             "prefill_attention": prefill_line,
             "ragged_decode": ragged_line,
-            "device_status": status,
+            "device_status": main["status"] | main.get("gather_check_status", 0),
         }
         print(json.dumps(line), flush=True)
+
+
+LONG_CASES = [(1, 32768, 2), (1, 32768, 3), (1, 32768, 4), (4, 32768, 3), (1, 131072, 3),
+              (4, 131072, 3)]
+
+
+def _summary(W, r, world, hbm_peak, args):
+    """An extra workload's key in the JSON line."""
+    out = {"workload": _config(W, world, args.gather)["workload"],
+           "scaling": W.scaling, "global_batch": r["B"], "n_gpus": world,
+           "tokens_per_s": r["value"], "ms_per_step": r["ms_step"],
+           "packed_kv_gbs_per_gpu": r["packed_kv_gbs_per_gpu"],
+           "decode_kernel": {"avg_launch_ms": r["dec_avg_ms"], "achieved_gbs": r["achieved_gbs"],
+                             "frac_of_hbm": r["achieved_gbs"] / hbm_peak,
+                             "algorithmic_bytes_per_launch": r["alg_bytes"]},
+           "device_status": r["status"] | r.get("gather_check_status", 0)}
+    if "e2e_value" in r:
+        out["e2e"] = {"tokens_per_s": r["e2e_value"],
+                      "h2d_bytes_per_step": r["h2d_bytes_per_step"],
+                      "d2h_bytes_per_step": r["d2h_bytes_per_step"]}
+    if "gather_exact" in r:
+        out["gather_exact"] = r["gather_exact"]
+    return out
 
 
 def bench_append(dev, args):
@@ -735,6 +879,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-append", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-serving", action="store_true",
+                    help="leave out the 256-sequence head-sharded serving workload")
+    ap.add_argument("--skip-long", action="store_true",
+                    help="leave out the long-context cases (1 GPU)")
     ap.add_argument("--profile", choices=["decode", "append", "step", "prefill"], default=None,
                     help="run a small single-layer case for ncu and exit")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mixtral",

@@ -27,7 +27,7 @@ PHASE_QPREP, PHASE_DECODE, PHASE_MERGE = 1, 2, 4
 EXPORTED = (
     "tq_last_error", "tq_version", "tq_page_bytes", "tq_quantize_rotated",
     "tq_append", "tq_dequantize", "tq_decode_workspace_bytes", "tq_decode_attn",
-    "tq_decode_step", "tq_decode_attn_noalloc", "tq_workspace_status", "tq_device_status",
+    "tq_decode_step", "tq_decode_attn_noalloc", "tq_noalloc_status", "tq_workspace_status", "tq_device_status",
     "tq_append_tensor_core", "tq_prefill_attn", "tq_prefill_tensor_core",
     "tq_shared_alloc", "tq_shared_open", "tq_shared_close", "tq_shared_free",
     "tq_tables_bytes", "tq_init_tables",
@@ -119,6 +119,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             "tq_decode_step": (I32, [P(Geom), P(Tables), P(Cache), P(Tensor4), P(Tensor4), I64,
                                      P(DecodeArgs), VP, SZ, VP]),
             "tq_decode_attn_noalloc": (I32, [P(Geom), P(Tables), P(Cache), P(DecodeArgs), VP]),
+            "tq_noalloc_status": (I32, [P(ctypes.c_uint32), VP]),
             "tq_workspace_status": (I32, [VP, P(ctypes.c_uint32), VP]),
             "tq_device_status": (I32, [P(ctypes.c_uint32), VP]),
             "tq_append_tensor_core": (I32, [P(Geom), P(Tables), P(Tensor4), P(Tensor4)]),

@@ -1238,36 +1238,42 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
     }
   }
   if (p.world > 1) {
-    // every thread's stores reach all ranks before the block's arrival counts
+    // Completion of the fused all-gather.  Each CTA's peer stores are made
+    // visible system-wide (fence) before the CTA counts itself done on its own
+    // GPU; the rank's last CTA then adds one arrival to every rank's counter
+    // (release at system scope) and waits until the counter reaches
+    // (calls completed + 1) * world.  The counter only grows (wrap-safe
+    // compare), so a late arrival after a timed-out wait still lands in its
+    // own call's count, and no rank can arrive twice before every rank has
+    // arrived once (its next arrival needs its own wait to have passed).
     __threadfence_system();
     __syncthreads();
     if (tid == 0) {
-      for (int r = 0; r < p.world; ++r) atomicAdd_system(p.peer_flag[r], 1u);
-      // the last CTA of this rank (all others have finished) waits until every
-      // rank's CTAs have arrived, bounded by ~2 s of %globaltimer, and resets
-      // both counters for the layer's next call; only other GPUs' kernels are
-      // waited on, and no rank can add to the counter again before this rank
-      // has finished the step
       uint32_t* arrived = p.peer_flag[p.rank];
       uint32_t* done = arrived + 1;
+      uint32_t* calls = arrived + 2;
       const uint32_t nctas = gridDim.x * gridDim.y;
       if (atomicAdd(done, 1u) + 1u == nctas) {
-        const uint32_t target = (uint32_t)p.world * nctas;
+        // every other CTA of this rank has finished: reset the local count for
+        // the layer's next call (which starts after this grid completes)
+        *done = 0u;
+        __threadfence_system();
+        for (int r = 0; r < p.world; ++r)
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_flag[r]) : "memory");
+        const uint32_t ncall = *calls + 1u;
+        const uint32_t target = ncall * (uint32_t)p.world;
         uint64_t t0 = 0;
         for (uint32_t i = 0;; ++i) {
           uint32_t v;
           asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(arrived) : "memory");
-          if (v >= target) break;
-          __nanosleep(32);
-          if ((i & 63u) == 63u) {
+          if ((int32_t)(v - target) >= 0) break;
+          if ((i & 255u) == 255u) {
             const uint64_t t = global_ns();
             if (t0 == 0) t0 = t;
             else if (t - t0 > 2000000000ull) { atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT); break; }
           }
         }
-        *arrived = 0u;
-        *done = 0u;
-        __threadfence();
+        *calls = ncall;
       }
     }
   }

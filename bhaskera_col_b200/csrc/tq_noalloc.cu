@@ -14,12 +14,18 @@
 // process exits.  Host code cannot use the array's name as a device address,
 // so the first call on each device looks the address up with
 // cudaGetSymbolAddress (with that device current) and caches it; make that
-// first call before any stream capture.  All calls on a device share the one
-// array and it keeps the last call's contents: each call clears the status
-// word the kernels report waits through, and every other byte a call reads
-// is written earlier in the same call.  Calls whose work overlaps on the GPU
-// (different streams, or host threads racing on one device) race on the
-// array; serialise them.
+// first call before any stream capture.  The cached address belongs to the
+// device's current context: after cudaDeviceReset (or anything else that
+// destroys the primary context) the library reloads at a new address and
+// the cache is stale, so do not call these entry points again in such a
+// process.  All calls on a device share the one array and it keeps the last
+// call's contents: each call clears the status word the kernels report
+// device-side errors through, and every other byte a call reads is written
+// earlier in the same call (which is why a call must run all three phases:
+// a phase-split sequence would read what an intervening call left there).
+// Calls whose work overlaps on the GPU (different streams, or host threads
+// racing on one device) race on the array; serialise them.
+// tq_noalloc_status reads and clears the array's status word.
 #include <mutex>
 
 #include "tq_common.cuh"
@@ -68,6 +74,12 @@ using namespace tq;
 extern "C" int32_t tq_decode_attn_noalloc(const tq_geom* g, const tq_tables* t,
                                           const tq_cache* c, const tq_decode_args* a,
                                           void* stream) {
+  constexpr int kAll = TQ_PHASE_QPREP | TQ_PHASE_DECODE | TQ_PHASE_MERGE;
+  if (a && a->phases != 0 && a->phases != kAll) {
+    set_error("tq_decode_attn_noalloc: phases must be 0 (all): a later phase would read "
+              "scratch that any other call on this device may have overwritten");
+    return TQ_ERR_INVALID;
+  }
   const size_t need = tq_decode_workspace_bytes(g, c, a);
   if (need == 0) {
     // argument errors are reported by the full check in tq_decode_attn below
@@ -88,4 +100,16 @@ extern "C" int32_t tq_decode_attn_noalloc(const tq_geom* g, const tq_tables* t,
     return TQ_ERR_CUDA;
   }
   return tq_decode_attn(g, t, c, a, scratch, kNoAllocScratchBytes, stream);
+}
+
+extern "C" int32_t tq_noalloc_status(uint32_t* status, void* stream) {
+  if (!status) {
+    set_error("tq_noalloc_status: NULL argument");
+    return TQ_ERR_INVALID;
+  }
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != TQ_OK) return rc;
+  // the status word sits at the start of the array, as in a workspace
+  return tq_workspace_status(scratch, status, stream);
 }

@@ -128,9 +128,11 @@ class SharedGather:
 
     One buffer per rank holds, for every layer, the (world * B, Hq / world, 1,
     D) gathered output (rank r's block at rows r*B .. r*B + B - 1, the layout
-    all_gather_into_tensor produces), followed by two uint32 counters per
-    layer (arrivals from all ranks; this rank's finished merge CTAs).  Every rank maps every other rank's buffer.  Collective: all
-    ranks construct it together (the IPC handles travel through the group)."""
+    all_gather_into_tensor produces), followed by 16 bytes per layer: three
+    uint32 words (arrivals from all ranks, which only grow; this rank's
+    finished merge CTAs; this rank's completed calls).  Every rank maps every
+    other rank's buffer.  Collective: all ranks construct it together (the IPC
+    handles travel through the group)."""
 
     def __init__(self, shard: HeadShard, layers: int, batch: int, head_dim: int,
                  device: torch.device, group=None, dtype=torch.bfloat16):
@@ -144,7 +146,7 @@ class SharedGather:
         self.layer_elems = shard.world * self.block_elems
         out_bytes = layers * self.layer_elems * 2
         self.flag_off = (out_bytes + 255) // 256 * 256
-        total = self.flag_off + 8 * layers
+        total = self.flag_off + 16 * layers
         lib = _lib.load()
         with torch.cuda.device(device):
             ptr = ctypes.c_void_p()
@@ -173,7 +175,7 @@ class SharedGather:
             blk = (layer * self.layer_elems + shard.rank * self.block_elems) * 2
             for r in range(shard.world):
                 g.peer_out[r] = self.bases[r] + blk
-                g.peer_flag[r] = self.bases[r] + self.flag_off + 8 * layer
+                g.peer_flag[r] = self.bases[r] + self.flag_off + 16 * layer
             self._args.append(g)
         dist.barrier(group=group)           # every rank has mapped every buffer
 

@@ -168,11 +168,12 @@ int32_t tq_dequantize(const tq_geom* g, const tq_tables* t, const tq_cache* c,
 /* Output all-gather fused into the decode (one process per GPU, KV heads
  * sharded over `world` ranks).  Each rank's merge kernel stores its
  * (B, Hq/world, 1, D) output block into every rank's copy of the gathered
- * buffer over peer memory (plain NVLink stores), then adds 1 per CTA to every
- * rank's arrival counter of the layer; the rank's last CTA waits (bounded,
- * TQ_DEV_WAIT_TIMEOUT in the status word on expiry) until all ranks' blocks
- * have arrived and resets the counters, so the call completes with the
- * gathered output in place.
+ * buffer over peer memory (plain NVLink stores); the rank's last CTA then
+ * adds 1 to every rank's arrival counter of the layer and waits (bounded,
+ * TQ_DEV_WAIT_TIMEOUT in the status word on expiry) until the counter shows
+ * every rank's arrival for this call, so the call completes with the
+ * gathered output in place.  The arrival counter only grows; the call count
+ * gives each call its target.
  * Buffers come from tq_shared_alloc / tq_shared_open.  Replaces the NCCL
  * all-gather after each layer's attention (the multi-GPU form of the
  * reference's single-process cache, kv_cache.py:516-624). */
@@ -183,9 +184,11 @@ typedef struct tq_gather {
   void* peer_out[TQ_MAX_PEERS];        /* on rank p: this rank's output block;
                                           peer_out[rank] == out->data; the
                                           block has out's strides on every rank */
-  uint32_t* peer_flag[TQ_MAX_PEERS];   /* on rank p: the layer's two counters
-                                          (arrivals, rank p's finished CTAs),
-                                          zero between calls                  */
+  uint32_t* peer_flag[TQ_MAX_PEERS];   /* on rank p: the layer's three words
+                                          (arrivals from all ranks, rank p's
+                                          finished CTAs, rank p's completed
+                                          calls), zeroed once before the first
+                                          call and owned by the kernels after */
 } tq_gather;
 
 typedef struct tq_decode_args {
@@ -270,13 +273,22 @@ int32_t tq_prefill_tensor_core(const tq_geom* g);
  * call an allocator while serving).  Same arguments and result as
  * tq_decode_attn, minus the workspace: the scratch is a fixed 8 MiB array
  * inside this library (held on every GPU that loads it until exit).  Calls
- * needing more scratch than that fail with TQ_ERR_WORKSPACE.  The first call
- * on a device looks the array's address up (do it before any stream
- * capture).  Calls share the array, so calls that overlap on the GPU race;
- * serialise them.  Device-side wait timeouts are recorded in the array's
- * status word, which each call clears.  No counterpart in the reference. */
+ * needing more scratch than that fail with TQ_ERR_WORKSPACE; a->phases must
+ * be 0 (all phases in one call), else TQ_ERR_INVALID.  The first call on a
+ * device looks the array's address up (do it before any stream capture);
+ * the address is not valid after cudaDeviceReset.  Calls share the array,
+ * so calls that overlap on the GPU race; serialise them.  Device-side errors
+ * (TQ_DEV_WAIT_TIMEOUT, TQ_DEV_BAD_BLOCK) are recorded in the array's status
+ * word, which each call clears at its start: read it with tq_noalloc_status
+ * after the call and before the next one.  No counterpart in the
+ * reference. */
 int32_t tq_decode_attn_noalloc(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                                const tq_decode_args* a, void* stream);
+
+/* Read and clear the status word of the current device's built-in
+ * tq_decode_attn_noalloc array (blocking copy on `stream`); TQ_ERR_DEVICE
+ * when a bit was set.  No counterpart in the reference. */
+int32_t tq_noalloc_status(uint32_t* status, void* stream);
 
 /* Read and clear the device status word kept at the start of a decode
  * workspace (blocking copy on `stream`). */

@@ -45,7 +45,11 @@ class RefLayer:
     """State of one reference _LayerKVStore with its decoded bf16 history."""
 
     def __init__(self, B, H, D, T, key_bits, value_bits, kc, kb, vc, vb, seed=42,
-                 dtype=torch.bfloat16):
+                 dtype=torch.bfloat16, history=True):
+        """``history``: start with a random decoded history of T tokens (a
+        steady-state timing sample); False: start empty, with room for T + 64
+        compressed tokens (the parity check against the reference's own
+        outputs)."""
         self.B, self.H, self.D, self.dtype = B, H, D, dtype
         self.kc, self.kb, self.vc, self.vb = kc, kb, vc, vb
         self.R = _rotation(D, seed)
@@ -54,12 +58,13 @@ class RefLayer:
         self.v_idx = torch.zeros(cap, B * H, D, dtype=torch.int16)
         self.k_norm = torch.zeros(cap, B * H, dtype=torch.float16)
         self.v_norm = torch.zeros(cap, B * H, dtype=torch.float16)
-        self.comp = T
+        self.comp = T if history else 0
         g = torch.Generator(device="cpu")
         g.manual_seed(seed)
         # decoded history of T tokens (values only matter for timing)
-        self.dec_k = torch.randn(B, H, T, D, generator=g).to(dtype)
-        self.dec_v = torch.randn(B, H, T, D, generator=g).to(dtype)
+        n = T if history else 0
+        self.dec_k = torch.randn(B, H, n, D, generator=g).to(dtype)
+        self.dec_v = torch.randn(B, H, n, D, generator=g).to(dtype)
 
     def _compress(self, k: torch.Tensor, v: torch.Tensor) -> None:
         B, H, T, D = k.shape
@@ -143,6 +148,17 @@ def time_append(B, H, D, T, bits, tokens=64, seed=0):
 
 
 def host_threads() -> int:
+    return torch.get_num_threads()
+
+
+def use_all_host_threads() -> int:
+    """Give torch every core this process may run on (a launcher such as
+    torchrun sets OMP_NUM_THREADS=1 per rank); returns the thread count."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    torch.set_num_threads(max(1, n))
     return torch.get_num_threads()
 
 

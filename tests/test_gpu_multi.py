@@ -2,8 +2,9 @@
 merge kernel stores each rank's output block into every rank's buffer over
 peer memory; the gathered outputs must equal NCCL's all-gather of the same
 per-rank outputs exactly (same kernels, same bytes), over several layers and
-steps (the arrival counters are reset and reused).  Skipped with fewer than
-two GPUs."""
+steps, and over a one-layer buffer called several times in a row (each call's
+arrivals counted against its own target).  Skipped with fewer than two
+GPUs."""
 import os
 import socket
 
@@ -61,8 +62,19 @@ def _worker(rank, world, port, result):
                 a = dec_f.decode(q, k, v, layer)
                 b = dec_n.decode(q, k, v, layer)
                 worst = max(worst, (a.float() - b.float()).abs().max().item())
+        # one layer, back-to-back calls on the same counters
+        one = SharedGather(shard, 1, B, D, dev)
+        dec_1 = HeadParallelDecoder(caches[0], shard, fused=one)
+        for step in range(4):
+            q = torch.randn(B, HQ, 1, D, device=dev, generator=g).bfloat16()
+            k = torch.randn(B, HKV, 1, D, device=dev, generator=g).bfloat16()
+            v = torch.randn(B, HKV, 1, D, device=dev, generator=g).bfloat16()
+            a = dec_1.decode(q, k, v, 0).clone()
+            b = dec_n.decode(q, k, v, 0)
+            worst = max(worst, (a.float() - b.float()).abs().max().item())
         torch.cuda.synchronize()
         status = caches[0].device_status() | caches[1].device_status()
+        one.close()
         fused.close()
         result[rank] = (worst, status)
     finally:

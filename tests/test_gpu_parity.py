@@ -354,6 +354,45 @@ def test_full_size_mixtral_decode_property():
     assert (got - want).abs().max().item() <= 1e-2
 
 
+def test_full_size_headline_decode_step_matches_oracle():
+    """The headline configuration exactly as bench.py runs it: B16, Hq32/Hkv8,
+    D128, 8192 tokens, K4 + QJL / V2, bf16 K/V ~ N(0,1) with 2 of 128 channels
+    x8, the last token stored by the fused decode step.  Rows 0, 7 and 15 (24
+    streams) are compared with the oracle evaluated on the kernel's own codes
+    and QJL bits, at the small cases' tolerance."""
+    B, Hkv, g, T, D = 16, 8, 4, 8192, 128
+    t = make_tables(D, 4, 2, True)
+    pages = new_pages(B * Hkv, T, t)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(3)
+    sc = torch.ones(D, device=DEV)
+    sc[torch.randperm(D, generator=torch.Generator().manual_seed(7))[:2].to(DEV)] = 8.0
+    for c0 in range(0, T, 2048):
+        n = min(2048, T - 1 - c0)
+        kk = (torch.randn((B, Hkv, n, D), device=DEV, generator=gen) * sc).to(torch.bfloat16)
+        vv = (torch.randn((B, Hkv, n, D), device=DEV, generator=gen) * sc).to(torch.bfloat16)
+        ops.append(t, pages, kk, vv, c0)
+    k1 = (torch.randn((B, Hkv, 1, D), device=DEV, generator=gen) * sc).to(torch.bfloat16)
+    v1 = (torch.randn((B, Hkv, 1, D), device=DEV, generator=gen) * sc).to(torch.bfloat16)
+    q = (torch.randn((B, Hkv * g, 1, D), device=DEV, generator=gen) * sc).to(torch.bfloat16)
+    ws = ops.DecodeWorkspace()
+    out = ops.decode_step(t, pages, k1, v1, T - 1, q, workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    rows = [0, 7, 15]
+    streams = [b * Hkv + h for b in rows for h in range(Hkv)]
+    _, got = parse(t, pages[streams], T)
+    Smat = _generate_qjl_matrix(D, 42).numpy()
+    want = O.decode_attention_codes(
+        q[rows, :, 0].float().cpu().numpy(), got["k_idx"], got["v_idx"], got["k_norm"],
+        got["v_norm"], t.k_centroids.cpu().numpy(), t.v_centroids.cpu().numpy(),
+        t.rot.cpu().numpy(), qbits=got["qbits"], gamma=got["gamma"], S=Smat, T=T)
+    o = out[rows, :, 0].float().cpu().numpy()
+    bf = 2 ** -8 * np.abs(want).max()          # output is bf16
+    assert np.abs(o - want).max() <= 2e-3 * np.abs(want).max() + bf
+    assert cosine(o, want) >= 0.9999
+
+
 # ------------------------------------------------------- fused decode step
 @pytest.mark.parametrize("D,kb,vb,qjl,B,Hkv,g,T,W", [
     (128, 4, 2, True, 2, 4, 4, 300, 0), (128, 3, 3, False, 1, 2, 5, 64, 0),

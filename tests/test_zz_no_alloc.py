@@ -5,8 +5,11 @@ memory through its own pool, or code that must not allocate while serving),
 so they cannot hand tq_decode_attn a workspace.  tq_decode_attn_noalloc keeps
 that scratch in a fixed array inside the library.  This test calls it through
 the C ABI twice in a row and checks each result against the workspace entry
-point, within the tolerance the decode tests use (max-abs <= 2e-3 * max|o|).
-It also checks that a call needing more than the array holds is refused.
+point.  Both run the same kernels on the same inputs, so the outputs must be
+bitwise equal.  After every call the array's status word must read 0 through
+tq_noalloc_status.  A paged call with a planted out-of-pool block-table entry
+must report TQ_DEV_BAD_BLOCK there.  A call needing more than the array holds
+is refused, and so is a phase-split call.
 """
 import ctypes
 
@@ -38,23 +41,35 @@ def _bf16(shape, seed):
     return torch.from_numpy(gi.outlier_normal(rng, shape, 2, 8.0)).to(DEV, torch.bfloat16)
 
 
-def _noalloc(tables, pages, q, n_tokens):
+def _noalloc(tables, pages, q, n_tokens, phases=0):
     lib = _lib.load()
     out = torch.empty_like(q)
     keep = []
-    a = ops._decode_args(q, out, n_tokens, None, None, None, 0, 0, keep)
+    a = ops._decode_args(q, out, n_tokens, None, None, None, 0, phases, keep)
     g, t, c = tables.geom(), tables.ctables(), ops._cache_desc(pages)
     rc = lib.tq_decode_attn_noalloc(ctypes.byref(g), ctypes.byref(t), ctypes.byref(c),
                                     ctypes.byref(a), ops._stream(DEV))
     return rc, out
 
 
-def test_noalloc_matches_workspace_entry_point_twice():
-    D, B, Hkv, g, T = 128, 2, 4, 4, 700
+def _noalloc_status():
+    st = ctypes.c_uint32(0)
+    rc = _lib.load().tq_noalloc_status(ctypes.byref(st), ops._stream(DEV))
+    assert rc in (_lib.TQ_OK, _lib.TQ_ERR_DEVICE), _lib.last_error()
+    return int(st.value)
+
+
+def _filled(D=128, B=2, Hkv=4, T=700):
     t = _tables(D, 4, 2, True)
     pages = torch.zeros((B * Hkv, -(-T // 64), ops.page_bytes(D, 4, 2, True)), dtype=torch.uint8,
                         device=DEV)
     ops.append(t, pages, _bf16((B, Hkv, T, D), 1), _bf16((B, Hkv, T, D), 2), 0)
+    return t, pages
+
+
+def test_noalloc_matches_workspace_entry_point_twice():
+    B, Hkv, g, T, D = 2, 4, 4, 700, 128
+    t, pages = _filled(D, B, Hkv, T)
     for call in range(2):
         q = _bf16((B, Hkv * g, 1, D), 10 + call)
         n = T - 37 * call                       # second call attends fewer tokens
@@ -62,8 +77,28 @@ def test_noalloc_matches_workspace_entry_point_twice():
         rc, got = _noalloc(t, pages, q, n)
         assert rc == _lib.TQ_OK, _lib.last_error()
         torch.cuda.synchronize()
-        tol = 2e-3 * want.float().abs().max().item()
-        assert torch.allclose(got.float(), want.float(), rtol=0.0, atol=tol), call
+        assert torch.equal(got, want), call
+        assert _noalloc_status() == 0, call
+
+
+def test_noalloc_reports_an_out_of_pool_block():
+    B, Hkv, g, T, D = 2, 4, 4, 700, 128
+    t, pages = _filled(D, B, Hkv, T)
+    S, P, pb = pages.shape
+    bt = torch.arange(S * P, dtype=torch.int32, device=DEV).view(S, P).clone()
+    bt[1, 3] = -1                               # never dereferenced: page 0 is read instead
+    paged = ops.PagedPages(pages.view(S * P, pb), bt)
+    q = _bf16((B, Hkv * g, 1, D), 20)
+    rc, _ = _noalloc(t, paged, q, T)
+    assert rc == _lib.TQ_OK, _lib.last_error()
+    assert _noalloc_status() & _lib.DEV_BAD_BLOCK
+    assert _noalloc_status() == 0               # read and cleared
+    # the next good call starts from a clear word and reports nothing
+    bt[1, 3] = 3 + P
+    rc, got = _noalloc(t, paged, q, T)
+    assert rc == _lib.TQ_OK, _lib.last_error()
+    assert _noalloc_status() == 0
+    assert torch.equal(got, ops.decode_attention(t, pages, q, T))
 
 
 def test_noalloc_refuses_calls_beyond_its_scratch():
@@ -83,3 +118,11 @@ def test_noalloc_refuses_calls_beyond_its_scratch():
                                     ctypes.byref(a), ops._stream(DEV))
     assert rc == _lib.TQ_ERR_WORKSPACE
     assert "8 MiB" in _lib.last_error()
+
+
+def test_noalloc_refuses_a_phase_split_call():
+    t, pages = _filled()
+    q = _bf16((2, 16, 1, 128), 30)
+    rc, _ = _noalloc(t, pages, q, 700, phases=_lib.PHASE_DECODE)
+    assert rc == _lib.TQ_ERR_INVALID
+    assert "phases" in _lib.last_error()
