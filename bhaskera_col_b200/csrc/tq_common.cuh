@@ -261,9 +261,11 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 // ---------------------------------------------------------------------------
 // Tensor-core helpers (mma.sync m16n8k16 f16 -> f32, movmatrix)
 // ---------------------------------------------------------------------------
+// Not volatile: the MMA has no side effect beyond its outputs, so the
+// compiler may interleave independent accumulator chains.
 __device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4],
                                               uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])

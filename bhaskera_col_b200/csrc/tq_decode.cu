@@ -254,7 +254,7 @@ struct Dec {
   static constexpr int NG = NCW / kTileWarps;          // page groups
   static constexpr int THREADS = 32 * (NCW + 1);       // + one producer warp
   static constexpr int MINB = FAST ? 1 : 3;            // CTAs per SM
-  static constexpr int SG = FAST ? 3 : 5;               // stages per page group
+  static constexpr int SG = 4;                          // stages per page group (pages go in pairs)
   static constexpr int STAGES = NG * SG;
   static constexpr int COMB = NCW * (16 + 8 * D) * 4;
   static constexpr int FLUT = 65536;
@@ -342,7 +342,7 @@ decode_kernel(DecodeParams p) {
     s_abort = 0;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kTileWarps);
+      mbar_init(&empty[s], kTileWarps / 2);   // the two warps that take a page
     }
     fence_mbar_init();
   }
@@ -442,6 +442,10 @@ decode_kernel(DecodeParams p) {
   }
 
   // ------------------------------------------------------------ consumers
+  // A page group's four warps take the unit's pages two at a time: warps 0
+  // and 1 the first page of the pair, warps 2 and 3 the second, each warp 32
+  // tokens (two 16-token tiles).  Two tiles per warp give every MMA chain a
+  // twin to interleave with and let one max reduction serve 32 tokens.
   const int gq = lane >> 2, tq = lane & 3;
   const uint32_t lane4 = (uint32_t)lane << 2;
   uint32_t qf[NJ][2], sqf[NJ][2];
@@ -468,7 +472,9 @@ decode_kernel(DecodeParams p) {
   };
   reset_state();
 
-  const int tw = warp % kTileWarps;             // 16-token tile of a page
+  const int tw = warp % kTileWarps;              // warp of the page group
+  const int half = tw >> 1;                      // 0: first page of a pair, 1: second
+  const int wt0 = (tw & 1) * 32;                 // the warp's first token in its page
   const int grp = warp / kTileWarps;             // page group: serves unit blockIdx.x * NG + grp
   constexpr int GT = 32 * kTileWarps;            // threads of a page group
   const int gtid = tid - grp * GT;
@@ -476,221 +482,249 @@ decode_kernel(DecodeParams p) {
   int64_t gp0, s_first;
   int npages;
   unit_range(grp, gp0, npages, s_first);
+
+  // scores of one 16-token tile (rows r0, r0 + 8 of the page) for the lane's
+  // two heads, norms applied; K and QJL fragments dequantised straight from
+  // the packed rows
+  auto tile_scores = [&](const uint8_t* pgb, int r0, float (&sc)[4]) {
+    const int r1 = r0 + 8;
+    uint32_t wk0[KQW], wk1[KQW];
+    load_bits<KQB, KQA>(pgb + r0 * G::KROW, tq * KQB, wk0);
+    load_bits<KQB, KQA>(pgb + r1 * G::KROW, tq * KQB, wk1);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t wq0[QQW], wq1[QQW];
+    if constexpr (QJL) {
+      load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r0 * G::QROW, tq * QQB, wq0);
+      load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r1 * G::QROW, tq * QQB, wq1);
+    }
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      uint32_t a[4];
+      const int o0 = (4 * j) * KB, o1 = (4 * j + 2) * KB;   // quad entries 4j.., 4j+2..
+      if constexpr (G::FAST) {
+        // pair bytes 2j and 2j + 1 of the quad
+        const int wi = j >> 1, b0 = 2 * (j & 1);
+        a[0] = lds32(smem, fast_addr(wk0[wi], lane4, b0));
+        a[1] = lds32(smem, fast_addr(wk1[wi], lane4, b0));
+        a[2] = lds32(smem, fast_addr(wk0[wi], lane4, b0 + 1));
+        a[3] = lds32(smem, fast_addr(wk1[wi], lane4, b0 + 1));
+      } else if constexpr (Lut<KB>::kPair) {
+        a[0] = lds32(lutk, field_addr<2 * KB>(wk0, o0, lane4));
+        a[1] = lds32(lutk, field_addr<2 * KB>(wk1, o0, lane4));
+        a[2] = lds32(lutk, field_addr<2 * KB>(wk0, o1, lane4));
+        a[3] = lds32(lutk, field_addr<2 * KB>(wk1, o1, lane4));
+      } else {
+        a[0] = lds16(lutk, getbits(wk0, o0, KB) << 1) | (lds16(lutk, getbits(wk0, o0 + KB, KB) << 1) << 16);
+        a[1] = lds16(lutk, getbits(wk1, o0, KB) << 1) | (lds16(lutk, getbits(wk1, o0 + KB, KB) << 1) << 16);
+        a[2] = lds16(lutk, getbits(wk0, o1, KB) << 1) | (lds16(lutk, getbits(wk0, o1 + KB, KB) << 1) << 16);
+        a[3] = lds16(lutk, getbits(wk1, o1, KB) << 1) | (lds16(lutk, getbits(wk1, o1 + KB, KB) << 1) << 16);
+      }
+      mma_f16_16816(acc, a, qf[j][0], qf[j][1]);
+      if constexpr (QJL) {
+        uint32_t b[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int pr = 2 * j + h;                 // pair index in the quad
+          const int ch = pr / SP, pin = pr % SP;
+          const int pe = ch * 2 * SP + pin, po = pe + SP;
+          const int wi = pe >> 5;
+          b[2 * h + 0] = sign_pair(wq0[wi], pe & 31, po - (wi << 5));
+          b[2 * h + 1] = sign_pair(wq1[wi], pe & 31, po - (wi << 5));
+        }
+        mma_f16_16816(acc2, b, sqf[j][0], sqf[j][1]);
+      }
+    }
+    const __half* kn = reinterpret_cast<const __half*>(pgb + G::OFF_KN);
+    const float n0 = __half2float(kn[r0]), n1 = __half2float(kn[r1]);
+    sc[0] = acc[0] * n0; sc[1] = acc[1] * n0; sc[2] = acc[2] * n1; sc[3] = acc[3] * n1;
+    if constexpr (QJL) {
+      const __half* kr = reinterpret_cast<const __half*>(pgb + G::OFF_KR);
+      const float g0 = __half2float(kr[r0]), g1 = __half2float(kr[r1]);
+      sc[0] = fmaf(acc2[0], g0, sc[0]); sc[1] = fmaf(acc2[1], g0, sc[1]);
+      sc[2] = fmaf(acc2[2], g1, sc[2]); sc[3] = fmaf(acc2[3], g1, sc[3]);
+    }
+  };
+
+  // O^T += V^T P' for one tile (rows t0r = tile start + 2 tq ...), P' the
+  // B fragments of the tile's probabilities times ||v||
+  auto tile_pv = [&](const uint8_t* pgb, int tile0, uint32_t pb0, uint32_t pb1) {
+    const int t0r = tile0 + 2 * tq;
+    uint32_t wa[VOW], wb[VOW], wc[VOW], wd[VOW];
+    load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 0) * G::VROW, gq * VOB, wa);
+    load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 1) * G::VROW, gq * VOB, wb);
+    load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 8) * G::VROW, gq * VOB, wc);
+    load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 9) * G::VROW, gq * VOB, wd);
+    if constexpr (G::FAST && VB == 2) {
+      // bytes of lo (hi): codes at positions 4k, 4k+1 (4k+2, 4k+3) of token
+      // a in the low nibble and of token b in the high nibble
+      const uint32_t lab = (wa[0] & 0x0F0F0F0Fu) | ((wb[0] << 4) & 0xF0F0F0F0u);
+      const uint32_t hab = ((wa[0] >> 4) & 0x0F0F0F0Fu) | (wb[0] & 0xF0F0F0F0u);
+      const uint32_t lcd = (wc[0] & 0x0F0F0F0Fu) | ((wd[0] << 4) & 0xF0F0F0F0u);
+      const uint32_t hcd = ((wc[0] >> 4) & 0x0F0F0F0Fu) | (wd[0] & 0xF0F0F0F0u);
+      const uint32_t lane_v = 128u + ((uint32_t)(lane & 15) << 3);
+#pragma unroll
+      for (int i2 = 0; i2 < NJ; ++i2) {
+        const uint2 eab = lds64(smem, fast_addr((i2 & 1) ? hab : lab, lane_v, i2 >> 1));
+        const uint2 ecd = lds64(smem, fast_addr((i2 & 1) ? hcd : lcd, lane_v, i2 >> 1));
+        const uint32_t a[4] = {eab.x, eab.y, ecd.x, ecd.y};
+        mma_f16_16816(O[i2], a, pb0, pb1);
+      }
+    } else if constexpr (G::FAST && VB == 4) {
+      // per word: byte k of lo (hi) = code at position 2k (2k+1) of token a,
+      // and of token b in the high nibble
+      uint32_t lab[2], hab[2], lcd[2], hcd[2];
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        lab[x] = (wa[x] & 0x0F0F0F0Fu) | ((wb[x] << 4) & 0xF0F0F0F0u);
+        hab[x] = ((wa[x] >> 4) & 0x0F0F0F0Fu) | (wb[x] & 0xF0F0F0F0u);
+        lcd[x] = (wc[x] & 0x0F0F0F0Fu) | ((wd[x] << 4) & 0xF0F0F0F0u);
+        hcd[x] = ((wc[x] >> 4) & 0x0F0F0F0Fu) | (wd[x] & 0xF0F0F0F0u);
+      }
+      const uint32_t lane_v = 128u + lane4;
+#pragma unroll
+      for (int i2 = 0; i2 < NJ; ++i2) {
+        const int x = i2 >> 2, k = i2 & 3;
+        const uint32_t a[4] = {lds32(smem, fast_addr(lab[x], lane_v, k)),
+                               lds32(smem, fast_addr(hab[x], lane_v, k)),
+                               lds32(smem, fast_addr(lcd[x], lane_v, k)),
+                               lds32(smem, fast_addr(hcd[x], lane_v, k))};
+        mma_f16_16816(O[i2], a, pb0, pb1);
+      }
+    } else if constexpr (VINTER) {
+      // combine the two tokens of each pair word-wise: field c of lo/hi is
+      // (code of token a) | (code of token b) << VB
+      constexpr uint32_t M = VB == 1 ? 0x55555555u : VB == 2 ? 0x33333333u : 0x0F0F0F0Fu;
+      uint32_t lab[VOW], hab[VOW], lcd[VOW], hcd[VOW];
+#pragma unroll
+      for (int x = 0; x < VOW; ++x) {
+        lab[x] = (wa[x] & M) | ((wb[x] << VB) & ~M);
+        hab[x] = ((wa[x] >> VB) & M) | (wb[x] & ~M);
+        lcd[x] = (wc[x] & M) | ((wd[x] << VB) & ~M);
+        hcd[x] = ((wc[x] >> VB) & M) | (wd[x] & ~M);
+      }
+      constexpr int PER = 32 / VB;                 // codes per word
+#pragma unroll
+      for (int i2 = 0; i2 < NJ; ++i2) {
+        const int c0 = 2 * i2;                     // even position -> lo, odd -> hi
+        const int o = ((c0 % PER) & ~1) * VB + (c0 / PER) * 32;
+        uint32_t a[4];
+        a[0] = lds32(lutv, field_addr<2 * VB>(lab, o, lane4));
+        a[1] = lds32(lutv, field_addr<2 * VB>(hab, o, lane4));
+        a[2] = lds32(lutv, field_addr<2 * VB>(lcd, o, lane4));
+        a[3] = lds32(lutv, field_addr<2 * VB>(hcd, o, lane4));
+        mma_f16_16816(O[i2], a, pb0, pb1);
+      }
+    } else {
+#pragma unroll
+      for (int i2 = 0; i2 < NJ; ++i2) {
+        const int c0p = (2 * i2) * VB, c1p = (2 * i2 + 1) * VB;
+        uint32_t a[4];
+        if constexpr (Lut<VB>::kPair) {
+          a[0] = lds32(lutv, (((getbits(wb, c0p, VB) << VB) | getbits(wa, c0p, VB)) << 7 | lane4));
+          a[1] = lds32(lutv, (((getbits(wb, c1p, VB) << VB) | getbits(wa, c1p, VB)) << 7 | lane4));
+          a[2] = lds32(lutv, (((getbits(wd, c0p, VB) << VB) | getbits(wc, c0p, VB)) << 7 | lane4));
+          a[3] = lds32(lutv, (((getbits(wd, c1p, VB) << VB) | getbits(wc, c1p, VB)) << 7 | lane4));
+        } else {
+          a[0] = lds16(lutv, (getbits(wa, c0p, VB) << 1)) | (lds16(lutv, (getbits(wb, c0p, VB) << 1)) << 16);
+          a[1] = lds16(lutv, (getbits(wa, c1p, VB) << 1)) | (lds16(lutv, (getbits(wb, c1p, VB) << 1)) << 16);
+          a[2] = lds16(lutv, (getbits(wc, c0p, VB) << 1)) | (lds16(lutv, (getbits(wd, c0p, VB) << 1)) << 16);
+          a[3] = lds16(lutv, (getbits(wc, c1p, VB) << 1)) | (lds16(lutv, (getbits(wd, c1p, VB) << 1)) << 16);
+        }
+        mma_f16_16816(O[i2], a, pb0, pb1);
+      }
+    }
+  };
+
   // Segments are the runs of one stream's pages in the unit's range; the
-  // group's four warps take one 16-token tile of every page, then combine
-  // their partial results for the segment.
+  // group's warps take the segment's real pages in pairs, then combine their
+  // partial results for the segment.
   const int cph = L.lens ? kSegPages : 0;       // placeholder pages opening a ragged stream
   int64_t s = s_first;                          // stream of the segment
   int64_t st0 = lay_start(L, s);                // its first compacted page
   int pg0 = (int)(gp0 - st0);                   // the segment's first page in the stream
   int i0 = 0;                                   // unit-relative index of that page
-  int inext = 0;                                // next page of the unit
   int ring = 0;                                 // position in the group's stage ring
   uint32_t phase = 0;
   while (i0 < npages) {
     const int64_t st1 = lay_start(L, s + 1);
     const int i1 = (int)tmin<int64_t>(npages, i0 + (st1 - st0 - pg0));   // pages [i0, i1)
     const int Ts = lay_tokens(L, s);            // valid tokens of the stream
-    if (inext < i1) load_q(s);
-    for (; inext < i1; ++inext) {
-      const int pg = pg0 + (inext - i0) - cph;  // page in the stream; < 0: a placeholder
-      if (pg < 0) continue;
-      const int st = grp * G::SG + ring;
-      if (!s_abort && !mbar_wait_poll(&full[st], phase)) {
-        atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
-        s_abort = 1;
-      }
-      const uint8_t* pgb = smem + G::STAGE0 + st * G::PB;
-      const int tok0 = pg * kPageTokens + tw * 16;
-
-      if (tok0 < Ts) {
-        // ---------------- scores: S^T tile (16 tokens x 8 heads) --------------
-        const int r0 = tw * 16 + gq, r1 = r0 + 8;
-        uint32_t wk0[KQW], wk1[KQW];
-        load_bits<KQB, KQA>(pgb + r0 * G::KROW, tq * KQB, wk0);
-        load_bits<KQB, KQA>(pgb + r1 * G::KROW, tq * KQB, wk1);
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        float acc2[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t wq0[QQW], wq1[QQW];
-        if constexpr (QJL) {
-          load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r0 * G::QROW, tq * QQB, wq0);
-          load_bits<QQB, (QQB % 32) == 0>(pgb + G::OFF_Q + r1 * G::QROW, tq * QQB, wq1);
+    const int ir0 = tmax(i0, i0 + cph - pg0);   // first real (non-placeholder) page
+    if (ir0 < i1) load_q(s);
+    for (int ip = ir0; ip < i1; ip += 2) {
+      const int npair = tmin(2, i1 - ip);       // pages taken this round
+      if (half < npair) {
+        const int rp = ring + half;             // ring slot of this warp's page
+        const int st = grp * G::SG + (rp >= G::SG ? rp - G::SG : rp);
+        const uint32_t ph = phase ^ (rp >= G::SG ? 1u : 0u);
+        if (!s_abort && !mbar_wait_poll(&full[st], ph)) {
+          atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
+          s_abort = 1;
         }
-  #pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          uint32_t a[4];
-          const int o0 = (4 * j) * KB, o1 = (4 * j + 2) * KB;   // quad entries 4j.., 4j+2..
-          if constexpr (G::FAST) {
-            // pair bytes 2j and 2j + 1 of the quad
-            const int wi = j >> 1, b0 = 2 * (j & 1);
-            a[0] = lds32(smem, fast_addr(wk0[wi], lane4, b0));
-            a[1] = lds32(smem, fast_addr(wk1[wi], lane4, b0));
-            a[2] = lds32(smem, fast_addr(wk0[wi], lane4, b0 + 1));
-            a[3] = lds32(smem, fast_addr(wk1[wi], lane4, b0 + 1));
-          } else if constexpr (Lut<KB>::kPair) {
-            a[0] = lds32(lutk, field_addr<2 * KB>(wk0, o0, lane4));
-            a[1] = lds32(lutk, field_addr<2 * KB>(wk1, o0, lane4));
-            a[2] = lds32(lutk, field_addr<2 * KB>(wk0, o1, lane4));
-            a[3] = lds32(lutk, field_addr<2 * KB>(wk1, o1, lane4));
-          } else {
-            a[0] = lds16(lutk, getbits(wk0, o0, KB) << 1) | (lds16(lutk, getbits(wk0, o0 + KB, KB) << 1) << 16);
-            a[1] = lds16(lutk, getbits(wk1, o0, KB) << 1) | (lds16(lutk, getbits(wk1, o0 + KB, KB) << 1) << 16);
-            a[2] = lds16(lutk, getbits(wk0, o1, KB) << 1) | (lds16(lutk, getbits(wk0, o1 + KB, KB) << 1) << 16);
-            a[3] = lds16(lutk, getbits(wk1, o1, KB) << 1) | (lds16(lutk, getbits(wk1, o1 + KB, KB) << 1) << 16);
+        const uint8_t* pgb = smem + G::STAGE0 + st * G::PB;
+        const int pg = pg0 + (ip + half - i0) - cph;   // page in the stream (real)
+        const int tokw = pg * kPageTokens + wt0;       // the warp's first token
+
+        if (tokw < Ts) {
+          float sc[2][4];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) tile_scores(pgb, wt0 + 16 * t + gq, sc[t]);
+          // rows beyond the stream's tokens take no weight
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int r = tokw + 16 * t + gq;
+            if (r >= Ts) { sc[t][0] = kNegInf; sc[t][1] = kNegInf; }
+            if (r + 8 >= Ts) { sc[t][2] = kNegInf; sc[t][3] = kNegInf; }
           }
-          mma_f16_16816(acc, a, qf[j][0], qf[j][1]);
-          if constexpr (QJL) {
-            uint32_t b[4];
-  #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int pr = 2 * j + h;                 // pair index in the quad
-              const int ch = pr / SP, pin = pr % SP;
-              const int pe = ch * 2 * SP + pin, po = pe + SP;
-              const int wi = pe >> 5;
-              b[2 * h + 0] = sign_pair(wq0[wi], pe & 31, po - (wi << 5));
-              b[2 * h + 1] = sign_pair(wq1[wi], pe & 31, po - (wi << 5));
+          // ---------------- online softmax over the 32 tokens (columns =
+          // heads 2tq, 2tq+1); the running max only moves when a lane's
+          // grows, checked once per warp
+          float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][2]), fmaxf(sc[1][0], sc[1][2]));
+          float mx1 = fmaxf(fmaxf(sc[0][1], sc[0][3]), fmaxf(sc[1][1], sc[1][3]));
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+          }
+          if (__any_sync(0xffffffffu, mx0 > m0 || mx1 > m1)) {
+            const float n0m = fmaxf(m0, mx0), n1m = fmaxf(m1, mx1);
+            const float c0 = n0m == m0 ? 1.f : fast_exp2(m0 - n0m);
+            const float c1 = n1m == m1 ? 1.f : fast_exp2(m1 - n1m);
+            l0 *= c0;
+            l1 *= c1;
+#pragma unroll
+            for (int i2 = 0; i2 < NJ; ++i2) {
+              O[i2][0] *= c0; O[i2][2] *= c0;
+              O[i2][1] *= c1; O[i2][3] *= c1;
             }
-            mma_f16_16816(acc2, b, sqf[j][0], sqf[j][1]);
+            m0 = n0m;
+            m1 = n1m;
+          }
+          const float b0s = m0 == kNegInf ? 0.f : m0, b1s = m1 == kNegInf ? 0.f : m1;
+          const __half* vn = reinterpret_cast<const __half*>(pgb + G::OFF_VN);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int r0 = wt0 + 16 * t + gq;
+            const float p00 = fast_exp2(sc[t][0] - b0s), p01 = fast_exp2(sc[t][1] - b1s);
+            const float p10 = fast_exp2(sc[t][2] - b0s), p11 = fast_exp2(sc[t][3] - b1s);
+            l0 += p00 + p10;
+            l1 += p01 + p11;
+            // ---------------- P' = p * ||v|| -> B fragments ---------------
+            // (a masked row has p = 0; its norm slot may be stale)
+            const float v0 = __half2float(vn[r0]), v1 = __half2float(vn[r0 + 8]);
+            const uint32_t pb0 = movmatrix_trans(pack_half2(p00 == 0.f ? 0.f : p00 * v0,
+                                                            p01 == 0.f ? 0.f : p01 * v0));
+            const uint32_t pb1 = movmatrix_trans(pack_half2(p10 == 0.f ? 0.f : p10 * v1,
+                                                            p11 == 0.f ? 0.f : p11 * v1));
+            tile_pv(pgb, wt0 + 16 * t, pb0, pb1);
           }
         }
-        const __half* kn = reinterpret_cast<const __half*>(pgb + G::OFF_KN);
-        const __half* vn = reinterpret_cast<const __half*>(pgb + G::OFF_VN);
-        const bool ok0 = tok0 + gq < Ts, ok1 = tok0 + gq + 8 < Ts;
-        const float n0 = __half2float(kn[r0]), n1 = __half2float(kn[r1]);
-        float s00 = acc[0] * n0, s01 = acc[1] * n0, s10 = acc[2] * n1, s11 = acc[3] * n1;
-        if constexpr (QJL) {
-          const __half* kr = reinterpret_cast<const __half*>(pgb + G::OFF_KR);
-          const float g0 = __half2float(kr[r0]), g1 = __half2float(kr[r1]);
-          s00 = fmaf(acc2[0], g0, s00); s01 = fmaf(acc2[1], g0, s01);
-          s10 = fmaf(acc2[2], g1, s10); s11 = fmaf(acc2[3], g1, s11);
-        }
-        if (!ok0) { s00 = kNegInf; s01 = kNegInf; }
-        if (!ok1) { s10 = kNegInf; s11 = kNegInf; }
-
-        // ---------------- online softmax (columns = heads 2tq, 2tq+1) ---------
-        float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
-  #pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-        }
-        if (mx0 > m0) {            // rescale only when the running max grows
-          const float c = fast_exp2(m0 - mx0);
-          l0 *= c;
-  #pragma unroll
-          for (int i2 = 0; i2 < NJ; ++i2) { O[i2][0] *= c; O[i2][2] *= c; }
-          m0 = mx0;
-        }
-        if (mx1 > m1) {
-          const float c = fast_exp2(m1 - mx1);
-          l1 *= c;
-  #pragma unroll
-          for (int i2 = 0; i2 < NJ; ++i2) { O[i2][1] *= c; O[i2][3] *= c; }
-          m1 = mx1;
-        }
-        const float b0s = m0 == kNegInf ? 0.f : m0, b1s = m1 == kNegInf ? 0.f : m1;
-        const float p00 = fast_exp2(s00 - b0s), p01 = fast_exp2(s01 - b1s);
-        const float p10 = fast_exp2(s10 - b0s), p11 = fast_exp2(s11 - b1s);
-        l0 += p00 + p10;
-        l1 += p01 + p11;
-
-        // ---------------- P' = p * ||v|| -> B fragments -----------------------
-        const float v0 = ok0 ? __half2float(vn[r0]) : 0.f;
-        const float v1 = ok1 ? __half2float(vn[r1]) : 0.f;
-        const uint32_t pb0 = movmatrix_trans(pack_half2(p00 * v0, p01 * v0));
-        const uint32_t pb1 = movmatrix_trans(pack_half2(p10 * v1, p11 * v1));
-
-        // ---------------- O^T += V^T P ----------------------------------------
-        const int t0r = tw * 16 + 2 * tq;
-        uint32_t wa[VOW], wb[VOW], wc[VOW], wd[VOW];
-        load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 0) * G::VROW, gq * VOB, wa);
-        load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 1) * G::VROW, gq * VOB, wb);
-        load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 8) * G::VROW, gq * VOB, wc);
-        load_bits<VOB, VOA>(pgb + G::OFF_V + (t0r + 9) * G::VROW, gq * VOB, wd);
-        if constexpr (G::FAST && VB == 2) {
-          // bytes of lo (hi): codes at positions 4k, 4k+1 (4k+2, 4k+3) of token
-          // a in the low nibble and of token b in the high nibble
-          const uint32_t lab = (wa[0] & 0x0F0F0F0Fu) | ((wb[0] << 4) & 0xF0F0F0F0u);
-          const uint32_t hab = ((wa[0] >> 4) & 0x0F0F0F0Fu) | (wb[0] & 0xF0F0F0F0u);
-          const uint32_t lcd = (wc[0] & 0x0F0F0F0Fu) | ((wd[0] << 4) & 0xF0F0F0F0u);
-          const uint32_t hcd = ((wc[0] >> 4) & 0x0F0F0F0Fu) | (wd[0] & 0xF0F0F0F0u);
-          const uint32_t lane_v = 128u + ((uint32_t)(lane & 15) << 3);
-  #pragma unroll
-          for (int i2 = 0; i2 < NJ; ++i2) {
-            const uint2 eab = lds64(smem, fast_addr((i2 & 1) ? hab : lab, lane_v, i2 >> 1));
-            const uint2 ecd = lds64(smem, fast_addr((i2 & 1) ? hcd : lcd, lane_v, i2 >> 1));
-            const uint32_t a[4] = {eab.x, eab.y, ecd.x, ecd.y};
-            mma_f16_16816(O[i2], a, pb0, pb1);
-          }
-        } else if constexpr (G::FAST && VB == 4) {
-          // per word: byte k of lo (hi) = code at position 2k (2k+1) of token a,
-          // and of token b in the high nibble
-          uint32_t lab[2], hab[2], lcd[2], hcd[2];
-  #pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            lab[x] = (wa[x] & 0x0F0F0F0Fu) | ((wb[x] << 4) & 0xF0F0F0F0u);
-            hab[x] = ((wa[x] >> 4) & 0x0F0F0F0Fu) | (wb[x] & 0xF0F0F0F0u);
-            lcd[x] = (wc[x] & 0x0F0F0F0Fu) | ((wd[x] << 4) & 0xF0F0F0F0u);
-            hcd[x] = ((wc[x] >> 4) & 0x0F0F0F0Fu) | (wd[x] & 0xF0F0F0F0u);
-          }
-          const uint32_t lane_v = 128u + lane4;
-  #pragma unroll
-          for (int i2 = 0; i2 < NJ; ++i2) {
-            const int x = i2 >> 2, k = i2 & 3;
-            const uint32_t a[4] = {lds32(smem, fast_addr(lab[x], lane_v, k)),
-                                   lds32(smem, fast_addr(hab[x], lane_v, k)),
-                                   lds32(smem, fast_addr(lcd[x], lane_v, k)),
-                                   lds32(smem, fast_addr(hcd[x], lane_v, k))};
-            mma_f16_16816(O[i2], a, pb0, pb1);
-          }
-        } else if constexpr (VINTER) {
-          // combine the two tokens of each pair word-wise: field c of lo/hi is
-          // (code of token a) | (code of token b) << VB
-          constexpr uint32_t M = VB == 1 ? 0x55555555u : VB == 2 ? 0x33333333u : 0x0F0F0F0Fu;
-          uint32_t lab[VOW], hab[VOW], lcd[VOW], hcd[VOW];
-  #pragma unroll
-          for (int x = 0; x < VOW; ++x) {
-            lab[x] = (wa[x] & M) | ((wb[x] << VB) & ~M);
-            hab[x] = ((wa[x] >> VB) & M) | (wb[x] & ~M);
-            lcd[x] = (wc[x] & M) | ((wd[x] << VB) & ~M);
-            hcd[x] = ((wc[x] >> VB) & M) | (wd[x] & ~M);
-          }
-          constexpr int PER = 32 / VB;                 // codes per word
-  #pragma unroll
-          for (int i2 = 0; i2 < NJ; ++i2) {
-            const int c0 = 2 * i2;                     // even position -> lo, odd -> hi
-            const int o = ((c0 % PER) & ~1) * VB + (c0 / PER) * 32;
-            uint32_t a[4];
-            a[0] = lds32(lutv, field_addr<2 * VB>(lab, o, lane4));
-            a[1] = lds32(lutv, field_addr<2 * VB>(hab, o, lane4));
-            a[2] = lds32(lutv, field_addr<2 * VB>(lcd, o, lane4));
-            a[3] = lds32(lutv, field_addr<2 * VB>(hcd, o, lane4));
-            mma_f16_16816(O[i2], a, pb0, pb1);
-          }
-        } else {
-  #pragma unroll
-          for (int i2 = 0; i2 < NJ; ++i2) {
-            const int c0p = (2 * i2) * VB, c1p = (2 * i2 + 1) * VB;
-            uint32_t a[4];
-            if constexpr (Lut<VB>::kPair) {
-              a[0] = lds32(lutv, (((getbits(wb, c0p, VB) << VB) | getbits(wa, c0p, VB)) << 7 | lane4));
-              a[1] = lds32(lutv, (((getbits(wb, c1p, VB) << VB) | getbits(wa, c1p, VB)) << 7 | lane4));
-              a[2] = lds32(lutv, (((getbits(wd, c0p, VB) << VB) | getbits(wc, c0p, VB)) << 7 | lane4));
-              a[3] = lds32(lutv, (((getbits(wd, c1p, VB) << VB) | getbits(wc, c1p, VB)) << 7 | lane4));
-            } else {
-              a[0] = lds16(lutv, (getbits(wa, c0p, VB) << 1)) | (lds16(lutv, (getbits(wb, c0p, VB) << 1)) << 16);
-              a[1] = lds16(lutv, (getbits(wa, c1p, VB) << 1)) | (lds16(lutv, (getbits(wb, c1p, VB) << 1)) << 16);
-              a[2] = lds16(lutv, (getbits(wc, c0p, VB) << 1)) | (lds16(lutv, (getbits(wd, c0p, VB) << 1)) << 16);
-              a[3] = lds16(lutv, (getbits(wc, c1p, VB) << 1)) | (lds16(lutv, (getbits(wd, c1p, VB) << 1)) << 16);
-            }
-            mma_f16_16816(O[i2], a, pb0, pb1);
-          }
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
       }
-
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-      if (++ring == G::SG) { ring = 0; phase ^= 1u; }
+      ring += npair;
+      if (ring >= G::SG) { ring -= G::SG; phase ^= 1u; }
     }
 
     // ---------------- segment end: combine warps, emit partial ---------------
