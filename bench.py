@@ -21,7 +21,8 @@ bitwise against NCCL's (`gather_exact`).
 Extra keys of the same JSON line: `serving` (256 sequences x 4096 context,
 K3+QJL/V3, KV heads split over the N ranks: strong scaling), `long_context`
 (1 GPU: Qwen2.5-14B shapes, B1/B4 x 32K/128K, bit widths 2/3/4), `append`
-(prefill append GB/s), `prefill_attention` (TFLOP/s) and `ragged_decode`
+(prefill append GB/s, 48 layers at 4 bits), `append_qjl` (the headline's
+K4+QJL/V2 prefill append), `prefill_attention` (TFLOP/s) and `ragged_decode`
 (continuous batching).
 
 The JSON line's `value` is decode tokens/s over all ranks (global batch /
@@ -563,9 +564,10 @@ def run_ours(args, rank, world, local_rank):
             r = measure_decode(LW, args, rank, world, local_rank, e2e=False)
             long_ctx.append(_summary(LW, r, world, hbm_peak, args))
 
-    append_line = prefill_line = ragged_line = None
+    append_line = append_qjl_line = prefill_line = ragged_line = None
     if rank == 0 and not args.skip_append and args.workload == "mixtral":
         append_line = bench_append(dev, args)
+        append_qjl_line = bench_append_qjl(dev, args)
         prefill_line = bench_prefill(dev, args)
         ragged_line = bench_ragged(dev, args)
 
@@ -610,6 +612,7 @@ def run_ours(args, rank, world, local_rank):
             "serving": serving,
             "long_context": long_ctx,
             "append": append_line,
+            "append_qjl": append_qjl_line,
             "prefill_attention": prefill_line,
             "ragged_decode": ragged_line,
             "device_status": main["status"] | main.get("gather_check_status", 0),
@@ -684,6 +687,61 @@ def bench_append(dev, args):
     return {"workload": f"prefill append {L} layers x B{B} x Hkv{H} x {T} tokens, D{Dd}, "
                         f"K{bits}/V{bits}, bf16 in", "ms": ms, "gbs": alg / (ms / 1e3) / 1e9,
             "token_heads_per_s": th / (ms / 1e3), "algorithmic_bytes": alg}
+
+
+def bench_append_qjl(dev, args):
+    """Prefill append of the headline configuration (Mixtral attention shapes:
+    B16 x Hkv8 x 8192 tokens x D128, K 4-bit + 1-bit QJL sketch, V 2-bit),
+    bf16 K/V in: 512 B read + 118 B written per token-head.  Four layers' page
+    sets written in turn (distinct memory; the 537 MB input exceeds L2)."""
+    import torch
+    from bhaskera_col_b200.inference import ops
+    from bhaskera_col_b200.inference.kv_cache import (FastLloydMaxCodebook, _generate_qjl_matrix,
+                                                      _generate_rotation_matrix)
+    L, B, H, T, Dd, kb, vb = 4, 16, 8, 8192, 128, 4, 2
+    kc, vc = FastLloydMaxCodebook.get(Dd, kb, dev), FastLloydMaxCodebook.get(Dd, vb, dev)
+    tables = [ops.LayerTables(Dd, kb, vb, True, kc.centroids, kc.boundaries, vc.centroids,
+                              vc.boundaries,
+                              _generate_rotation_matrix(Dd, 42 + 13 * i, dev).contiguous(),
+                              _generate_qjl_matrix(Dd, 42 + 13 * i, dev).contiguous())
+              for i in range(L)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(17)
+    sc = torch.ones(Dd, device=dev)
+    sc[torch.randperm(Dd, generator=torch.Generator().manual_seed(7))[:2].to(dev)] = 8.0
+    k = (torch.randn((B, H, T, Dd), device=dev, generator=gen) * sc).to(torch.bfloat16)
+    v = (torch.randn((B, H, T, Dd), device=dev, generator=gen) * sc).to(torch.bfloat16)
+    pb = ops.page_bytes(Dd, kb, vb, True)
+    pages = [torch.zeros((B * H, T // 64, pb), dtype=torch.uint8, device=dev) for _ in range(L)]
+
+    def run():
+        for i in range(L):
+            ops.append(tables[i], pages[i], k, v, 0)
+
+    run()
+    torch.cuda.synchronize()
+    reps = max(1, min(args.steps, 3))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps / L
+    th = B * H * T
+    alg = th * (2 * Dd * 2 + pb // 64)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["hbm_gbs"])
+    except Exception:
+        peak = 6650.0
+    gbs = alg / (ms / 1e3) / 1e9
+    return {"workload": f"prefill append of one layer: B{B} x Hkv{H} x {T} tokens, D{Dd}, "
+                        f"K{kb}+QJL/V{vb}, bf16 in (average over {L} layers' page sets)",
+            "ms_per_layer": ms, "gbs": gbs, "frac_of_hbm": gbs / peak,
+            "token_heads_per_s": th / (ms / 1e3), "algorithmic_bytes_per_layer": alg,
+            "tensor_cores": ops.append_uses_tensor_cores(tables[0], k, v),
+            "device_status": ops.device_status(dev)}
 
 
 def bench_prefill(dev, args):

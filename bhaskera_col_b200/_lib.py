@@ -28,7 +28,8 @@ EXPORTED = (
     "tq_last_error", "tq_version", "tq_page_bytes", "tq_quantize_rotated",
     "tq_append", "tq_dequantize", "tq_decode_workspace_bytes", "tq_decode_attn",
     "tq_decode_step", "tq_decode_attn_noalloc", "tq_noalloc_status", "tq_workspace_status", "tq_device_status",
-    "tq_append_tensor_core", "tq_prefill_attn", "tq_prefill_tensor_core",
+    "tq_append_tensor_core", "tq_prefill_attn", "tq_prefill_workspace_bytes",
+    "tq_prefill_tensor_core",
     "tq_shared_alloc", "tq_shared_open", "tq_shared_close", "tq_shared_free",
     "tq_tables_bytes", "tq_init_tables",
 )
@@ -54,7 +55,8 @@ class Tables(ctypes.Structure):
                 ("v_centroids", ctypes.c_void_p), ("v_boundaries", ctypes.c_void_p),
                 ("rot", ctypes.c_void_p), ("qjl", ctypes.c_void_p),
                 ("rot_t", ctypes.c_void_p), ("qjl_t", ctypes.c_void_p),
-                ("rot_bf16x3", ctypes.c_void_p), ("rot_f16", ctypes.c_void_p)]
+                ("rot_bf16x3", ctypes.c_void_p), ("rot_f16", ctypes.c_void_p),
+                ("qjl_bf16", ctypes.c_void_p)]
 
 
 class Cache(ctypes.Structure):
@@ -80,13 +82,16 @@ class DecodeArgs(ctypes.Structure):
                 ("n_tokens", ctypes.c_int64), ("num_q_heads", ctypes.c_int64),
                 ("scale", ctypes.c_float), ("num_ctas", ctypes.c_int32),
                 ("phases", ctypes.c_int32), ("gather", ctypes.POINTER(Gather)),
-                ("seq_lens", ctypes.c_void_p)]
+                ("seq_lens", ctypes.c_void_p), ("kv_start", ctypes.c_void_p)]
 
 
 class PrefillArgs(ctypes.Structure):
     _fields_ = [("q", ctypes.POINTER(Tensor4)), ("out", ctypes.POINTER(Tensor4)),
                 ("n_tokens", ctypes.c_int64), ("scale", ctypes.c_float),
-                ("causal", ctypes.c_int32), ("engine", ctypes.c_int32)]
+                ("causal", ctypes.c_int32), ("engine", ctypes.c_int32),
+                ("kv_start", ctypes.c_void_p),
+                ("window_k", ctypes.POINTER(Tensor4)), ("window_v", ctypes.POINTER(Tensor4)),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
 
 
 _lock = threading.Lock()
@@ -124,6 +129,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
             "tq_device_status": (I32, [P(ctypes.c_uint32), VP]),
             "tq_append_tensor_core": (I32, [P(Geom), P(Tables), P(Tensor4), P(Tensor4)]),
             "tq_prefill_attn": (I32, [P(Geom), P(Tables), P(Cache), P(PrefillArgs), VP]),
+            "tq_prefill_workspace_bytes": (SZ, [P(Geom), P(Cache), P(PrefillArgs)]),
             "tq_prefill_tensor_core": (I32, [P(Geom)]),
             "tq_shared_alloc": (I32, [SZ, P(ctypes.c_void_p), VP]),
             "tq_shared_open": (I32, [VP, P(ctypes.c_void_p)]),

@@ -396,16 +396,55 @@ int32_t tq_prefill_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
     set_error("%s: B * Hq = %lld exceeds the grid limit 65535", fn, (long long)(B * Hq));
     return TQ_ERR_INVALID;
   }
-  if (a->n_tokens < Tq || a->n_tokens > c->pages_per_stream * TQ_PAGE_TOKENS) {
-    set_error("%s: n_tokens %lld must lie in [Tq = %lld, capacity %lld]", fn,
+  int64_t W = 0;
+  if (a->window_k || a->window_v) {
+    if (!a->window_k || !a->window_v) {
+      set_error("%s: window_k and window_v come together", fn);
+      return TQ_ERR_INVALID;
+    }
+    if ((rc = check_t4(a->window_k, "window_k", fn)) || (rc = check_t4(a->window_v, "window_v", fn)))
+      return rc;
+    W = a->window_k->shape[2];
+    for (int i = 0; i < 4; ++i)
+      if (a->window_k->shape[i] != a->window_v->shape[i]) {
+        set_error("%s: window_k and window_v shapes differ", fn);
+        return TQ_ERR_INVALID;
+      }
+    if (a->window_k->shape[0] != B || a->window_k->shape[1] != c->streams / B ||
+        a->window_k->shape[3] != g->head_dim) {
+      set_error("%s: the window must be (B, Hkv, W, head_dim)", fn);
+      return TQ_ERR_INVALID;
+    }
+    if (W > 0 && (a->engine == 1 || !prefill_tc_applies(g))) {
+      set_error("%s: a residual window needs the tcgen05 kernel (head_dim 128, 2-4 bit codes, "
+                "engine 0, 2 or 3)", fn);
+      return TQ_ERR_INVALID;
+    }
+    if (W > 0 && (!a->workspace || a->workspace_bytes < tq_prefill_workspace_bytes(g, c, a) ||
+                  reinterpret_cast<uintptr_t>(a->workspace) % 256)) {
+      set_error("%s: a residual window needs a 256-byte aligned workspace of %zu bytes", fn,
+                tq_prefill_workspace_bytes(g, c, a));
+      return TQ_ERR_WORKSPACE;
+    }
+  }
+  if (a->n_tokens < Tq || a->n_tokens < W ||
+      a->n_tokens - W > c->pages_per_stream * TQ_PAGE_TOKENS) {
+    set_error("%s: n_tokens %lld must lie in [Tq = %lld, capacity %lld + window %lld]", fn,
               (long long)a->n_tokens, (long long)Tq,
-              (long long)(c->pages_per_stream * TQ_PAGE_TOKENS));
+              (long long)(c->pages_per_stream * TQ_PAGE_TOKENS), (long long)W);
     return TQ_ERR_INVALID;
   }
   if (!(a->scale > 0.f)) { set_error("%s: scale must be positive", fn); return TQ_ERR_INVALID; }
   uint32_t* status = device_status_word();
   if (!status) { set_error("%s: device status word unavailable", fn); return TQ_ERR_CUDA; }
   return launch_prefill(g, t, c, a, status, (cudaStream_t)stream);
+}
+
+size_t tq_prefill_workspace_bytes(const tq_geom* g, const tq_cache* c, const tq_prefill_args* a) {
+  if (!g || !c || !a || !a->window_k || a->window_k->shape[2] <= 0) return 0;
+  // the window rotated into fp16, K then V: [streams][W][head_dim] each
+  const size_t one = (size_t)c->streams * (size_t)a->window_k->shape[2] * (size_t)g->head_dim * 2;
+  return 2 * ((one + 255) & ~(size_t)255);
 }
 
 int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream) {
@@ -483,7 +522,7 @@ int32_t tq_shared_free(void* dptr) {
 namespace {
 
 struct TableLayout {
-  size_t kc, kb, vc, vb, rot, rot_t, qjl, qjl_t, bf3, f16, total;
+  size_t kc, kb, vc, vb, rot, rot_t, qjl, qjl_t, bf3, f16, qb, total;
 };
 
 TableLayout table_layout(const tq_geom* g) {
@@ -505,6 +544,7 @@ TableLayout table_layout(const tq_geom* g) {
   L.qjl_t = g->qjl ? take(DD * 4) : 0;
   L.bf3 = D == 128 ? take(6 * DD * 2) : 0;
   L.f16 = take(DD * 2);
+  L.qb = g->qjl && D == 128 ? take(DD * 2) : 0;
   L.total = off;
   return L;
 }
@@ -590,6 +630,16 @@ int32_t tq_init_tables(const tq_geom* g, const float* k_centroids, const float* 
         }
       }
   }
+  // S in bf16 for the tensor-core sketch, rows and columns in K quad order,
+  // only when every entry is exactly a bf16 value
+  bool qb_ok = g->qjl && D == 128;
+  if (qb_ok) {
+    for (size_t i = 0; i < DD && qb_ok; ++i) qb_ok = bf16_value(bf16_bits(qjl[i])) == qjl[i];
+    uint16_t* qb = reinterpret_cast<uint16_t*>(host.data() + L.qb);
+    for (int p = 0; qb_ok && p < D; ++p)
+      for (int c = 0; c < D; ++c)
+        qb[(size_t)p * D + c] = bf16_bits(qjl[(size_t)k_coord_at(p, D) * D + k_coord_at(c, D)]);
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemcpyAsync(device_buf, host.data(), L.total, cudaMemcpyHostToDevice, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
@@ -608,6 +658,7 @@ int32_t tq_init_tables(const tq_geom* g, const float* k_centroids, const float* 
   t->qjl_t = g->qjl ? reinterpret_cast<const float*>(base + L.qjl_t) : nullptr;
   t->rot_bf16x3 = D == 128 ? reinterpret_cast<const uint16_t*>(base + L.bf3) : nullptr;
   t->rot_f16 = reinterpret_cast<const uint16_t*>(base + L.f16);
+  t->qjl_bf16 = qb_ok ? reinterpret_cast<const uint16_t*>(base + L.qb) : nullptr;
   return TQ_OK;
 }
 

@@ -34,7 +34,10 @@
 
 namespace tq {
 
-constexpr int kTileWarps = 4;     // warps sharing one 64-token page (16 tokens each)
+constexpr int kTileWarps = 4;     // warps of a page group (two per page, 32 tokens each)
+// dynamic shared memory a decode CTA may take: the 227 KB opt-in limit less
+// 1 KB for the kernel's static shared memory
+constexpr int kSmemBudget = 226 * 1024;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegInf = -INFINITY;
 
@@ -50,6 +53,7 @@ struct PageLayout {
   const int32_t* lens;    // [B] tokens of each batch row; NULL: uniform (T each)
   int32_t* cum;           // [S + 1] ragged: first compacted page of each stream
   int32_t* rq;            // ragged: pages per unit
+  const int32_t* kstart;  // [B] first attended position of each batch row (left padding); NULL: 0
 };
 
 // A ragged layout opens every non-empty stream with this many placeholder
@@ -67,6 +71,13 @@ __device__ __forceinline__ int lay_tokens(const PageLayout& L, int64_t s) {
   if (!L.lens) return (int)L.T;
   const int64_t n = __ldg(L.lens + s / L.hkv);
   return (int)(n < 0 ? 0 : n > L.T ? L.T : n);
+}
+
+// First position stream s attends (left padding), >= 0.
+__device__ __forceinline__ int lay_kstart(const PageLayout& L, int64_t s) {
+  if (!L.kstart) return 0;
+  const int v = __ldg(L.kstart + s / L.hkv);
+  return v < 0 ? 0 : v;
 }
 
 // The stream owning compacted page x (< cum[S]): the largest s with
@@ -254,7 +265,11 @@ struct Dec {
   static constexpr int NG = NCW / kTileWarps;          // page groups
   static constexpr int THREADS = 32 * (NCW + 1);       // + one producer warp
   static constexpr int MINB = FAST ? 1 : 3;            // CTAs per SM
-  static constexpr int SG = 4;                          // stages per page group (pages go in pairs)
+  // stages per page group (pages go in pairs): 4, or 3 where four do not fit
+  // beside the FAST table and its combine scratch
+  static constexpr int SG =
+      (FAST && 65536 + NG * 4 * PB + 2 * NG * 4 * 8 + 128 + NCW * (16 + 8 * D) * 4 > kSmemBudget)
+          ? 3 : 4;
   static constexpr int STAGES = NG * SG;
   static constexpr int COMB = NCW * (16 + 8 * D) * 4;
   static constexpr int FLUT = 65536;
@@ -266,7 +281,7 @@ struct Dec {
   static constexpr int BARS = STAGE0 + STAGES * PB;
   static constexpr int COMB_OFF = align128(BARS + 2 * STAGES * 8);
   static constexpr int SMEM = FAST ? COMB_OFF + COMB : BARS + 2 * STAGES * 8;
-  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(SMEM <= kSmemBudget, "shared memory");
 };
 
 // The K4 / V2|V4 table region (see Dec::FAST): rows [r0, r1) of 256 B, one
@@ -325,6 +340,7 @@ decode_kernel(DecodeParams p) {
 
   __shared__ __align__(128) unsigned char s_lut0[G::REGION0];
   __shared__ __align__(128) unsigned char s_lutv_static[G::LUTV_STATIC];
+  unsigned char* stages = smem + G::STAGE0;
   unsigned char* lutk = G::FAST ? smem : s_lut0;
   unsigned char* lutv = G::FAST ? smem : G::VSTATIC ? s_lutv_static : smem + G::LUTV;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::BARS);
@@ -430,7 +446,7 @@ decode_kernel(DecodeParams p) {
         const int64_t ps = pok ? cur : 0;
         const uint8_t* src = p.pages + ps * (int64_t)G::PAGE;
         mbar_expect_tx(&full[st], (uint32_t)G::PAGE);
-        bulk_g2s(smem + G::STAGE0 + st * G::PB, src, (uint32_t)G::PAGE, &full[st]);
+        bulk_g2s(stages + st * G::PB, src, (uint32_t)G::PAGE, &full[st]);
         issued = ++kr;
       }
       if (s_abort) {   // never leave with a copy still writing shared memory
@@ -650,6 +666,7 @@ decode_kernel(DecodeParams p) {
     const int64_t st1 = lay_start(L, s + 1);
     const int i1 = (int)tmin<int64_t>(npages, i0 + (st1 - st0 - pg0));   // pages [i0, i1)
     const int Ts = lay_tokens(L, s);            // valid tokens of the stream
+    const int Ks = lay_kstart(L, s);            // first attended token (left padding)
     const int ir0 = tmax(i0, i0 + cph - pg0);   // first real (non-placeholder) page
     if (ir0 < i1) load_q(s);
     for (int ip = ir0; ip < i1; ip += 2) {
@@ -662,20 +679,21 @@ decode_kernel(DecodeParams p) {
           atomicOr(p.status, TQ_DEV_WAIT_TIMEOUT);
           s_abort = 1;
         }
-        const uint8_t* pgb = smem + G::STAGE0 + st * G::PB;
+        const uint8_t* pgb = stages + st * G::PB;
         const int pg = pg0 + (ip + half - i0) - cph;   // page in the stream (real)
         const int tokw = pg * kPageTokens + wt0;       // the warp's first token
 
-        if (tokw < Ts) {
+        if (tokw < Ts && tokw + 32 > Ks) {
           float sc[2][4];
 #pragma unroll
           for (int t = 0; t < 2; ++t) tile_scores(pgb, wt0 + 16 * t + gq, sc[t]);
-          // rows beyond the stream's tokens take no weight
+          // rows beyond the stream's tokens or before its first attended
+          // token take no weight
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             const int r = tokw + 16 * t + gq;
-            if (r >= Ts) { sc[t][0] = kNegInf; sc[t][1] = kNegInf; }
-            if (r + 8 >= Ts) { sc[t][2] = kNegInf; sc[t][3] = kNegInf; }
+            if (r >= Ts || r < Ks) { sc[t][0] = kNegInf; sc[t][1] = kNegInf; }
+            if (r + 8 >= Ts || r + 8 < Ks) { sc[t][2] = kNegInf; sc[t][3] = kNegInf; }
           }
           // ---------------- online softmax over the 32 tokens (columns =
           // heads 2tq, 2tq+1); the running max only moves when a lane's
@@ -1139,10 +1157,12 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
 #pragma unroll
         for (int h = 0; h < 8; ++h) acc[h] = fmaf(qv[h * D + c], kx, acc[h]);
       }
+      // window token t sits at position (the row's packed tokens) + t
+      const bool masked = lay_tokens(p.lay, s) + t < lay_kstart(p.lay, s);
 #pragma unroll
       for (int h = 0; h < 8; ++h) {
         const float v = warp_sum(acc[h]);
-        if (lane == 0) sc[h * W + t] = v * p.scale_log2;
+        if (lane == 0) sc[h * W + t] = masked ? kNegInf : v * p.scale_log2;
       }
     }
     __syncthreads();
@@ -1272,26 +1292,31 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
     }
   }
   if (p.world > 1) {
-    // Completion of the fused all-gather.  Each CTA's peer stores are made
-    // visible system-wide (fence) before the CTA counts itself done on its own
-    // GPU; the rank's last CTA then adds one arrival to every rank's counter
-    // (release at system scope) and waits until the counter reaches
+    // Completion of the fused all-gather.  The CTA's barrier orders all its
+    // threads' peer stores before thread 0, whose system-scope fence makes
+    // them (cumulatively) visible to every GPU before the CTA counts itself
+    // done on its own GPU: one fence per CTA, not one per thread.  The rank's
+    // last CTA then acquires the other CTAs' counts and adds one arrival to
+    // every rank's counter (a release at system scope, cumulative over the
+    // other CTAs' fenced stores it has acquired) and waits until the counter reaches
     // (calls completed + 1) * world.  The counter only grows (wrap-safe
     // compare), so a late arrival after a timed-out wait still lands in its
     // own call's count, and no rank can arrive twice before every rank has
     // arrived once (its next arrival needs its own wait to have passed).
-    __threadfence_system();
     __syncthreads();
     if (tid == 0) {
+      __threadfence_system();
       uint32_t* arrived = p.peer_flag[p.rank];
       uint32_t* done = arrived + 1;
       uint32_t* calls = arrived + 2;
       const uint32_t nctas = gridDim.x * gridDim.y;
       if (atomicAdd(done, 1u) + 1u == nctas) {
-        // every other CTA of this rank has finished: reset the local count for
-        // the layer's next call (which starts after this grid completes)
+        // every other CTA of this rank has finished: acquire their counts (so
+        // their fenced stores precede the release below), and reset the local
+        // count for the layer's next call (which starts after this grid
+        // completes)
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         *done = 0u;
-        __threadfence_system();
         for (int r = 0; r < p.world; ++r)
           asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.peer_flag[r]) : "memory");
         const uint32_t ncall = *calls + 1u;
@@ -1453,6 +1478,7 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   lay.S = pl.S; lay.Pv = pl.Pv; lay.T = pl.T; lay.Q = pl.Q;
   lay.hkv = (int)Hkv; lay.nid = pl.nid;
   lay.lens = a->seq_lens;
+  lay.kstart = a->kv_start;
   lay.cum = reinterpret_cast<int32_t*>(w + pl.off_cum);
   lay.rq = reinterpret_cast<int32_t*>(w + kWsRaggedQ);
 

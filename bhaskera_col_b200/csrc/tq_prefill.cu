@@ -46,6 +46,7 @@ struct PrefillParams {
   float scale;                  // softmax scale
   int causal;
   int nqb;                      // query blocks per head
+  const int32_t* kv_start;      // [B] first attended key of each batch row, or NULL
   uint32_t* status;
 };
 
@@ -119,6 +120,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(PrefillParams p)
   const int64_t qpos_max = t_base + tmin<int64_t>((int64_t)(qb + 1) * P, p.Tq) - 1;
   const int64_t kend = p.causal ? qpos_max + 1 : p.n_tokens;   // keys this CTA needs
   const int ntiles = (int)((kend + 63) / 64);
+  int64_t kst = 0;                                     // first attended key (left padding)
+  if (p.kv_start) {
+    const int v = __ldg(p.kv_start + b);
+    kst = v < 0 ? 0 : v;
+  }
 
   if (tid == 0) {
     mbar_init(&full[0], 1);
@@ -290,8 +296,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(PrefillParams p)
           const int64_t key = k0 + kl;
           const float nk = kn[kl];
           float v0 = s[n][c] * nk, v1 = s[n][2 + c] * nk;
-          const bool lim0 = key < p.n_tokens && (!p.causal || key <= qp0);
-          const bool lim1 = key < p.n_tokens && (!p.causal || key <= qp1);
+          const bool lim0 = key < p.n_tokens && key >= kst && (!p.causal || key <= qp0);
+          const bool lim1 = key < p.n_tokens && key >= kst && (!p.causal || key <= qp1);
           v0 = lim0 ? v0 : -INFINITY;
           v1 = lim1 ? v1 : -INFINITY;
           s[n][c] = v0;
@@ -445,6 +451,7 @@ int launch_prefill(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   p.n_tokens = a->n_tokens;
   p.scale = a->scale;
   p.causal = a->causal;
+  p.kv_start = a->kv_start;
   p.nqb = (int)((p.Tq + 16 * (kPfWarps / p.hc) - 1) / (16 * (kPfWarps / p.hc)));
   p.status = status;
   if (p.Tq == 0) return TQ_OK;

@@ -309,6 +309,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
     const bool valid = t < p.Tq;
     const int64_t qpos = valid ? t_base + t : qpos_max;
     const int64_t lim = p.causal ? qpos : p.n_tokens - 1;    // keys <= lim are seen
+    const int64_t kst = row_kstart(p.kv_start, b);           // keys >= kst are seen
     bool ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status));
     if (ok) {
       // q' (fp32, K order) -> fp16 pairs in tensor memory (A of the S MMA)
@@ -342,7 +343,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
       if (!ok) break;
       tc::tc_fence_after();
       const int64_t k0 = (int64_t)j * kKeys;
-      const bool need_mask = k0 + kKeys - 1 > lim;
+      const bool need_mask = k0 + kKeys - 1 > lim || k0 < kst;
       const uint32_t scol = tl + s * 128;
       // pass 1: row max (four independent 3-input chains)
       float mx;
@@ -356,8 +357,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
           tmem_ld_wait(x0);
           tmem_ld_wait(x1);
           if (need_mask) {
-            mask_keys(x0, lim - (k0 + 64 * hh));
-            mask_keys(x1, lim - (k0 + 64 * hh + 32));
+            mask_keys(x0, kst - (k0 + 64 * hh), lim - (k0 + 64 * hh));
+            mask_keys(x1, kst - (k0 + 64 * hh + 32), lim - (k0 + 64 * hh + 32));
           }
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
@@ -389,8 +390,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
         tmem_ld_wait(x0);
         tmem_ld_wait(x1);
         if (need_mask) {
-          mask_keys(x0, lim - (k0 + 64 * hh));
-          mask_keys(x1, lim - (k0 + 64 * hh + 32));
+          mask_keys(x0, kst - (k0 + 64 * hh), lim - (k0 + 64 * hh));
+          mask_keys(x1, kst - (k0 + 64 * hh + 32), lim - (k0 + 64 * hh + 32));
         }
         uint32_t h[32];
 #pragma unroll
@@ -537,6 +538,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
       pv.part = part;
     }
     pv.kend = kend;
+    pv.W = p.W;
+    pv.kpacked = p.n_tokens - p.W;
     const unsigned char* lk = sm + OFF_LUT + 4 * (lane & (p.rk - 1));
     const unsigned char* lv = sm + OFF_LUT + 4 * nk * p.rk + 4 * (lane & (p.rv - 1));
     const int rk4 = 4 * p.rk, rv4 = 4 * p.rv;
@@ -548,6 +551,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
     bool ok = true;
     load_half<KB>(kc, pv, 0, 0, p.off_kn);
     decode_half<KB>(kc, lk, rk4, sm + OFF_K, co);
+    if (tile_has_window(pv, 0)) window_half<2>(pv, 0, p.wk, sm + OFF_K, co);
     tc::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL]);
@@ -564,6 +568,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
                              p.status);
         if (!__all_sync(0xffffffffu, ok)) break;
         decode_half<KB>(kc, lk, rk4, sm + OFF_K + sk * kStage, co);
+        if (tile_has_window(pv, jk)) window_half<2>(pv, jk, p.wk, sm + OFF_K + sk * kStage, co);
         tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL + sk]);
@@ -577,6 +582,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
         ok = wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) break;
       decode_half<VB>(vc, lv, rv4, sm + OFF_V + s * kStage, co);
+      if (tile_has_window(pv, j)) window_half<2>(pv, j, p.wv, sm + OFF_V + s * kStage, co);
       tc::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cta(&bars[B_VFULL + s]);
@@ -640,7 +646,7 @@ using TcFn = void (*)(TcPrefillParams);
 TcFn tc_fn(int kb, int vb) {
 #define TQ_PTC(K, V) if (kb == K && vb == V) return prefill_tc_kernel<K, V>;
   TQ_PTC(4, 2) TQ_PTC(4, 4) TQ_PTC(3, 3) TQ_PTC(2, 2) TQ_PTC(3, 2) TQ_PTC(4, 3)
-  TQ_PTC(2, 4) TQ_PTC(3, 4) TQ_PTC(2, 3)
+  TQ_PTC(2, 4) TQ_PTC(3, 4) TQ_PTC(2, 3) TQ_PTC(6, 4) TQ_PTC(5, 5) TQ_PTC(6, 6) TQ_PTC(5, 4)
 #undef TQ_PTC
   return nullptr;
 }
@@ -657,6 +663,50 @@ bool vec_ok(const tq_tensor4* x) {
 
 bool prefill_tc_applies(const tq_geom* G) {
   return G->head_dim == kD && tc_fn(G->key_bits, G->value_bits) != nullptr;
+}
+
+// The residual window rotated once for the prefill kernels: row w of stream
+// s of K (V) becomes fp16 (x R^T) with columns in K quad (V octet) order, the
+// order of the decoded tiles.  grid (streams, ceil(W / kWinRows), 2: K, V),
+// 128 threads; thread p computes position p of kWinRows rows from R^T and
+// the rows staged in shared memory.
+constexpr int kWinRows = 16;
+
+struct WinParams {
+  const void* x[2]; int dtype[2]; int64_t xs[2][4];
+  int64_t Hkv, W;
+  const float* rot_t;           // R^T [128][128]
+  __half* out[2];               // [streams][W][128]
+};
+
+__global__ void __launch_bounds__(128) window_rotate_kernel(WinParams p) {
+  extern __shared__ __align__(16) float wsm[];
+  float* rt = wsm;                        // [128][128] R^T
+  float* xr = rt + kD * kD;               // [kWinRows][128]
+  const int which = blockIdx.z, tid = threadIdx.x;
+  const int64_t s = blockIdx.x, b = s / p.Hkv, h = s % p.Hkv;
+  const int64_t w0 = (int64_t)blockIdx.y * kWinRows;
+  const int nrow = (int)tmin<int64_t>(kWinRows, p.W - w0);
+  stage_async(rt, p.rot_t, kD * kD * 4, tid, 128);
+  const int64_t* xs = p.xs[which];
+  for (int i = tid; i < nrow * kD; i += 128) {
+    const int r = i / kD, c = i % kD;
+    xr[i] = load_elem(p.x[which], p.dtype[which],
+                      b * xs[0] + h * xs[1] + (w0 + r) * xs[2] + c * xs[3]);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int coord = which == 0 ? k_coord(tid) : v_coord(tid);
+  float acc[kWinRows];
+#pragma unroll
+  for (int r = 0; r < kWinRows; ++r) acc[r] = 0.f;
+  for (int c = 0; c < kD; ++c) {
+    const float rc = rt[c * kD + coord];
+#pragma unroll
+    for (int r = 0; r < kWinRows; ++r) acc[r] = fmaf(xr[r * kD + c], rc, acc[r]);
+  }
+  for (int r = 0; r < nrow; ++r)
+    p.out[which][(s * p.W + w0 + r) * kD + tid] = __float2half_rn(acc[r]);
 }
 
 int launch_prefill_tc(const tq_geom* G, const tq_tables* t, const tq_cache* c,
@@ -690,6 +740,31 @@ int launch_prefill_tc(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   p.nqb = (int)((p.Tq + P - 1) / P);
   p.qscale = a->scale * kLog2e;
   p.causal = a->causal;
+  p.kv_start = a->kv_start;
+  p.W = a->window_k ? a->window_k->shape[2] : 0;
+  p.wk = p.wv = nullptr;
+  if (p.W > 0) {
+    // rotate the window into the workspace (K, then V)
+    const size_t one = tq_prefill_workspace_bytes(G, c, a) / 2;
+    WinParams wp;
+    const tq_tensor4* wx[2] = {a->window_k, a->window_v};
+    for (int i = 0; i < 2; ++i) {
+      wp.x[i] = wx[i]->data;
+      wp.dtype[i] = wx[i]->dtype;
+      for (int d = 0; d < 4; ++d) wp.xs[i][d] = wx[i]->stride[d];
+      wp.out[i] = reinterpret_cast<__half*>(static_cast<uint8_t*>(a->workspace) + i * one);
+    }
+    wp.Hkv = c->streams / a->q->shape[0];
+    wp.W = p.W;
+    wp.rot_t = t->rot_t;
+    const size_t wsmem = (size_t)(kD * kD + kWinRows * kD) * 4;
+    if (set_smem_attr((const void*)window_rotate_kernel, wsmem) != TQ_OK) return TQ_ERR_CUDA;
+    dim3 wgrid((unsigned)c->streams, (unsigned)((p.W + kWinRows - 1) / kWinRows), 2);
+    window_rotate_kernel<<<wgrid, 128, wsmem, st>>>(wp);
+    if (check_launch("tq_prefill_attn/window") != TQ_OK) return TQ_ERR_CUDA;
+    p.wk = wp.out[0];
+    p.wv = wp.out[1];
+  }
   // pair tables: 32 copies (one per lane) where they fit, else 16 / 8
   const int nk = 1 << (2 * G->key_bits), nv = 1 << (2 * G->value_bits);
   int rk = 32, rv = 32;

@@ -43,6 +43,12 @@ struct TcPrefillParams {
   float qscale;                 // softmax scale * log2(e)
   int causal;
   int rk, rv;                   // pair-table replication (lanes per copy set)
+  const int32_t* kv_start;      // [B] first attended key of each batch row, or NULL
+  // residual window: keys n_tokens - W .. n_tokens - 1 come rotated (fp16,
+  // [stream][W][128], K quad / V octet order) from wk / wv instead of pages
+  const __half* wk;
+  const __half* wv;
+  int64_t W;
   uint32_t* status;
 };
 
@@ -104,11 +110,19 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Scores of keys past `last` (an index into this 32-key chunk) -> -inf.
-__device__ __forceinline__ void mask_keys(uint32_t (&x)[32], int64_t last) {
+// Scores of keys before `first` or past `last` (indices into this 32-key
+// chunk) -> -inf.
+__device__ __forceinline__ void mask_keys(uint32_t (&x)[32], int64_t first, int64_t last) {
 #pragma unroll
   for (int e = 0; e < 32; ++e)
-    if (e > last) x[e] = 0xFF800000u;
+    if (e > last || e < first) x[e] = 0xFF800000u;
+}
+
+// The first key batch row b attends (left padding), >= 0.
+__device__ __forceinline__ int64_t row_kstart(const int32_t* kv_start, int64_t b) {
+  if (!kv_start) return 0;
+  const int v = __ldg(kv_start + b);
+  return v < 0 ? 0 : v;
 }
 
 // fp16 pair {exp2(a - bias), exp2(b - bias)} (a in the low half): the
@@ -124,15 +138,7 @@ __device__ __forceinline__ uint32_t exp2_pair(uint32_t a, uint32_t b, uint64_t n
   return p;
 }
 
-__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
-        "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
-        "r"(r[14]), "r"(r[15])
-      : "memory");
-}
+using tc::tmem_st_x16;
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
@@ -266,6 +272,8 @@ struct TcParamsView {
   int page_bytes, off_v, off_kn, off_vn;
   int kk, part;
   int64_t kend;                 // keys this CTA needs
+  int64_t kpacked;              // keys [0, kpacked) are in pages, the rest in the window
+  int64_t W;                    // window tokens (rows of the rotated window buffers)
 };
 
 // One operand's codes and norms that a decoder thread needs for one tile:
@@ -282,10 +290,11 @@ __device__ __forceinline__ void load_half(HalfRegs<NB, NR>& t, const TcParamsVie
                                           int off_codes, int off_norm) {
   constexpr int RPP = NR / 2, STEP = 64 / RPP;
   const uint8_t* pgs[2];
+  const int64_t kpend = tmin<int64_t>(pv.kend, pv.kpacked);   // needed keys held in pages
 #pragma unroll
   for (int pgi = 0; pgi < 2; ++pgi) {
     pgs[pgi] = pv.pool;
-    if ((int64_t)j * kKeys + pgi * 64 < pv.kend) {     // the page holds needed keys
+    if ((int64_t)j * kKeys + pgi * 64 < kpend) {        // the page holds needed keys
       bool ok;
       const int64_t ps = page_slot(pv.pm, pv.stream, 2 * (int64_t)j + pgi, ok);
       if (!ok) atomicOr(pv.status, TQ_DEV_BAD_BLOCK);
@@ -296,7 +305,7 @@ __device__ __forceinline__ void load_half(HalfRegs<NB, NR>& t, const TcParamsVie
   for (int r = 0; r < NR; ++r) {
     const int pgi = r / RPP, key_in_page = pv.kk + STEP * (r % RPP);
     const int64_t key = (int64_t)j * kKeys + pgi * 64 + key_in_page;
-    if (key < pv.kend) {
+    if (key < kpend) {
       const uint8_t* pg = pgs[pgi];
       load_stream<NB>(t.c[r], pg + off_codes + key_in_page * (16 * NB) + pv.part * (4 * NB));
       t.n[r] = __ldg(reinterpret_cast<const unsigned short*>(pg + off_norm) + key_in_page);
@@ -323,6 +332,32 @@ __device__ __forceinline__ void decode_half(const HalfRegs<NB, NR>& t, const uns
   }
 }
 
+
+// Rows of tile j that lie in the residual window: copy the thread's 32
+// positions (4 chunks) of the rotated fp16 row straight into the tile, over
+// what decode_half wrote there (zeros: such rows load no codes).
+template <int NR>
+__device__ __forceinline__ void window_half(const TcParamsView& pv, int j, const __half* wbuf,
+                                            unsigned char* tile, const ChunkOffsets& co) {
+  constexpr int RPP = NR / 2, STEP = 64 / RPP;
+#pragma unroll
+  for (int r = 0; r < NR; ++r) {
+    const int pgi = r / RPP, kin = pv.kk + STEP * (r % RPP);
+    const int64_t key = (int64_t)j * kKeys + pgi * 64 + kin;
+    if (key >= pv.kpacked && key < pv.kend) {
+      const uint4* src = reinterpret_cast<const uint4*>(
+          wbuf + ((pv.stream * pv.W + (key - pv.kpacked)) * kD + pv.part * 32));
+      unsigned char* row = tile + (pgi * 64 + STEP * (r % RPP)) * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(row + co.o[q]) = __ldg(src + q);
+    }
+  }
+}
+
+// Does tile j hold any window key this CTA needs?
+__device__ __forceinline__ bool tile_has_window(const TcParamsView& pv, int j) {
+  return pv.W > 0 && (int64_t)(j + 1) * kKeys > pv.kpacked && (int64_t)j * kKeys < pv.kend;
+}
 
 }  // namespace pftc
 

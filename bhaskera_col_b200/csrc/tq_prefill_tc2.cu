@@ -295,6 +295,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
     const bool valid = id.pos < p.Tq;
     const int64_t qpos = valid ? t_base + id.pos : qpos_max;
     const int64_t lim = p.causal ? qpos : p.n_tokens - 1;    // keys <= lim are seen
+    const int64_t kst = row_kstart(p.kv_start, b);           // keys >= kst are seen
     bool ok = __all_sync(0xffffffffu, wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status));
     if (ok) {
       // q'_X (fp32, K order) -> fp16 A operand over Q_X
@@ -326,7 +327,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
       if (!ok) break;
       tc::tc_fence_after();
       const int64_t k0 = (int64_t)j * kKeys;
-      const bool need_mask = k0 + kKeys - 1 > lim;
+      const bool need_mask = k0 + kKeys - 1 > lim || k0 < kst;
       // pass 1: row max (four independent 3-input chains)
       float mx;
       {
@@ -339,8 +340,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
           tmem_ld_wait(x0);
           tmem_ld_wait(x1);
           if (need_mask) {
-            mask_keys(x0, lim - (k0 + 64 * hh));
-            mask_keys(x1, lim - (k0 + 64 * hh + 32));
+            mask_keys(x0, kst - (k0 + 64 * hh), lim - (k0 + 64 * hh));
+            mask_keys(x1, kst - (k0 + 64 * hh + 32), lim - (k0 + 64 * hh + 32));
           }
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
@@ -385,8 +386,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
         tmem_ld_wait(x0);
         tmem_ld_wait(x1);
         if (need_mask) {
-          mask_keys(x0, lim - (k0 + 64 * hh));
-          mask_keys(x1, lim - (k0 + 64 * hh + 32));
+          mask_keys(x0, kst - (k0 + 64 * hh), lim - (k0 + 64 * hh));
+          mask_keys(x1, kst - (k0 + 64 * hh + 32), lim - (k0 + 64 * hh + 32));
         }
         uint32_t h[32];
 #pragma unroll
@@ -496,6 +497,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
       pv.part = part;
     }
     pv.kend = kend;
+    pv.W = p.W;
+    pv.kpacked = p.n_tokens - p.W;
     const unsigned char* lk = sm + OFF_LUT + 4 * (lane & (p.rk - 1));
     const unsigned char* lv = sm + OFF_LUT + 4 * nk * p.rk + 4 * (lane & (p.rv - 1));
     const int rk4 = 4 * p.rk, rv4 = 4 * p.rv;
@@ -505,6 +508,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
     bool ok = true;
     load_half<KB>(kc, pv, 0, 0, p.off_kn);
     decode_half<KB>(kc, lk, rk4, sm + OFF_K, co);
+    if (tile_has_window(pv, 0)) window_half<4>(pv, 0, p.wk, sm + OFF_K, co);
     tc::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL]);
@@ -521,6 +525,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
                              p.status);
         if (!__all_sync(0xffffffffu, ok)) break;
         decode_half<KB>(kc, lk, rk4, sm + OFF_K + sk * kStage, co);
+        if (tile_has_window(pv, jk)) window_half<4>(pv, jk, p.wk, sm + OFF_K + sk * kStage, co);
         tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL + sk]);
@@ -535,6 +540,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
         ok = wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) break;
       decode_half<VB>(vc, lv, rv4, sm + OFF_V + s * kStage, co);
+      if (tile_has_window(pv, j)) window_half<4>(pv, j, p.wv, sm + OFF_V + s * kStage, co);
       tc::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cta(&bars[B_VFULL + s]);
@@ -584,7 +590,7 @@ using TcFn = void (*)(TcPrefillParams);
 TcFn tc2_fn(int kb, int vb) {
 #define TQ_PTC(K, V) if (kb == K && vb == V) return prefill_tc2_kernel<K, V>;
   TQ_PTC(4, 2) TQ_PTC(4, 4) TQ_PTC(3, 3) TQ_PTC(2, 2) TQ_PTC(3, 2) TQ_PTC(4, 3)
-  TQ_PTC(2, 4) TQ_PTC(3, 4) TQ_PTC(2, 3)
+  TQ_PTC(2, 4) TQ_PTC(3, 4) TQ_PTC(2, 3) TQ_PTC(6, 4) TQ_PTC(5, 5) TQ_PTC(6, 6) TQ_PTC(5, 4)
 #undef TQ_PTC
   return nullptr;
 }

@@ -15,10 +15,18 @@ With ``fused_attention=True`` the cache's ``update()`` stores nothing and
 hands the new K/V straight back; the registered attention function then
 stores them and attends in one call: ``cache.decode`` for a single-token step
 (append fused into the decode kernels), ``cache.prefill`` for a prompt chunk
-(append, then the prefill-attention kernel).  Cases the kernels do not cover
--- a padding mask, or a prompt chunk with a nonzero residual window -- store
-the tokens and run transformers' SDPA on the dense dequantised K/V, which is
-exactly the reference's computation.
+(append, then the prefill-attention kernel, the residual window's tokens
+entering exactly).  A padded batch (batched ``generate`` pads prompts on the
+left) reaches the same kernels: the mask builder turns the 2-D padding mask
+into each row's first real position on the device (no host synchronisation)
+and the kernels give the padding keys no weight.  Only other masks (sliding
+windows, custom mask functions, a 4-D mask from the caller) and, with a
+residual window, layers whose bit widths have no tensor-core prefill kernel
+store the tokens and run transformers' SDPA on the dense dequantised K/V,
+which is exactly the reference's computation.
+
+A padding mask must be left padding (zeros, then ones), the form
+``generate`` produces for decoder-only models.
 
 transformers calls the attention function of a layer right after that
 layer's ``update()`` on the same thread, so the cache marks itself as the
@@ -49,6 +57,13 @@ def current():
     return cache
 
 
+def _left_pad(attention_mask) -> Optional[torch.Tensor]:
+    """The per-row first real position the mask builder attached, or None."""
+    if attention_mask is not None and getattr(attention_mask, "_tq_left_pad", False):
+        return attention_mask
+    return None
+
+
 def turboquant_attention(module: torch.nn.Module, query: torch.Tensor, key: torch.Tensor,
                          value: torch.Tensor, attention_mask: Optional[torch.Tensor],
                          scaling: Optional[float] = None, dropout: float = 0.0, **kwargs):
@@ -56,42 +71,59 @@ def turboquant_attention(module: torch.nn.Module, query: torch.Tensor, key: torc
     (B, Hkv, T, D) K/V -> ((B, T, Hq, D) output, None)."""
     if dropout:
         raise ValueError("turboquant attention is inference-only (dropout must be 0)")
+    from . import ops
     cache = current()
     layer = module.layer_idx
     T = query.shape[2]
-    if attention_mask is None and T == 1:
-        out = cache.decode(query, key, value, layer, scale=scaling)
-    elif attention_mask is None and cache.residual_window <= 0:
-        out = cache.prefill(query, key, value, layer, scale=scaling, causal=True)
-    else:
-        # reference path: store, then SDPA over the dense dequantised K/V
-        from transformers.integrations.sdpa_attention import sdpa_attention_forward
+    pad = _left_pad(attention_mask)
+    if attention_mask is None or pad is not None:
+        if T == 1:
+            out = cache.decode(query, key, value, layer, scale=scaling, kv_start=pad)
+            return out.transpose(1, 2).contiguous(), None
         store = cache._stores[layer]
-        store.store(key, value, cache.residual_window)
-        k_all, v_all = store.dense()
-        if attention_mask is None and T > 1:
-            # causal, aligned to the end: query i sits at position kv - T + i
-            kv = k_all.shape[2]
-            pos = torch.arange(kv, device=query.device)
-            qpos = torch.arange(kv - T, kv, device=query.device)
-            attention_mask = (pos[None, :] <= qpos[:, None])[None, None]
-        return sdpa_attention_forward(module, query, k_all, v_all, attention_mask,
-                                      dropout=0.0, scaling=scaling, **kwargs)
-    return out.transpose(1, 2).contiguous(), None
+        if cache.residual_window <= 0 or ops.prefill_uses_tensor_cores(store.tables):
+            out = cache.prefill(query, key, value, layer, scale=scaling, causal=True,
+                                kv_start=pad)
+            return out.transpose(1, 2).contiguous(), None
+    # reference path: store, then SDPA over the dense dequantised K/V
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+    store = cache._stores[layer]
+    store.store(key, value, cache.residual_window)
+    k_all, v_all = store.dense()
+    kv = k_all.shape[2]
+    if attention_mask is None or pad is not None:
+        # causal, aligned to the end: query i sits at position kv - T + i;
+        # keys before a row's first real position are padding
+        pos = torch.arange(kv, device=query.device)
+        qpos = torch.arange(kv - T, kv, device=query.device)
+        m = (pos[None, :] <= qpos[:, None])[None, None]
+        if pad is not None:
+            m = m & (pos[None, None, None, :] >= pad.long()[:, None, None, None])
+        attention_mask = m
+    return sdpa_attention_forward(module, query, k_all, v_all, attention_mask,
+                                  dropout=0.0, scaling=scaling, **kwargs)
 
 
 def turboquant_mask(batch_size: int, q_length: int, kv_length: int, q_offset: int = 0,
                     kv_offset: int = 0, mask_function=None, attention_mask=None,
                     local_size: Optional[int] = None, **kwargs):
-    """Mask builder for the attention function: no mask for a plain causal
-    pattern without padding (the kernels take causality from token positions,
-    also for a prompt chunk after cached tokens), else SDPA's mask."""
+    """Mask builder for the attention function.  A plain causal pattern needs
+    no mask (the kernels take causality from token positions, also for a
+    prompt chunk after cached tokens); with a 2-D left-padding mask it returns
+    each row's first real position, kv_length - (real tokens), an int32 (B,)
+    tensor computed on the device and marked for the attention function.
+    Anything else gets SDPA's mask."""
     from transformers.masking_utils import causal_mask_function, sdpa_mask
     if mask_function is None:
         mask_function = causal_mask_function
-    if (local_size is None and mask_function is causal_mask_function
-            and (attention_mask is None or bool(attention_mask.all()))):
-        return None
+    if local_size is None and mask_function is causal_mask_function and kv_offset == 0:
+        if attention_mask is None:
+            return None
+        if attention_mask.dim() == 2:
+            real = attention_mask[:, :kv_length].to(torch.int32).sum(-1, dtype=torch.int32)
+            pad = (kv_length - real).to(torch.int32).contiguous()
+            pad._tq_left_pad = True
+            return pad
     return sdpa_mask(batch_size, q_length, kv_length, q_offset=q_offset, kv_offset=kv_offset,
                      mask_function=mask_function, attention_mask=attention_mask,
                      local_size=local_size, **kwargs)

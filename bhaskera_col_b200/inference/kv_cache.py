@@ -70,10 +70,12 @@ def _generate_rotation_matrix(d: int, seed: int = 42,
 
 def _generate_qjl_matrix(d: int, rotation_seed: int,
                          device: torch.device = torch.device("cpu")) -> torch.Tensor:
-    """i.i.d. N(0,1) (d, d) sketch matrix for the 1-bit QJL residual."""
+    """(d, d) sketch matrix for the 1-bit QJL residual: i.i.d. N(0,1) draws
+    rounded to bf16 (exact bf16 values, so the tensor-core append forms S r
+    with a single S term; the rounding moves each entry by < 2^-9 of itself)."""
     gen = torch.Generator(device="cpu")
     gen.manual_seed(rotation_seed + QJL_SEED_OFFSET)
-    return torch.randn(d, d, generator=gen).to(device)
+    return torch.randn(d, d, generator=gen).bfloat16().float().to(device)
 
 
 # ---------------------------------------------------------------------------
@@ -253,6 +255,9 @@ class _LayerKVStore:
         self._dense_valid = 0
         self._allocated = False
         self.workspace = ops.DecodeWorkspace()
+        # scratch of a windowed prefill (the rotated window); kept apart from the
+        # decode workspace, whose first word is the decode status word
+        self.prefill_workspace = ops.DecodeWorkspace()
 
     # -- storage -------------------------------------------------------------
     def _lazy_alloc(self, B: int, H: int) -> None:
@@ -338,17 +343,18 @@ class _LayerKVStore:
 
     # -- fused decode attention ----------------------------------------------
     def attend(self, q: torch.Tensor, scale: Optional[float] = None,
-               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+               out: Optional[torch.Tensor] = None,
+               kv_start: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Single-token attention of q (B, Hq, 1, D) over everything stored."""
         if not self._allocated:
             raise RuntimeError("attend() before any token was stored in this layer")
         return ops.decode_attention(self.tables, self._pages, q, self._comp_ptr,
                                     self._win_k, self._win_v, scale=scale, out=out,
-                                    workspace=self.workspace)
+                                    workspace=self.workspace, kv_start=kv_start)
 
     def decode(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, residual_window: int,
                scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
-               gather=None) -> torch.Tensor:
+               gather=None, kv_start: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Store one new token and attend q to everything stored, in one fused
         call when exactly one token moves into packed storage this step.
         ``gather`` (a _lib.Gather, see head_parallel.SharedGather) fuses the
@@ -364,7 +370,8 @@ class _LayerKVStore:
         if T == 1 and residual_window <= 0 and W == 0:
             self._ensure_capacity(1)
             out = ops.decode_step(self.tables, self._pages, k, v, self._comp_ptr, q, scale=scale,
-                                  out=out, workspace=self.workspace, gather=gather)
+                                  out=out, workspace=self.workspace, gather=gather,
+                                  kv_start=kv_start)
             self._comp_ptr += 1
             return out
         if T == 1 and 0 < residual_window == W:
@@ -375,24 +382,28 @@ class _LayerKVStore:
             self._ensure_capacity(1)
             out = ops.decode_step(self.tables, self._pages, ek, ev, self._comp_ptr, q,
                                   window_k=wk, window_v=wv, scale=scale, out=out,
-                                  workspace=self.workspace)
+                                  workspace=self.workspace, kv_start=kv_start)
             self._comp_ptr += 1
             self._win_k, self._win_v = wk, wv
             return out
         self.store(k, v, residual_window)
-        return self.attend(q, scale=scale, out=out)
+        return self.attend(q, scale=scale, out=out, kv_start=kv_start)
 
     def prefill(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, residual_window: int,
                 scale: Optional[float] = None, causal: bool = True,
-                out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Store T new tokens and return the attention of q (B, Hq, T, D) at
-        their positions over everything stored, straight off the pages."""
-        if residual_window > 0 or self._win_k is not None:
-            raise ValueError("fused prefill attention needs residual_window == 0 "
-                             "(window tokens stay dense; use update() instead)")
+                out: Optional[torch.Tensor] = None,
+                kv_start: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Store T new tokens (reference window semantics) and return the
+        attention of q (B, Hq, T, D) at their positions over everything stored:
+        the packed tokens straight off the pages, the residual window's tokens
+        exactly.  ``kv_start`` (int32 (B,)): left padding per batch row."""
         self.store(k, v, residual_window)
-        return ops.prefill_attention(self.tables, self._pages, q, self._comp_ptr, scale=scale,
-                                     causal=causal, out=out)
+        W = 0 if self._win_k is None else self._win_k.shape[2]
+        return ops.prefill_attention(self.tables, self._pages, q, self._comp_ptr + W,
+                                     scale=scale, causal=causal, out=out, kv_start=kv_start,
+                                     window_k=self._win_k if W else None,
+                                     window_v=self._win_v if W else None,
+                                     workspace=self.prefill_workspace)
 
     def reset(self) -> None:
         self._comp_ptr = 0
@@ -490,25 +501,28 @@ class TurboQuantKVCache(BaseKVCache):
 
     def decode(self, query_states: torch.Tensor, key_states: torch.Tensor,
                value_states: torch.Tensor, layer_idx: int, scale: Optional[float] = None,
-               out: Optional[torch.Tensor] = None, gather=None) -> torch.Tensor:
+               out: Optional[torch.Tensor] = None, gather=None,
+               kv_start: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One decode step of one layer: store the new token(s) (reference
         update() semantics, including the residual window) and return the
         attention of query_states (B, Hq, 1, D) over the whole cache, without
-        materialising dense K/V."""
+        materialising dense K/V.  ``kv_start`` (int32 (B,) on the device):
+        each batch row's first attended position (left padding)."""
         return self._stores[layer_idx].decode(query_states, key_states, value_states,
                                               self.residual_window, scale=scale, out=out,
-                                              gather=gather)
+                                              gather=gather, kv_start=kv_start)
 
     def prefill(self, query_states: torch.Tensor, key_states: torch.Tensor,
                 value_states: torch.Tensor, layer_idx: int, scale: Optional[float] = None,
-                causal: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """A prefill forward of one layer: store the T new tokens and return the
-        causal attention of query_states (B, Hq, T, D) over the whole cache
-        (the SDPA that follows update() in the reference), without dense K/V.
-        Needs residual_window == 0."""
+                causal: bool = True, out: Optional[torch.Tensor] = None,
+                kv_start: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """A prefill forward of one layer: store the T new tokens (residual
+        window included) and return the causal attention of query_states
+        (B, Hq, T, D) over the whole cache (the SDPA that follows update() in
+        the reference), without dense K/V.  ``kv_start``: left padding."""
         return self._stores[layer_idx].prefill(query_states, key_states, value_states,
                                                self.residual_window, scale=scale,
-                                               causal=causal, out=out)
+                                               causal=causal, out=out, kv_start=kv_start)
 
     def device_status(self) -> int:
         """OR of the device status words of all layers and of the library's

@@ -58,6 +58,7 @@ class LayerTables:
     qjl_t: Optional[torch.Tensor] = None
     rot_bf16x3: Optional[torch.Tensor] = None
     rot_f16: Optional[torch.Tensor] = None
+    qjl_bf16: Optional[torch.Tensor] = None
 
     def __post_init__(self):
         self.rot = self.rot.contiguous().float()
@@ -79,6 +80,13 @@ class LayerTables:
         if self.qjl_mat is not None:
             self.qjl_mat = self.qjl_mat.contiguous().float()
             self.qjl_t = self.qjl_mat.t().contiguous()
+            # the tensor-core append sketches with S in bf16: only when S is
+            # exactly bf16 (the library's own S is), rows and columns in K
+            # quad order (tq_tables.qjl_bf16)
+            sb = self.qjl_mat.bfloat16()
+            if self.head_dim == 128 and torch.equal(sb.float(), self.qjl_mat):
+                ko = torch.as_tensor(row_orders(self.head_dim)[0], device=self.qjl_mat.device)
+                self.qjl_bf16 = sb[ko][:, ko].contiguous()
 
     def __setattr__(self, name, value):
         # a changed table invalidates the cached C descriptors
@@ -113,6 +121,7 @@ class LayerTables:
         t.qjl_t = self.qjl_t.data_ptr() if self.qjl_t is not None else None
         t.rot_bf16x3 = self.rot_bf16x3.data_ptr() if self.rot_bf16x3 is not None else None
         t.rot_f16 = self.rot_f16.data_ptr() if self.rot_f16 is not None else None
+        t.qjl_bf16 = self.qjl_bf16.data_ptr() if self.qjl_bf16 is not None else None
         return t
 
 
@@ -265,8 +274,20 @@ def _seq_lens_ptr(seq_lens: Optional[torch.Tensor], q: torch.Tensor) -> Optional
     return seq_lens.data_ptr()
 
 
+def _row_ptr(x: Optional[torch.Tensor], q: torch.Tensor, name: str) -> Optional[int]:
+    """Device pointer of an int32 (B,) per-row tensor (seq_lens, kv_start)."""
+    if x is None:
+        return None
+    if x.dtype != torch.int32 or x.dim() != 1 or x.shape[0] != q.shape[0] or \
+            not x.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous int32 (B,) tensor")
+    if x.device != q.device:
+        raise ValueError(f"{name} must be on the query's device")
+    return x.data_ptr()
+
+
 def _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, keep,
-                 seq_lens=None):
+                 seq_lens=None, kv_start=None):
     qt, ot = tensor4(q), tensor4(out)
     wk = tensor4(window_k) if window_k is not None and window_k.shape[2] > 0 else None
     wv = tensor4(window_v) if wk is not None else None
@@ -282,6 +303,7 @@ def _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, 
     a.num_ctas = int(num_ctas)
     a.phases = int(phases)
     a.seq_lens = _seq_lens_ptr(seq_lens, q)
+    a.kv_start = _row_ptr(kv_start, q, "kv_start")
     return a
 
 
@@ -292,7 +314,8 @@ def decode_step(tables: LayerTables, pages: torch.Tensor, k_new: torch.Tensor,
                 out: Optional[torch.Tensor] = None,
                 workspace: Optional[DecodeWorkspace] = None,
                 num_ctas: int = 0, gather: Optional[_lib.Gather] = None,
-                seq_lens: Optional[torch.Tensor] = None) -> torch.Tensor:
+                seq_lens: Optional[torch.Tensor] = None,
+                kv_start: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Store the new (B, Hkv, 1, D) token at ``pos`` and attend q over tokens
     [0, pos + 1) plus the window, in one call (tq_decode_step).  ``gather``
     (a filled _lib.Gather whose peer_out[rank] is ``out``) also delivers the
@@ -300,14 +323,17 @@ def decode_step(tables: LayerTables, pages: torch.Tensor, k_new: torch.Tensor,
 
     ``seq_lens`` (int32 (B,) on the device, each <= pos + 1) makes the batch
     ragged: row b stores its token at seq_lens[b] - 1 and attends tokens
-    [0, seq_lens[b]); ``pos`` is then the bound (the longest row's position)."""
+    [0, seq_lens[b]); ``pos`` is then the bound (the longest row's position).
+    ``kv_start`` (int32 (B,) on the device): row b's keys before that position
+    take no weight (left padding)."""
     _require_cuda(pages, q, k_new, v_new)
     lib = _lib.load()
     if out is None:
         out = torch.empty_like(q)
     g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
     keep = []
-    a = _decode_args(q, out, pos + 1, window_k, window_v, scale, num_ctas, 0, keep, seq_lens)
+    a = _decode_args(q, out, pos + 1, window_k, window_v, scale, num_ctas, 0, keep, seq_lens,
+                     kv_start)
     if gather is not None:
         a.gather = ctypes.pointer(gather)
     kt, vt = tensor4(k_new), tensor4(v_new)
@@ -329,12 +355,20 @@ def prefill_uses_tensor_cores(tables: LayerTables) -> bool:
 
 def prefill_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
                       n_tokens: int, scale: Optional[float] = None, causal: bool = True,
-                      out: Optional[torch.Tensor] = None, engine: int = 0) -> torch.Tensor:
+                      out: Optional[torch.Tensor] = None, engine: int = 0,
+                      kv_start: Optional[torch.Tensor] = None,
+                      window_k: Optional[torch.Tensor] = None,
+                      window_v: Optional[torch.Tensor] = None,
+                      workspace: Optional[DecodeWorkspace] = None) -> torch.Tensor:
     """Attention of queries q (B, Hq, Tq, D) at positions n_tokens - Tq ..
     n_tokens - 1 over the packed tokens [0, n_tokens) of every stream (causal:
     a query sees keys at or before its position).  ``engine`` 0 picks the
     fastest kernel (tcgen05 where prefill_uses_tensor_cores), 1 the mma.sync
-    kernel, 2 / 3 the tcgen05 kernel with 128 / 256 query rows per CTA."""
+    kernel, 2 / 3 the tcgen05 kernel with 128 / 256 query rows per CTA.
+    ``kv_start`` (int32 (B,) on the device): row b's keys before that position
+    take no weight (left padding; a query with no key left returns zeros).
+    ``window_k`` / ``window_v`` ((B, Hkv, W, D)): the residual window, dense
+    keys at positions n_tokens - W .. n_tokens - 1 after the packed ones."""
     _require_cuda(pages, q)
     lib = _lib.load()
     if out is None:
@@ -343,7 +377,13 @@ def prefill_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
     qt, ot = tensor4(q), tensor4(out)
     a = _lib.PrefillArgs(ctypes.pointer(qt), ctypes.pointer(ot), int(n_tokens),
                          float(scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])),
-                         1 if causal else 0, int(engine))
+                         1 if causal else 0, int(engine), _row_ptr(kv_start, q, "kv_start"))
+    if window_k is not None and window_k.shape[2] > 0:
+        wk, wv = tensor4(window_k), tensor4(window_v)
+        a.window_k, a.window_v = ctypes.pointer(wk), ctypes.pointer(wv)
+        nbytes = lib.tq_prefill_workspace_bytes(ctypes.byref(g), ctypes.byref(c), ctypes.byref(a))
+        ws = (workspace or DecodeWorkspace()).get(nbytes, q.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _lib.check("tq_prefill_attn", lib.tq_prefill_attn(
         ctypes.byref(g), ctypes.byref(t), ctypes.byref(c), ctypes.byref(a), _stream(q.device)))
     return out
@@ -355,14 +395,17 @@ def decode_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
                      out: Optional[torch.Tensor] = None,
                      workspace: Optional[DecodeWorkspace] = None,
                      num_ctas: int = 0, phases: int = 0,
-                     seq_lens: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     seq_lens: Optional[torch.Tensor] = None,
+                     kv_start: Optional[torch.Tensor] = None) -> torch.Tensor:
     """softmax(q K^T * scale) V over the packed tokens [0, n_tokens) of every
     stream plus an optional full-precision window.  q: (B, Hq, 1, D).
 
     ``phases`` (OR of _lib.PHASE_*) runs a subset of the three kernels; the
     later phases read what the earlier ones left in the same ``workspace``.
     ``seq_lens`` (int32 (B,) on the device) gives each batch row its own
-    token count, clamped to [0, n_tokens] (continuous batching)."""
+    token count, clamped to [0, n_tokens] (continuous batching).  ``kv_start``
+    (int32 (B,) on the device): row b's keys before that position, window
+    tokens included, take no weight (left padding)."""
     _require_cuda(pages, q)
     lib = _lib.load()
     if out is None:
@@ -370,7 +413,7 @@ def decode_attention(tables: LayerTables, pages: torch.Tensor, q: torch.Tensor,
     g, t, c = tables.geom(), tables.ctables(), _cache_desc(pages)
     keep = []
     a = _decode_args(q, out, n_tokens, window_k, window_v, scale, num_ctas, phases, keep,
-                     seq_lens)
+                     seq_lens, kv_start)
     nbytes = lib.tq_decode_workspace_bytes(ctypes.byref(g), ctypes.byref(c), ctypes.byref(a))
     if nbytes == 0:
         raise _lib.TqError("tq_decode_workspace_bytes", _lib.TQ_ERR_INVALID, _lib.last_error())

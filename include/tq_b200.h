@@ -90,6 +90,12 @@ typedef struct tq_tables {
   const uint16_t* rot_bf16x3;
   /* R [D][D] fp16, row-major: required by tq_prefill_attn, unused elsewhere. */
   const uint16_t* rot_f16;
+  /* Optional, head_dim 128 with qjl only: S in bf16, [D][D], rows and columns
+   * in K quad order ([p][c] = S[k_order[p]][k_order[c]]).  Set only when every
+   * entry of S is exactly a bf16 value (the library's own S is); then
+   * tq_append computes the QJL sketch of bf16 inputs on the tensor cores with
+   * the same signs as the CUDA-core kernel up to fp32 rounding of z. */
+  const uint16_t* qjl_bf16;
 } tq_tables;
 
 /* Packed cache of one layer. */
@@ -212,6 +218,12 @@ typedef struct tq_decode_args {
    * token is stored at seq_lens[b] - 1 (nothing is stored where that is
    * negative).  Needs TQ_PHASE_QPREP in `phases` (0 = all phases). */
   const int32_t* seq_lens;
+  /* Left padding (HF batched generation): NULL, or a device int32[B] whose
+   * entry b is the first position row b attends; keys at earlier positions
+   * (packed and window alike; window token w sits at position n_b + w, n_b
+   * the row's packed tokens) take no weight.  A row whose every key is
+   * masked returns zeros. */
+  const int32_t* kv_start;
 } tq_decode_args;
 
 #define TQ_PHASE_QPREP 1       /* rotate + sketch the query                  */
@@ -242,10 +254,10 @@ int32_t tq_decode_step(const tq_geom* g, const tq_tables* t, const tq_cache* c,
  * stream's tokens [0, n_tokens) (causal: a query at position p attends keys
  * <= p), GQA with Hq a multiple of Hkv; out (B, Hq, Tq, D).  Keys and values
  * are the dequantised ones, n (c[idx] R) (MSE codes; a QJL sketch is not
- * used), so the result is SDPA over what update() returns at
- * residual_window 0.  head_dim 64 or 128; t->rot_f16 is required.  No
- * workspace; device-side wait timeouts go to the library status word
- * (tq_device_status).  Replaces HF attention over update()'s output in a
+ * used), so the result is SDPA over what update() returns; keys
+ * in a residual window (window_k/v below) enter exactly.  head_dim 64 or
+ * 128; t->rot_f16 is required.  Workspace only for a window; device-side
+ * wait timeouts go to the library status word (tq_device_status).  Replaces HF attention over update()'s output in a
  * prefill forward (kv_cache.py:483-488, engine.py:389). */
 typedef struct tq_prefill_args {
   const tq_tensor4* q;
@@ -259,10 +271,28 @@ typedef struct tq_prefill_args {
                                   longer than one 128-row block); 1: the
                                   mma.sync kernel; 2 / 3: the tcgen05 kernel
                                   with 128 / 256 rows per CTA                 */
+  /* Left padding: NULL, or a device int32[B]: row b's keys before position
+   * kv_start[b] take no weight (a query row with no key left returns zeros). */
+  const int32_t* kv_start;
+  /* Residual window (the reference's residual_window, kv_cache.py:461-477):
+   * NULL, or (B, Hkv, W, D) dense K and V of the stream's newest W tokens,
+   * which sit at positions n_tokens - W .. n_tokens - 1 after the packed
+   * tokens [0, n_tokens - W).  They are attended exactly as given (rotated
+   * once into fp16 in `workspace`, no quantisation).  Needs the tcgen05
+   * kernel (tq_prefill_tensor_core) and a workspace of
+   * tq_prefill_workspace_bytes. */
+  const tq_tensor4* window_k;
+  const tq_tensor4* window_v;
+  void* workspace;
+  size_t workspace_bytes;
 } tq_prefill_args;
 
 int32_t tq_prefill_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                         const tq_prefill_args* a, void* stream);
+
+/* Workspace bytes tq_prefill_attn needs for these arguments (the rotated
+ * residual window; 0 without one). */
+size_t tq_prefill_workspace_bytes(const tq_geom* g, const tq_cache* c, const tq_prefill_args* a);
 
 /* 1 when tq_prefill_attn with engine 0 runs on the tcgen05 tensor cores for
  * this geometry (head_dim 128, key and value codes of 2 to 4 bits), else 0. */
@@ -295,8 +325,9 @@ int32_t tq_noalloc_status(uint32_t* status, void* stream);
 int32_t tq_workspace_status(void* workspace, uint32_t* status, void* stream);
 
 /* 1 when tq_append with these arguments runs the tensor-core kernel (head_dim
- * 128, no QJL, bf16 views with 16-byte aligned rows, >= 32 tokens,
- * rot_bf16x3 set), 0 when it runs the CUDA-core kernel.  Host-only query. */
+ * 128, bf16 views with 16-byte aligned rows, >= 32 tokens, rot_bf16x3 set,
+ * and with qjl also qjl_bf16), 0 when it runs the CUDA-core kernel.
+ * Host-only query. */
 int32_t tq_append_tensor_core(const tq_geom* g, const tq_tables* t, const tq_tensor4* k,
                               const tq_tensor4* v);
 

@@ -110,12 +110,13 @@ def rotation_matrix(d: int, seed: int) -> np.ndarray:
 
 
 def qjl_matrix(d: int, rotation_seed: int) -> np.ndarray:
-    """Gaussian sketch matrix S (d x d, i.i.d. N(0,1)) for the QJL residual,
-    acting in the rotated basis.  Build-defined (no reference counterpart)."""
+    """Gaussian sketch matrix S (d x d, i.i.d. N(0,1) rounded to bf16) for the
+    QJL residual, acting in the rotated basis.  Build-defined (no reference
+    counterpart)."""
     import torch
     g = torch.Generator(device="cpu")
     g.manual_seed(rotation_seed + QJL_SEED_OFFSET)
-    return torch.randn(d, d, generator=g).numpy().astype(np.float32)
+    return torch.randn(d, d, generator=g).bfloat16().float().numpy().astype(np.float32)
 
 
 # =============================================================================
@@ -259,22 +260,32 @@ class TurboQuantCache:
 # =============================================================================
 
 def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool = False,
-         out_dtype: str = "float32") -> np.ndarray:
+         out_dtype: str = "float32", kv_start=None) -> np.ndarray:
     """softmax(q k^T / sqrt(D)) v with GQA repeat (query head j uses kv head
-    j // (Hq/Hkv)), computed in float64.  q (B,Hq,Tq,D), k/v (B,Hkv,T,D)."""
+    j // (Hq/Hkv)), computed in float64.  q (B,Hq,Tq,D), k/v (B,Hkv,T,D).
+    ``kv_start`` (B,): keys of row b before that position are padding (the
+    mask transformers builds from a left-padding mask); a query row with no
+    key left gives zeros."""
     B, Hq, Tq, D = q.shape
     Hkv = k.shape[1]
     g = Hq // Hkv
+    T = k.shape[2]
     kk = np.repeat(k.astype(np.float64), g, axis=1)
     vv = np.repeat(v.astype(np.float64), g, axis=1)
     s = np.einsum("bhqd,bhkd->bhqk", q.astype(np.float64), kk) / math.sqrt(D)
+    keep = np.ones((B, 1, Tq, T), bool)
     if causal:
-        T = k.shape[2]
         qpos = np.arange(T - Tq, T)[:, None]
-        s = np.where(np.arange(T)[None, :] <= qpos, s, -np.inf)
-    s -= s.max(-1, keepdims=True)
-    p = np.exp(s)
-    p /= p.sum(-1, keepdims=True)
+        keep &= (np.arange(T)[None, :] <= qpos)[None, None]
+    if kv_start is not None:
+        st = np.asarray(kv_start).reshape(B, 1, 1, 1)
+        keep &= np.arange(T)[None, None, None, :] >= st
+    s = np.where(keep, s, -np.inf)
+    mx = s.max(-1, keepdims=True)
+    none = ~np.isfinite(mx)
+    p = np.exp(s - np.where(none, 0.0, mx))
+    den = p.sum(-1, keepdims=True)
+    p = np.where(none, 0.0, p / np.where(none, 1.0, den))
     o = np.einsum("bhqk,bhkd->bhqd", p, vv)
     return cast_model_dtype(o.astype(np.float32), out_dtype)
 
@@ -495,7 +506,7 @@ def parse_pages(geom: PageGeom, pages: np.ndarray, T: int):
 
 def decode_attention_codes(q, k_idx, v_idx, k_norm, v_norm, kc, vc, R,
                            qbits=None, gamma=None, S=None, T=None,
-                           window_k=None, window_v=None):
+                           window_k=None, window_v=None, kv_start=None):
     """Single-query attention over a compressed history plus an optional
     full-precision window, in float64.
 
@@ -503,6 +514,8 @@ def decode_attention_codes(q, k_idx, v_idx, k_norm, v_norm, kc, vc, R,
     window (B, Hkv, W, D) unrotated.  The compressed part is evaluated in the
     rotated basis: q_rot = q R^T, score = n <q_rot, c[idx]> (+ QJL term
     gamma * alpha * <S q_rot, 2b-1>), output o = (sum p n_v c_v[idx]) R.
+    ``kv_start`` (B,): positions of row b before it (compressed position t,
+    window token w at T + w) are padding; a row with no key left gives zeros.
     Returns (B, Hq, D) float64.
     """
     B, Hq, D = q.shape
@@ -530,7 +543,12 @@ def decode_attention_codes(q, k_idx, v_idx, k_norm, v_norm, kc, vc, R,
             if window_k is not None and window_k.shape[2] > 0:
                 parts.append((qh @ window_k[b, h].astype(np.float64).T) * scale)
             allsc = np.concatenate(parts, 1)
+            if kv_start is not None:
+                allsc = np.where(np.arange(allsc.shape[1])[None, :] >= kv_start[b], allsc,
+                                 -np.inf)
             m = allsc.max(1, keepdims=True)
+            if not np.isfinite(m).all():          # every key is padding
+                continue
             p = np.exp(allsc - m)
             l = p.sum(1, keepdims=True)
             vh = vc.astype(np.float64)[v_idx[s, :T].astype(np.int64)] * \

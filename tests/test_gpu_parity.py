@@ -219,6 +219,41 @@ def test_decode_matches_oracle(D, kb, vb, qjl, B, Hkv, g, T, W):
     assert cosine(o, want) >= 0.9999
 
 
+@pytest.mark.parametrize("D,kb,vb,qjl,W", [(128, 4, 2, True, 0), (128, 4, 2, False, 7),
+                                            (128, 3, 3, False, 0), (64, 4, 4, False, 5)])
+def test_decode_left_padding_matches_oracle(D, kb, vb, qjl, W):
+    """kv_start: each row's keys before its first real position (packed and
+    window alike) take no weight; a row with nothing left returns zeros."""
+    B, Hkv, g, T = 4, 2, 4, 300
+    t = make_tables(D, kb, vb, qjl)
+    k, v = rand_kv((B, Hkv, T, D), 61), rand_kv((B, Hkv, T, D), 62)
+    pages = new_pages(B * Hkv, T, t)
+    ops.append(t, pages, k.to(DEV), v.to(DEV), 0)
+    q = rand_kv((B, Hkv * g, 1, D), 63, outliers=0)
+    wk = rand_kv((B, Hkv, W, D), 64) if W else None
+    wv = rand_kv((B, Hkv, W, D), 65) if W else None
+    start = [0, 37, 299, T + W]                 # the last row: everything is padding
+    ks = torch.tensor(start, dtype=torch.int32, device=DEV)
+    ws = ops.DecodeWorkspace()
+    out = ops.decode_attention(t, pages, q.to(DEV), T, wk.to(DEV) if W else None,
+                               wv.to(DEV) if W else None, workspace=ws, kv_start=ks)
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    _, got = parse(t, pages, T)
+    Smat = _generate_qjl_matrix(D, 42).numpy() if qjl else None
+    want = O.decode_attention_codes(
+        q[:, :, 0].float().numpy(), got["k_idx"], got["v_idx"], got["k_norm"], got["v_norm"],
+        t.k_centroids.cpu().numpy(), t.v_centroids.cpu().numpy(), t.rot.cpu().numpy(),
+        qbits=got.get("qbits"), gamma=got.get("gamma"), S=Smat, T=T,
+        window_k=wk.float().numpy() if W else None, window_v=wv.float().numpy() if W else None,
+        kv_start=start)
+    o = out[:, :, 0].float().cpu().numpy()
+    assert np.abs(o[3]).max() == 0.0
+    bf = 2 ** -8 * np.abs(want).max()
+    assert np.abs(o - want).max() <= 2e-3 * np.abs(want).max() + bf
+    assert cosine(o[:3], want[:3]) >= 0.9999
+
+
 def test_decode_no_device_errors_and_split_independence():
     """Results do not depend on how the page space is split across CTAs."""
     D, B, Hkv, g, T = 128, 2, 4, 4, 2000

@@ -187,3 +187,42 @@ def test_prefill_full_size_sampled():
         qs = q[b:b + 1, h:h + 1].float().cpu().numpy()
         want = O.sdpa(qs, kd.reshape(1, 1, T, D), vd.reshape(1, 1, T, D), causal=True)
         _check(out[b:b + 1, h:h + 1, rows], want[:, :, rows])
+
+
+WINDOW_CASES = [
+    # kb, vb, n_packed, W, Tq, engine
+    (4, 2, 300, 128, 300, 0),      # whole-prompt tail in the window (256-row kernel)
+    (4, 2, 0, 100, 100, 0),        # prompt shorter than the window: no packed key
+    (6, 4, 170, 128, 50, 2),       # protected layer bits, 128-row kernel, a later chunk
+    (3, 3, 64, 33, 97, 3),         # ragged window, 256-row kernel
+]
+
+
+@pytest.mark.parametrize("kb,vb,npk,W,Tq,engine", WINDOW_CASES)
+def test_prefill_window_and_left_padding_match_oracle(kb, vb, npk, W, Tq, engine):
+    """Residual window (dense keys after the packed ones, attended exactly)
+    and kv_start (left padding), against the oracle's SDPA over the
+    dequantised packed keys followed by the exact window."""
+    D, B, Hkv, g = 128, 3, 2, 4
+    n = npk + W
+    t = make_tables(D, kb, vb, False)
+    pages = new_pages(B * Hkv, max(npk, 1), t)
+    if npk:
+        ops.append(t, pages, rand_kv((B, Hkv, npk, D), 71).to(DEV),
+                   rand_kv((B, Hkv, npk, D), 72).to(DEV), 0)
+    wk, wv = rand_kv((B, Hkv, W, D), 73), rand_kv((B, Hkv, W, D), 74)
+    q = rand_kv((B, Hkv * g, Tq, D), 75)
+    start = [0, min(n - 1, 45), min(n - 2, npk + 5)]
+    ks = torch.tensor(start, dtype=torch.int32, device=DEV)
+    out = ops.prefill_attention(t, pages, q.to(DEV), n, engine=engine, kv_start=ks,
+                                window_k=wk.to(DEV), window_v=wv.to(DEV))
+    torch.cuda.synchronize()
+    assert ops.device_status(DEV) == 0
+    if npk:
+        kd, vd = _dequant(t, pages, npk)
+        kall = np.concatenate([kd.reshape(B, Hkv, npk, D), wk.float().numpy()], 2)
+        vall = np.concatenate([vd.reshape(B, Hkv, npk, D), wv.float().numpy()], 2)
+    else:
+        kall, vall = wk.float().numpy(), wv.float().numpy()
+    want = O.sdpa(q.float().numpy(), kall, vall, causal=True, kv_start=start)
+    _check(out, want)

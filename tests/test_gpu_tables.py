@@ -58,12 +58,16 @@ def test_init_tables_matches_python_tables(D, kb, vb, qjl):
         pairs += [("qjl", t.qjl_mat), ("qjl_t", t.qjl_t)]
     if D == 128:
         pairs += [("rot_bf16x3", t.rot_bf16x3)]
+    if D == 128 and qjl:
+        pairs += [("qjl_bf16", t.qjl_bf16)]     # S in bf16, K quad order, for the sketch
     for name, ref in pairs:
         ref = ref.contiguous()
         got = _dev_bytes(getattr(ct, name), ref.numel() * ref.element_size())
         assert torch.equal(got, ref.view(torch.uint8).flatten()), name
     if D != 128:
         assert not ct.rot_bf16x3
+    if D != 128 or not qjl:
+        assert not ct.qjl_bf16
 
 
 def test_kernels_identical_with_c_tables():

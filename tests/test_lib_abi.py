@@ -138,8 +138,9 @@ def test_init_tables_sizes_and_validation():
     g = _geom(D=128, kb=4, vb=2, q=1)
     n = lib.tq_tables_bytes(ctypes.byref(g))
     # kc 64 B, kb 60, vc 16, vb 12 (each in a 256-byte slot), R, R^T, S, S^T
-    # (64 KiB each), three bf16 terms x 2 orders (192 KiB), R fp16 (32 KiB)
-    assert n == 4 * 256 + 4 * 65536 + 196608 + 32768
+    # (64 KiB each), three bf16 terms x 2 orders (192 KiB), R fp16 (32 KiB),
+    # S in bf16 for the tensor-core sketch (32 KiB)
+    assert n == 4 * 256 + 4 * 65536 + 196608 + 32768 + 32768
     assert lib.tq_tables_bytes(ctypes.byref(_geom(D=48))) == 0
     t = _lib.Tables()
     host = (ctypes.c_float * (128 * 128))()
