@@ -22,8 +22,8 @@
 //     K position q, so each thread packs one QJL word;
 //   * one warp issues TMA, one warp issues the MMAs (M = N = 128, K = 16;
 //     24 per tile, + 16 for the sketch) into one of two TMEM accumulators;
-//     kSplit epilogue warps per TMEM lane quarter each take 128 / kSplit
-//     positions (one K quad) of 32 vectors.
+//     kSplit epilogue warps per TMEM lane quarter (2, or 4 with the sketch)
+//     each take 128 / kSplit positions of 32 vectors.
 //
 // Bucketize, almost all on the fp32 pipe (the integer pipe issues at half
 // the rate and bounded the first versions).  With w = 0.4 x the smallest
@@ -66,13 +66,24 @@ constexpr int kHalf = kM * 64 * 2;         // 16 KB: 128 rows x 64 bf16, 128-byt
 constexpr int kABytes = 2 * kHalf;         // one x tile
 constexpr int kBBytes = 6 * kHalf;         // 3 terms of R x 2 K-halves
 constexpr int kSBytes = 2 * kHalf;         // S (bf16) x 2 K-halves
-constexpr int kSplit = 4;                  // epilogue warps per TMEM lane quarter
-constexpr int kCW = kD / kSplit;           // positions per epilogue thread (one K quad)
-constexpr int kEpiWarps = 4 * kSplit;
-constexpr int kThreads = 32 * (2 + kEpiWarps);   // warp 0 TMA, warp 1 MMA, then epilogue
 constexpr float kCmpScale = 1.2676506e30f; // K = 2^100
-constexpr int kRep = 8;                    // lookup-grid replicas (an LDS.128 serves 8 lanes a phase)
-constexpr int kCellShift = 7;              // log2(16 B x kRep)
+
+// Epilogue shape.  Without the sketch: two warps per TMEM lane quarter, 64
+// positions each, 8-byte lookup entries {-b K, base} replicated for 16 lanes
+// (an 8-byte load serves 16 lanes per shared-memory phase).  With it: four
+// warps per quarter, one K quad (32 positions, one QJL word) each, 16-byte
+// entries that also carry c[base] and c[base + 1], replicated for 8 lanes.
+// Either way a cell is 128 bytes of table.
+template <bool QJL>
+struct Epi {
+  static constexpr int kSplit = QJL ? 4 : 2;       // epilogue warps per TMEM lane quarter
+  static constexpr int kCW = kD / kSplit;          // positions per epilogue thread
+  static constexpr int kEpiWarps = 4 * kSplit;
+  static constexpr int kThreads = 32 * (2 + kEpiWarps);   // warp 0 TMA, warp 1 MMA, then epilogue
+  static constexpr int kEntry = QJL ? 16 : 8;      // bytes per lookup entry
+  static constexpr int kRep = 128 / kEntry;        // replicas per cell
+};
+constexpr int kCellShift = 7;                      // log2(bytes per cell)
 // tensor memory: two 128-column fp32 accumulators of y; with the QJL sketch
 // also the residual as a bf16 A operand (hi, lo: 64 columns each) and the
 // 128-column fp32 accumulator of z = r S^T
@@ -85,6 +96,7 @@ struct TcSmem {
   static constexpr int OFF_S = OFF_B + kBBytes;                  // QJL only
   static constexpr int OFF_A = OFF_S + (QJL ? kSBytes : 0);
   static constexpr int OFF_BND = OFF_A + STAGES * kABytes;       // [256] boundaries
+  static constexpr int kSplit = Epi<QJL>::kSplit;
   static constexpr int OFF_XN = OFF_BND + 256 * 4;               // [2][kSplit][kM] partial ||x||^2
   static constexpr int OFF_RN = OFF_XN + 2 * kSplit * kM * 4;    // [kSplit][kM] partial ||r||^2
   static constexpr int OFF_BAR = OFF_RN + (QJL ? kSplit * kM * 4 : 0);
@@ -153,11 +165,14 @@ __device__ __forceinline__ void umma_ts_bf16(uint32_t d_tmem, uint32_t a_tmem, u
 // bf16, rows and columns in K quad order), and the epilogue packs the signs
 // of z and stores gamma = ||k|| ||r||.
 template <int BITS, bool QJL>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Epi<QJL>::kThreads, 1)
 append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
                  const __grid_constant__ CUtensorMap smap, TcParams p, int b_row0) {
   using SM = TcSmem<QJL>;
   constexpr int kAStages = SM::STAGES;
+  constexpr int kSplit = Epi<QJL>::kSplit, kCW = Epi<QJL>::kCW, kEpiWarps = Epi<QJL>::kEpiWarps;
+  constexpr int kThreads = Epi<QJL>::kThreads, kRep = Epi<QJL>::kRep;
+  static_assert(!QJL || kCW == 32, "the sketch packs one QJL word per epilogue thread");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -198,8 +213,8 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
   }
   for (int i = tid; i < nb; i += kThreads) bnd[i] = p.bnd[i];
   __syncthreads();
-  // lookup grid (see the file comment); 16-byte entries {-b K, base, c[base],
-  // c[base + 1]}, replicated for kRep lanes
+  // lookup grid (see the file comment); entries {-b K, base} (with the
+  // sketch also c[base], c[base + 1]), replicated for kRep lanes
   if (tid == 0) {
     float gap = 1.f;
     for (int i = 0; i + 1 < nb; ++i) gap = fminf(gap, bnd[i + 1] - bnd[i]);
@@ -207,7 +222,7 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
     const float span = fmaxf(fabsf(bnd[0]), fabsf(bnd[nb - 1]));
     const float L = ceilf(span / w) + 3.f;
     const float nc = 2.f * L + 1.f;
-    const bool ok = w > 0.f && nc * (float)(16 * kRep) <= (float)SM::LUT_BYTES && span < 1.f;
+    const bool ok = w > 0.f && nc * 128.f <= (float)SM::LUT_BYTES && span < 1.f;
     lutpar[0] = 1.f / (2.f * L * w);          // u = sat(v * lutpar[0] + 0.5)
     lutpar[1] = 2.f * L;                       // cell = round(u * 2L)
     lutpar[2] = ok ? nc : 0.f;
@@ -227,8 +242,13 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
         if (bnd[mid] < wl) base = mid + 1; else hi = mid;
       }
       const float nbk = (base < nb && bnd[base] <= wh) ? -bnd[base] * kCmpScale : -INFINITY;
-      const float clo = __ldg(p.cent + base), chi = __ldg(p.cent + tmin(base + 1, nb));
-      reinterpret_cast<float4*>(sm + SM::OFF_LUT)[c * kRep + l] = make_float4(nbk, (float)base, clo, chi);
+      if constexpr (QJL) {
+        const float clo = __ldg(p.cent + base), chi = __ldg(p.cent + tmin(base + 1, nb));
+        reinterpret_cast<float4*>(sm + SM::OFF_LUT)[c * kRep + l] =
+            make_float4(nbk, (float)base, clo, chi);
+      } else {
+        reinterpret_cast<float2*>(sm + SM::OFF_LUT)[c * kRep + l] = make_float2(nbk, (float)base);
+      }
     }
   }
   tc::tc_fence_before();
@@ -375,8 +395,10 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
       ok2 = __all_sync(0xffffffffu, ok2);
       if (ok2) {
         tc::tc_fence_after();
-        tc::tmem_ld_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ac * kD + part * kCW),
-                        *reinterpret_cast<uint32_t(*)[32]>(yb));
+#pragma unroll
+        for (int c = 0; c < kCW / 32; ++c)
+          tc::tmem_ld_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ac * kD + part * kCW + c * 32),
+                          *reinterpret_cast<uint32_t(*)[32]>(yb + c * 32));
         tc::tmem_wait_ld();
         tc::tc_fence_before();
         __syncwarp();
@@ -414,7 +436,8 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
         }
       };
       if (use_lut) {
-        const uint32_t lane_off = smem_u32(sm + SM::OFF_LUT) + (uint32_t)(lane % kRep) * 16u -
+        const uint32_t lane_off = smem_u32(sm + SM::OFF_LUT) +
+                                  (uint32_t)((lane % kRep) * Epi<QJL>::kEntry) -
                                   (0x4B000000u << kCellShift);
         const float ca = inv * lutpar[0], cK = inv * kCmpScale, c2l = lutpar[1];
         float acc = 8388608.f;
@@ -432,7 +455,14 @@ append_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant
           const float y = __uint_as_float(yb[j]);
           const float u = __saturatef(fmaf(y, ca, 0.5f));
           const float tc = fmaf(u, c2l, 8388608.f);
-          const float4 e = lds_f4((__float_as_uint(tc) << kCellShift) + lane_off);
+          const uint32_t ea = (__float_as_uint(tc) << kCellShift) + lane_off;
+          float4 e;
+          if constexpr (QJL) {
+            e = lds_f4(ea);
+          } else {
+            const float2 e2 = tc::lds_f2(ea);
+            e = make_float4(e2.x, e2.y, 0.f, 0.f);
+          }
           const float sgt = __saturatef(fmaf(y, cK, e.x) * kCmpScale);
           acc = fmaf(e.y + sgt, (float)(1u << gl), acc);
           gl += BITS;
@@ -671,7 +701,8 @@ int launch_append_tc(const tq_geom* G, const tq_tables* t, const tq_cache* c,
     p.nblk = nblk;
     p.ntiles = B * H * nblk;
     const int grid = (int)tmin<int64_t>(p.ntiles, (int64_t)sms);
-    fns[which]<<<grid, kThreads, TcSmem<false>::BYTES, st>>>(amap[which], bmap, smap, p, which * 3 * kD);
+    const int threads = (which == 0 && G->qjl) ? Epi<true>::kThreads : Epi<false>::kThreads;
+    fns[which]<<<grid, threads, TcSmem<false>::BYTES, st>>>(amap[which], bmap, smap, p, which * 3 * kD);
     if (check_launch("tq_append (tensor-core)") != TQ_OK) return TQ_ERR_CUDA;
   }
   return TQ_OK;

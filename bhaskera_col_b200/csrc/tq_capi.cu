@@ -12,10 +12,23 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "tq_common.cuh"
 #include "tq_internal.h"
 
 namespace tq {
+
+// An NVTX range over one entry point (host side: the span in which it
+// validates and enqueues its kernels), so a profiler's timeline shows the
+// append, decode, decode-step (with the fused gather) and prefill calls.
+// NVTX does nothing unless a profiler is attached.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 static thread_local char g_err[512] = "";
 
@@ -184,6 +197,7 @@ int32_t tq_quantize_rotated(const float* y, int64_t n, const float* boundaries,
 
 int32_t tq_append(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                   const tq_tensor4* k, const tq_tensor4* v, int64_t pos, void* stream) {
+  NvtxRange range("tq_append");
   const char* fn = "tq_append";
   int rc;
   if ((rc = check_geom(g, fn)) || (rc = check_tables(g, t, fn)) || (rc = check_cache(c, fn)) ||
@@ -214,6 +228,7 @@ int32_t tq_append(const tq_geom* g, const tq_tables* t, const tq_cache* c,
 
 int32_t tq_dequantize(const tq_geom* g, const tq_tables* t, const tq_cache* c, int64_t t0,
                       int64_t t1, const tq_tensor4* k_out, const tq_tensor4* v_out, void* stream) {
+  NvtxRange range("tq_dequantize");
   const char* fn = "tq_dequantize";
   int rc;
   if ((rc = check_geom(g, fn)) || (rc = check_tables(g, t, fn)) || (rc = check_cache(c, fn)))
@@ -316,6 +331,7 @@ size_t tq_decode_workspace_bytes(const tq_geom* g, const tq_cache* c, const tq_d
 int32_t tq_decode_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                        const tq_decode_args* a, void* workspace, size_t workspace_bytes,
                        void* stream) {
+  NvtxRange range("tq_decode_attn");
   const char* fn = "tq_decode_attn";
   int rc = check_decode(g, t, c, a, fn);
   if (rc) return rc;
@@ -326,6 +342,7 @@ int32_t tq_decode_step(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                        const tq_tensor4* k_new, const tq_tensor4* v_new, int64_t pos,
                        const tq_decode_args* a, void* workspace, size_t workspace_bytes,
                        void* stream) {
+  NvtxRange range("tq_decode_step");
   const char* fn = "tq_decode_step";
   int rc = check_decode(g, t, c, a, fn);
   if (rc) return rc;
@@ -353,6 +370,7 @@ int32_t tq_decode_step(const tq_geom* g, const tq_tables* t, const tq_cache* c,
 
 int32_t tq_prefill_attn(const tq_geom* g, const tq_tables* t, const tq_cache* c,
                         const tq_prefill_args* a, void* stream) {
+  NvtxRange range("tq_prefill_attn");
   const char* fn = "tq_prefill_attn";
   int rc;
   if ((rc = check_geom(g, fn)) || (rc = check_tables(g, t, fn)) || (rc = check_cache(c, fn)))

@@ -224,13 +224,14 @@ __device__ __forceinline__ void named_bar(int id, int count) {
 // so the kernel reserves NG + 1 barriers, not all sixteen).
 template <int NG>
 __device__ __forceinline__ void group_bar(int grp, int count) {
-  static_assert(NG >= 1 && NG <= 3, "page groups");
+  static_assert(NG >= 1 && NG <= 4, "page groups");
   if constexpr (NG == 1) {
     named_bar(1, count);
   } else {
     if (grp == 0) named_bar(1, count);
     else if (NG == 2 || grp == 1) named_bar(2, count);
-    else named_bar(3, count);
+    else if (NG == 3 || grp == 2) named_bar(3, count);
+    else named_bar(4, count);
   }
 }
 

@@ -193,18 +193,13 @@ __global__ void __launch_bounds__(512, 1) prefill_tc_kernel(TcPrefillParams p) {
         sts128(sbase + OFF_RK + sw_chunk(it >> 4, it & 15), v[m]);
       }
     }
-    // pair tables: one entry per thread, its rk (rv) copies written 16 bytes
-    // at a time (rk, rv >= 8 and nk, nv <= 256 = decoder threads)
-    if (dt < nk) {
-      const uint32_t v = pack_half2(__ldg(p.kc + (dt & ((1 << KB) - 1))), __ldg(p.kc + (dt >> KB)));
-      const uint4 v4 = make_uint4(v, v, v, v);
-      for (int c = 0; c < p.rk; c += 4) sts128(lut_k + 4u * (uint32_t)(dt * p.rk + c), v4);
-    }
-    if (dt < nv) {
-      const uint32_t v = pack_half2(__ldg(p.vc + (dt & ((1 << VB) - 1))), __ldg(p.vc + (dt >> VB)));
-      const uint4 v4 = make_uint4(v, v, v, v);
-      for (int c = 0; c < p.rv; c += 4) sts128(lut_v + 4u * (uint32_t)(dt * p.rv + c), v4);
-    }
+    // pair tables: entries dt, dt + kDecThreads, ... with their rk (rv) copies
+    for (int e = dt; e < nk; e += kDecThreads)
+      put_pair_entry(lut_k, e, p.rk,
+                     pack_half2(__ldg(p.kc + (e & ((1 << KB) - 1))), __ldg(p.kc + (e >> KB))));
+    for (int e = dt; e < nv; e += kDecThreads)
+      put_pair_entry(lut_v, e, p.rv,
+                     pack_half2(__ldg(p.vc + (e & ((1 << VB) - 1))), __ldg(p.vc + (e >> VB))));
   }
   tc::fence_proxy_async_smem();
   tc::tc_fence_before();

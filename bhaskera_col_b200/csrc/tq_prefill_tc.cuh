@@ -145,6 +145,21 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
                ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
 
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+// The `rep` copies of pair-table entry e (4 bytes each) at `table`: 16-byte
+// stores where the copies come in fours, else one store per copy.
+__device__ __forceinline__ void put_pair_entry(uint32_t table, int e, int rep, uint32_t v) {
+  const uint32_t at = table + 4u * (uint32_t)(e * rep);
+  if (rep >= 4) {
+    for (int c = 0; c < rep; c += 4) sts128(at + 4u * (uint32_t)c, make_uint4(v, v, v, v));
+  } else {
+    for (int c = 0; c < rep; ++c) sts32(at + 4u * (uint32_t)c, v);
+  }
+}
+
 // Byte offset of 16-byte chunk `c` (0..15, 8 elements each) of row `r` in a
 // [2][rows][128 B] swizzled operand.
 __device__ __forceinline__ uint32_t sw_chunk(int r, int c) {

@@ -10,7 +10,7 @@
 // hc/2 - 1 at the CTA's 256/hc positions (both tiles need the same keys);
 // with hc = 1 tile X holds positions 128 X .. 128 X + 127 of the head.
 //
-// Warp roles (13 warps):
+// Warp roles (17 warps):
 //   warp 0      owns tensor memory; one thread issues every MMA in the order
 //               S_A(0) S_B(0), then per tile j: PV_A(j) S_A(j+1) PV_B(j)
 //               S_B(j+1); finally OUT_X = O^_X R_V
@@ -18,7 +18,9 @@
 //               per query row (tensor-memory lane): S_X(j) -> P_X(j) as fp16
 //               pairs over the S_X columns, row sums l in registers (sums of
 //               the fp16 P the PV MMA uses), lazy O_X rescale in tensor memory
-//   warps 9-12  decoders (K^ one tile ahead of V^, four rows per thread)
+//   warps 9-16  decoders (K^ one tile ahead of V^, two rows per thread: the
+//               same key row of both pages; eight warps so that decoding, not
+//               issue latency, sets their pace)
 // Tensor memory (512 columns): S_A 0, S_B 128, O_A 256, O_B 384.  With one S
 // buffer per tile, S_X(j) complete implies PV_X(j-1) complete (issued
 // before it), so a rescale of O_X needs no extra wait.
@@ -39,9 +41,9 @@ namespace {
 using namespace pftc;
 
 constexpr int kSoftWarps = 8;              // 4 per query tile
-constexpr int kDecWarps = 4;
+constexpr int kDecWarps = 8;
 constexpr int kWarps = 1 + kSoftWarps + kDecWarps;
-constexpr int kThreads = 32 * kWarps;      // 416
+constexpr int kThreads = 32 * kWarps;      // 544
 constexpr int kDecThreads = 32 * kDecWarps;
 constexpr int kTmemCols = 512;
 
@@ -76,7 +78,7 @@ __device__ __forceinline__ RowId row_id(const TcPrefillParams& p, int qb, int X,
 }
 
 template <int KB, int VB>
-__global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) {
+__global__ void __launch_bounds__(kThreads, 1) prefill_tc2_kernel(TcPrefillParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -176,16 +178,12 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
     // pair tables: entries dt, dt + 128, ... with their rk (rv) copies
     const uint32_t lut_k = sbase + OFF_LUT;
     const uint32_t lut_v = lut_k + (uint32_t)(nk * p.rk * 4);
-    for (int e = dt; e < nk; e += kDecThreads) {
-      const uint32_t v = pack_half2(__ldg(p.kc + (e & ((1 << KB) - 1))), __ldg(p.kc + (e >> KB)));
-      const uint4 v4 = make_uint4(v, v, v, v);
-      for (int c = 0; c < p.rk; c += 4) sts128(lut_k + 4u * (uint32_t)(e * p.rk + c), v4);
-    }
-    for (int e = dt; e < nv; e += kDecThreads) {
-      const uint32_t v = pack_half2(__ldg(p.vc + (e & ((1 << VB) - 1))), __ldg(p.vc + (e >> VB)));
-      const uint4 v4 = make_uint4(v, v, v, v);
-      for (int c = 0; c < p.rv; c += 4) sts128(lut_v + 4u * (uint32_t)(e * p.rv + c), v4);
-    }
+    for (int e = dt; e < nk; e += kDecThreads)
+      put_pair_entry(lut_k, e, p.rk,
+                     pack_half2(__ldg(p.kc + (e & ((1 << KB) - 1))), __ldg(p.kc + (e >> KB))));
+    for (int e = dt; e < nv; e += kDecThreads)
+      put_pair_entry(lut_v, e, p.rv,
+                     pack_half2(__ldg(p.vc + (e & ((1 << VB) - 1))), __ldg(p.vc + (e >> VB))));
   }
   tc::fence_proxy_async_smem();
   tc::tc_fence_before();
@@ -488,8 +486,8 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
     pv.off_kn = p.off_kn;
     pv.off_vn = p.off_vn;
     // lane -> (key, part) as in tq_prefill_tc.cu (8 keys x 4 parts per warp,
-    // conflict-free 16-byte stores); each thread also takes the keys 32 rows
-    // below in both pages
+    // conflict-free 16-byte stores); each thread takes its key row in both
+    // pages
     {
       const int G = lane >> 3, u = lane & 7, part = u & 3;
       const int klo = ((u >> 2) ^ ((((part >> 1) ^ G) & 1) << 1)) | ((G >> 1) << 2);
@@ -503,12 +501,12 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
     const unsigned char* lv = sm + OFF_LUT + 4 * nk * p.rk + 4 * (lane & (p.rv - 1));
     const int rk4 = 4 * p.rk, rv4 = 4 * p.rv;
     const ChunkOffsets co = chunk_offsets(pv.kk, pv.part);
-    HalfRegs<KB, 4> kc, kn;
-    HalfRegs<VB, 4> vc, vn;
+    HalfRegs<KB, 2> kc, kn;
+    HalfRegs<VB, 2> vc, vn;
     bool ok = true;
     load_half<KB>(kc, pv, 0, 0, p.off_kn);
     decode_half<KB>(kc, lk, rk4, sm + OFF_K, co);
-    if (tile_has_window(pv, 0)) window_half<4>(pv, 0, p.wk, sm + OFF_K, co);
+    if (tile_has_window(pv, 0)) window_half<2>(pv, 0, p.wk, sm + OFF_K, co);
     tc::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL]);
@@ -525,7 +523,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
                              p.status);
         if (!__all_sync(0xffffffffu, ok)) break;
         decode_half<KB>(kc, lk, rk4, sm + OFF_K + sk * kStage, co);
-        if (tile_has_window(pv, jk)) window_half<4>(pv, jk, p.wk, sm + OFF_K + sk * kStage, co);
+        if (tile_has_window(pv, jk)) window_half<2>(pv, jk, p.wk, sm + OFF_K + sk * kStage, co);
         tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive_cta(&bars[B_KFULL + sk]);
@@ -540,7 +538,7 @@ __global__ void __launch_bounds__(512, 1) prefill_tc2_kernel(TcPrefillParams p) 
         ok = wait_or_abort(&bars[B_ROT], 0u, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) break;
       decode_half<VB>(vc, lv, rv4, sm + OFF_V + s * kStage, co);
-      if (tile_has_window(pv, j)) window_half<4>(pv, j, p.wv, sm + OFF_V + s * kStage, co);
+      if (tile_has_window(pv, j)) window_half<2>(pv, j, p.wv, sm + OFF_V + s * kStage, co);
       tc::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cta(&bars[B_VFULL + s]);

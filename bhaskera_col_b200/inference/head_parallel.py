@@ -106,7 +106,8 @@ class HeadShard:
                               device=out_local.device)
         try:
             # concatenated along dim 0 (the form every backend accepts)
-            dist.all_gather_into_tensor(buf, out_local.contiguous(), group=group)
+            with torch.cuda.nvtx.range("tq.all_gather"):
+                dist.all_gather_into_tensor(buf, out_local.contiguous(), group=group)
         except Exception as e:    # gloo / NCCL timeouts and peer failures
             where = f" at layer {layer}" if layer is not None else ""
             raise ShardFailure(f"rank {self.rank}: all-gather of attention outputs failed"

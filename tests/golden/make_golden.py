@@ -2,7 +2,8 @@
 
 Run in a container where the reference tree is readable:
 
-    python tests/golden/make_golden.py /root/reference/src
+    python tests/golden/make_golden.py <reference>/src
+    (or set BHASKERA_REFERENCE_SRC to the reference checkout's src directory)
 
 The reference is imported from source with bytecode caching redirected to a
 scratch directory, so none of the compiled ``__pycache__`` files shipped with
@@ -195,4 +196,8 @@ def main(src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("BHASKERA_REFERENCE_SRC")
+    if not src:
+        sys.exit("usage: make_golden.py <reference src directory> "
+                 "(or set BHASKERA_REFERENCE_SRC)")
+    main(src)

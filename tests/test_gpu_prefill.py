@@ -126,8 +126,20 @@ def test_prefill_growing_scores(engine):
 
 def test_tensor_core_coverage():
     assert not ops.prefill_uses_tensor_cores(make_tables(64, 4, 2, False))
-    assert not ops.prefill_uses_tensor_cores(make_tables(128, 6, 4, False))
+    assert not ops.prefill_uses_tensor_cores(make_tables(128, 8, 8, False))
     assert ops.prefill_uses_tensor_cores(make_tables(128, 4, 2, True))
+    # protected layers of K4/V2 and K3/V3 (+2 bits): pair tables with fewer
+    # than four copies per entry
+    assert ops.prefill_uses_tensor_cores(make_tables(128, 6, 4, False))
+    assert ops.prefill_uses_tensor_cores(make_tables(128, 5, 5, False))
+
+
+@pytest.mark.parametrize("engine", [2, 3])
+@pytest.mark.parametrize("kb,vb", [(6, 4), (5, 5), (6, 6), (5, 4)])
+def test_prefill_protected_layer_bits_match_oracle(kb, vb, engine):
+    """5- and 6-bit codes on the tcgen05 kernels (pair tables of 1024 / 4096
+    entries, down to one copy per entry)."""
+    _run_case(128, kb, vb, False, 2, 2, 4, 300, 300, True, engine)
 
 
 def test_prefill_last_row_equals_decode():
@@ -156,10 +168,16 @@ def test_cache_prefill_api_and_window_rule():
     want = ops.prefill_attention(st.tables, st._pages, q, T)
     assert torch.equal(out, want)
     assert cache.device_status() == 0
+    # with a residual window the newest tokens stay dense and enter exactly
     windowed = TurboQuantKVCache(num_layers=1, batch_size=B, num_heads=Hkv, head_dim=D,
                                  residual_window=8, protected_layers=0, device=DEV)
-    with pytest.raises(ValueError):
-        windowed.prefill(q, k, v, 0)
+    got = windowed.prefill(q, k, v, 0)
+    ws = windowed._stores[0]
+    assert ws._comp_ptr == T - 8 and ws._win_k.shape[2] == 8
+    want = ops.prefill_attention(ws.tables, ws._pages, q, T, window_k=k[:, :, T - 8:],
+                                 window_v=v[:, :, T - 8:])
+    assert torch.equal(got, want)
+    assert windowed.device_status() == 0
 
 
 def test_prefill_full_size_sampled():
