@@ -872,6 +872,8 @@ def run_profile(args):
     --profile decode : one Mixtral layer (B16 Hkv8 T8192, K4+QJL/V2), 4 decode calls
     --profile append : one prefill-append layer (B8 Hkv8 T4096 D128 4-bit), 4 calls
     --profile step   : one layer's fused decode step (tq_decode_step), 4 calls
+    --profile append_qjl : K4+QJL/V2 prefill append, B4 x Hkv8 x 8192 tokens, 4 calls
+    --profile prefill    : prefill attention, B2 x Hq32/Hkv8 x 2048 tokens, 3 calls
     """
     import torch
     from bhaskera_col_b200.inference import TurboQuantKVCache, ops
@@ -895,6 +897,26 @@ def run_profile(args):
         for _ in range(3):
             ops.prefill_attention(t, pages, q, Tp)
         torch.cuda.synchronize()
+        return
+    if args.profile == "append_qjl":
+        # one layer's K4+QJL/V2 prefill append, a quarter of the headline's
+        # streams (B4 x Hkv8 x 8192 tokens; 134 MB of bf16 input > L2)
+        from bhaskera_col_b200.inference.kv_cache import (FastLloydMaxCodebook,
+                                                          _generate_qjl_matrix,
+                                                          _generate_rotation_matrix)
+        Bp, Hp, Tp, Dp = 4, 8, 8192, 128
+        kc, vc = FastLloydMaxCodebook.get(Dp, 4, dev), FastLloydMaxCodebook.get(Dp, 2, dev)
+        t = ops.LayerTables(Dp, 4, 2, True, kc.centroids, kc.boundaries, vc.centroids,
+                            vc.boundaries, _generate_rotation_matrix(Dp, 42, dev).contiguous(),
+                            _generate_qjl_matrix(Dp, 42, dev).contiguous())
+        k = torch.randn((Bp, Hp, Tp, Dp), device=dev, generator=gen).to(torch.bfloat16)
+        pages = torch.zeros((Bp * Hp, Tp // 64, ops.page_bytes(Dp, 4, 2, True)),
+                            dtype=torch.uint8, device=dev)
+        for _ in range(4):
+            ops.append(t, pages, k, k, 0)
+        torch.cuda.synchronize()
+        if ops.device_status(dev) != 0:
+            raise RuntimeError("device status error")
         return
     if args.profile == "append":
         c = APPEND_CFG
@@ -941,7 +963,8 @@ def main():
                     help="leave out the 256-sequence head-sharded serving workload")
     ap.add_argument("--skip-long", action="store_true",
                     help="leave out the long-context cases (1 GPU)")
-    ap.add_argument("--profile", choices=["decode", "append", "step", "prefill"], default=None,
+    ap.add_argument("--profile", choices=["decode", "append", "append_qjl", "step", "prefill"],
+                    default=None,
                     help="run a small single-layer case for ncu and exit")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mixtral",
                     help="decode-step workload (default: the Mixtral headline)")
