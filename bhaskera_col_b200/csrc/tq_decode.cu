@@ -40,6 +40,9 @@ constexpr int kTileWarps = 4;     // warps of a page group (two per page, 32 tok
 constexpr int kSmemBudget = 226 * 1024;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegInf = -INFINITY;
+// The decode's softmax bias runs this far (log2 units) above the running max,
+// so the max is reduced across a warp only when a score passes it.
+constexpr float kLazyBits = 8.f;
 
 // Which pages a decode walks.  Stream s owns the compacted page range
 // [start(s), start(s + 1)): s * Pv for a uniform batch, and for a ragged one
@@ -689,24 +692,30 @@ decode_kernel(DecodeParams p) {
 #pragma unroll
           for (int t = 0; t < 2; ++t) tile_scores(pgb, wt0 + 16 * t + gq, sc[t]);
           // rows beyond the stream's tokens or before its first attended
-          // token take no weight
+          // token take no weight (warp-uniform test: only a stream's first
+          // and last pages hold such rows)
+          const bool edge = tokw + 32 > Ts || tokw < Ks;
+          if (edge) {
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int r = tokw + 16 * t + gq;
-            if (r >= Ts || r < Ks) { sc[t][0] = kNegInf; sc[t][1] = kNegInf; }
-            if (r + 8 >= Ts || r + 8 < Ks) { sc[t][2] = kNegInf; sc[t][3] = kNegInf; }
+            for (int t = 0; t < 2; ++t) {
+              const int r = tokw + 16 * t + gq;
+              if (r >= Ts || r < Ks) { sc[t][0] = kNegInf; sc[t][1] = kNegInf; }
+              if (r + 8 >= Ts || r + 8 < Ks) { sc[t][2] = kNegInf; sc[t][3] = kNegInf; }
+            }
           }
           // ---------------- online softmax over the 32 tokens (columns =
-          // heads 2tq, 2tq+1); the running max only moves when a lane's
-          // grows, checked once per warp
+          // heads 2tq, 2tq+1).  The exponent bias is the running max m plus
+          // kLazyBits: while no score exceeds it, p = exp2(s - bias) <= 1 and
+          // the max needs no warp reduction; only then is m reduced across
+          // the warp and O, l rescaled
           float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][2]), fmaxf(sc[1][0], sc[1][2]));
           float mx1 = fmaxf(fmaxf(sc[0][1], sc[0][3]), fmaxf(sc[1][1], sc[1][3]));
+          if (__any_sync(0xffffffffu, mx0 > m0 + kLazyBits || mx1 > m1 + kLazyBits)) {
 #pragma unroll
-          for (int o = 4; o < 32; o <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-          }
-          if (__any_sync(0xffffffffu, mx0 > m0 || mx1 > m1)) {
+            for (int o = 4; o < 32; o <<= 1) {
+              mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+              mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+            }
             const float n0m = fmaxf(m0, mx0), n1m = fmaxf(m1, mx1);
             const float c0 = n0m == m0 ? 1.f : fast_exp2(m0 - n0m);
             const float c1 = n1m == m1 ? 1.f : fast_exp2(m1 - n1m);
@@ -720,7 +729,8 @@ decode_kernel(DecodeParams p) {
             m0 = n0m;
             m1 = n1m;
           }
-          const float b0s = m0 == kNegInf ? 0.f : m0, b1s = m1 == kNegInf ? 0.f : m1;
+          const float b0s = m0 == kNegInf ? 0.f : m0 + kLazyBits;
+          const float b1s = m1 == kNegInf ? 0.f : m1 + kLazyBits;
           const __half* vn = reinterpret_cast<const __half*>(pgb + G::OFF_VN);
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
@@ -732,10 +742,14 @@ decode_kernel(DecodeParams p) {
             // ---------------- P' = p * ||v|| -> B fragments ---------------
             // (a masked row has p = 0; its norm slot may be stale)
             const float v0 = __half2float(vn[r0]), v1 = __half2float(vn[r0 + 8]);
-            const uint32_t pb0 = movmatrix_trans(pack_half2(p00 == 0.f ? 0.f : p00 * v0,
-                                                            p01 == 0.f ? 0.f : p01 * v0));
-            const uint32_t pb1 = movmatrix_trans(pack_half2(p10 == 0.f ? 0.f : p10 * v1,
-                                                            p11 == 0.f ? 0.f : p11 * v1));
+            uint32_t pb0, pb1;
+            if (edge) {
+              pb0 = movmatrix_trans(pack_half2(p00 == 0.f ? 0.f : p00 * v0, p01 == 0.f ? 0.f : p01 * v0));
+              pb1 = movmatrix_trans(pack_half2(p10 == 0.f ? 0.f : p10 * v1, p11 == 0.f ? 0.f : p11 * v1));
+            } else {
+              pb0 = movmatrix_trans(pack_half2(p00 * v0, p01 * v0));
+              pb1 = movmatrix_trans(pack_half2(p10 * v1, p11 * v1));
+            }
             tile_pv(pgb, wt0 + 16 * t, pb0, pb1);
           }
         }
@@ -761,8 +775,9 @@ decode_kernel(DecodeParams p) {
       float* cm = comb + warp * (16 + 8 * D);
       float* cl = cm + 8;
       float* co = cm + 16;
-      if (gq == 0) {
-        cm[2 * tq] = m0; cm[2 * tq + 1] = m1;
+      if (gq == 0) {                           // l and O are relative to m + kLazyBits
+        cm[2 * tq] = m0 == kNegInf ? kNegInf : m0 + kLazyBits;
+        cm[2 * tq + 1] = m1 == kNegInf ? kNegInf : m1 + kLazyBits;
         cl[2 * tq] = L0; cl[2 * tq + 1] = L1;
       }
 #pragma unroll
@@ -830,74 +845,9 @@ struct QPrepParams {
   int D, g, Hkv, nch;
   const void* q; int q_dtype; int64_t q_stride[4];
   const float* RT; const float* ST;   // R^T, S^T (row-major)
-  // tensor-core query rotation (head_dim 128, bf16 q): R as three bf16 terms
-  // with rows in K quad order, and S in bf16 with rows and columns in K quad
-  // order (tq_tables.rot_bf16x3 / qjl_bf16); NULL: the CUDA-core rotation
-  const uint16_t* rot3;
-  const uint16_t* qjlb;
   float scale_q, scale_s;
   uint32_t* qf; uint32_t* sqf;
 };
-
-// bf16 m16n8k16 MMA, fp32 accumulate (A row-major, B column-major).
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1,
-                                               uint32_t a2, uint32_t a3, uint32_t b0,
-                                               uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// out[h][k_coord(p)] = sum_c A[h][c] B[p][c] for the first 8 rows of A (the
-// query heads; rows 8-15 of the MMA tile are zero) and all 128 positions p,
-// A given as NT bf16 terms [NT][8][kQLd] in shared memory, B a [128][128]
-// bf16 matrix in global memory (L2 resident) with rows in K quad order.
-// Eight warps; warp w takes positions 16 w .. 16 w + 15.  Exact bf16
-// products, fp32 accumulation.
-constexpr int kQLd = 136;             // bf16 row pitch of the staged A terms
-template <int NT, int NB>
-__device__ __forceinline__ void tc_rot8(const uint16_t* a_s, const uint16_t* const (&bmat)[NB],
-                                        float* out, int warp, int lane) {
-  const int gq = lane >> 2, tq = lane & 3;
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll 1
-  for (int bt = 0; bt < NB; ++bt) {
-#pragma unroll 1
-    for (int at = 0; at < NT; ++at) {
-      const uint16_t* arow = a_s + (at * 8 + gq) * kQLd;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(arow + 16 * kk + 2 * tq);
-        const uint32_t a2 = *reinterpret_cast<const uint32_t*>(arow + 16 * kk + 2 * tq + 8);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const uint16_t* brow = bmat[bt] + (16 * warp + 8 * nt + gq) * 128 + 16 * kk + 2 * tq;
-          const uint32_t b0 = __ldg(reinterpret_cast<const uint32_t*>(brow));
-          const uint32_t b1 = __ldg(reinterpret_cast<const uint32_t*>(brow + 8));
-          mma_bf16_16816(acc[nt], a0, 0u, a2, 0u, b0, b1);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    const int p = 16 * warp + 8 * nt + 2 * tq;
-    out[gq * 128 + k_coord_at(p, 128)] = acc[nt][0];
-    out[gq * 128 + k_coord_at(p + 1, 128)] = acc[nt][1];
-  }
-}
-
-// Three bf16 terms (hi, mid, lo: 24 significant bits) of x.
-__device__ __forceinline__ void bf16x3_split(float x, uint16_t& hi, uint16_t& mid, uint16_t& lo) {
-  const __nv_bfloat16 h = __float2bfloat16_rn(x);
-  const float r1 = x - __bfloat162float(h);
-  const __nv_bfloat16 m = __float2bfloat16_rn(r1);
-  const __nv_bfloat16 l = __float2bfloat16_rn(r1 - __bfloat162float(m));
-  hi = __bfloat16_as_ushort(h);
-  mid = __bfloat16_as_ushort(m);
-  lo = __bfloat16_as_ushort(l);
-}
 
 struct PrepParams {
   QPrepParams q;
@@ -961,12 +911,9 @@ __device__ __noinline__ void ragged_layout(const PageLayout L, int units, int ti
 template <int D>
 struct PrepSmem {
   // floats: R^T, S^T, xs[10][D] (q x8, k, v), ys[10][D], codebooks 4x256, norms 4;
-  // then codes, order tables, and (head_dim 128) the bf16 A terms of the
-  // tensor-core rotation [3][8][kQLd]
+  // then codes and order tables
   static size_t bytes(bool qjl) {
-    const size_t base = ((qjl ? 2 : 1) * (size_t)D * D + 20 * D + 4 * 256 + 4) * 4 + 3 * D +
-                        3 * D * 2 + 16;
-    return ((base + 15) & ~(size_t)15) + (D == 128 ? 24 * kQLd * 2 : 0);
+    return ((qjl ? 2 : 1) * (size_t)D * D + 20 * D + 4 * 256 + 4) * 4 + 3 * D + 3 * D * 2 + 16;
   }
 };
 
@@ -1000,15 +947,8 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   const bool app = pp.append && hc == 0;
   const int nbk = (1 << g.kb) - 1, nbv = (1 << g.vb) - 1;
 
-  // the query heads rotate on the tensor cores when the bf16 tables are given
-  // (head_dim 128, bf16 q); R^T / S^T in shared memory then serve only the
-  // appended token, whose page bytes must equal tq_append's
-  const bool tcq = D == 128 && p.rot3 != nullptr && p.q_dtype == TQ_BF16 &&
-                   (!qjl || p.qjlb != nullptr);
-  if (!tcq || app) {
-    stage_async(rt, p.RT, D * D * 4, tid, kPrepThreads);
-    if (qjl) stage_async(stt, p.ST, D * D * 4, tid, kPrepThreads);
-  }
+  stage_async(rt, p.RT, D * D * 4, tid, kPrepThreads);
+  if (qjl) stage_async(stt, p.ST, D * D * 4, tid, kPrepThreads);
   if (app) {
     // the layer's constant tables: read before the dependency wait, so their
     // latency overlaps the previous kernel
@@ -1046,24 +986,13 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   // phase A: rotate the nh real query heads (and u_k, u_v); vector a of the
   // active list sits at row a (a head) or 8 + a - nh (u_k, u_v).  The loop
   // is bound by shared-memory wavefronts, one per (vector, i) and warp, so
-  // the heads a GQA group pads to 8 are not computed.  With the tensor-core
-  // rotation the heads go through tc_rot8 and the loop keeps u_k, u_v.
-  uint16_t* a16 = reinterpret_cast<uint16_t*>(
-      (reinterpret_cast<uintptr_t>(qinv + D) + 15) & ~(uintptr_t)15);   // tcq: [3][8][kQLd] bf16
-  if (tcq) {
-    // q rows as bf16 (exact: q is bf16), one term
-    for (int i = tid; i < 8 * D; i += kPrepThreads) {
-      const int hl = i / D, c = i % D;
-      a16[hl * kQLd + c] = __bfloat16_as_ushort(__float2bfloat16_rn(xs[i]));
-    }
-    __syncthreads();
-    const uint16_t* rterms[3] = {p.rot3, p.rot3 + D * D, p.rot3 + 2 * D * D};
-    tc_rot8<1, 3>(a16, rterms, ys, warp, lane);
-  }
+  // the heads a GQA group pads to 8 are not computed.  (A tensor-core
+  // rotation of the heads with bf16 terms of R, B fragments read from L2,
+  // measured slower: 14.8 against 10.7 us per call.)
   {
-    const int nvec = (tcq ? 0 : nh) + (app ? 2 : 0);
+    const int nvec = nh + (app ? 2 : 0);
     const int mine = (grp < G && nvec > grp) ? (nvec - grp + G - 1) / G : 0;
-    const int nhl = tcq ? 0 : nh;                // heads left to this loop
+    const int nhl = nh;
     int row[NA];
 #pragma unroll
     for (int k = 0; k < NA; ++k) {
@@ -1086,23 +1015,8 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   if (qjl) {
     if (app && tid < D) ys[8 * D + tid] -= cb[code[tid]];   // K residual y - c[idx]
     __syncthreads();
-    // phase B: S q_rot for the nh heads, S r for the K residual (row 8).
-    // Tensor cores: q_rot in K order as three bf16 terms against S (exact in
-    // bf16), into xs (the heads' q rows are no longer needed).
-    if (tcq) {
-      for (int i = tid; i < 8 * D; i += kPrepThreads) {
-        const int hl = i / D, c = i % D;
-        uint16_t h, m, l;
-        bf16x3_split(ys[hl * D + k_coord_at(c, D)], h, m, l);
-        a16[hl * kQLd + c] = h;
-        a16[(8 + hl) * kQLd + c] = m;
-        a16[(16 + hl) * kQLd + c] = l;
-      }
-      __syncthreads();
-      const uint16_t* sterm[1] = {p.qjlb};
-      tc_rot8<3, 1>(a16, sterm, xs, warp, lane);
-    }
-    const int nhl = tcq ? 0 : nh;
+    // phase B: S q_rot for the nh heads, S r for the K residual (row 8)
+    const int nhl = nh;
     const int nvec = nhl + (app ? 1 : 0);
     const int mine = (grp < G && nvec > grp) ? (nvec - grp + G - 1) / G : 0;
     int row[NB];
@@ -1594,8 +1508,6 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   qp.q = a->q->data; qp.q_dtype = a->q->dtype;
   for (int i = 0; i < 4; ++i) qp.q_stride[i] = a->q->stride[i];
   qp.RT = t->rot_t; qp.ST = G->qjl ? t->qjl_t : nullptr;
-  qp.rot3 = t->rot_bf16x3;
-  qp.qjlb = G->qjl ? t->qjl_bf16 : nullptr;
   qp.scale_q = a->scale * kLog2e;
   qp.scale_s = a->scale * kLog2e * alpha;
   qp.qf = reinterpret_cast<uint32_t*>(w + pl.off_qf);
