@@ -66,11 +66,22 @@ __device__ __forceinline__ void rot_rows_n(const float* x, const int (&row)[NA],
     acc[v] = 0.f;
     xp[v] = x + row[v] * D;
   }
-#pragma unroll 4
-  for (int i = 0; i < D; ++i) {
-    const float t = T[i * D + j];
+  // x rows are 16-byte aligned shared-memory rows: four coordinates of each
+  // vector come in one broadcast load (one wavefront per vector and four
+  // steps instead of four), the FMA order per vector unchanged
+  static_assert(D % 4 == 0, "head_dim");
+#pragma unroll 2
+  for (int i = 0; i < D; i += 4) {
+    const float t0 = T[i * D + j], t1 = T[(i + 1) * D + j];
+    const float t2 = T[(i + 2) * D + j], t3 = T[(i + 3) * D + j];
 #pragma unroll
-    for (int v = 0; v < N; ++v) acc[v] = fmaf(xp[v][i], t, acc[v]);
+    for (int v = 0; v < N; ++v) {
+      const float4 xv = *reinterpret_cast<const float4*>(xp[v] + i);
+      acc[v] = fmaf(xv.x, t0, acc[v]);
+      acc[v] = fmaf(xv.y, t1, acc[v]);
+      acc[v] = fmaf(xv.z, t2, acc[v]);
+      acc[v] = fmaf(xv.w, t3, acc[v]);
+    }
   }
 }
 
