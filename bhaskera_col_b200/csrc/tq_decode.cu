@@ -835,11 +835,14 @@ decode_kernel(DecodeParams p) {
 //
 // q_rot = q R^T and Sq = S q_rot for the <= 8 query heads of a head chunk
 // become fp16 fragments for decode_kernel (softmax scale * log2e folded in).
-// With `append` set, the CTAs of head chunk 0 also store the stream's new
-// K/V token at position `pos`, with the same math and summation order as
-// append_kernel (kv_cache.py:382-398), so the page bytes are identical to a
-// tq_append of that token.  grid = (S, nch), 256 threads; thread (j, grp)
-// owns output coordinate j of the vectors grp, grp + G, ... (G = 256 / D).
+// With `append` set, the stream's new K/V token is stored at position `pos`,
+// with the same math and summation order as append_kernel
+// (kv_cache.py:382-398), so the page bytes are identical to a tq_append of
+// that token: by the CTAs of head chunk 0 or, when the grid still fits one
+// wave with it (`append_cta`: small batches), by one more CTA per stream
+// (blockIdx.y == nch) that runs beside the query CTAs.  grid = (S, nch [+ 1]),
+// 256 threads; thread (j, grp) owns output coordinate j of the vectors grp,
+// grp + G, ... (G = 256 / D).
 // ---------------------------------------------------------------------------
 struct QPrepParams {
   int D, g, Hkv, nch;
@@ -859,6 +862,7 @@ struct PrepParams {
   uint32_t* status;
   PageLayout lay;        // ragged (lay.lens set): store at row length - 1, lay out the pages
   int units;             // the decode's work units (CTAs x page groups)
+  int append_cta;        // the append has its own CTA per stream (blockIdx.y == nch)
 };
 
 constexpr int kPrepThreads = 256;
@@ -943,8 +947,9 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   const int64_t s = blockIdx.x;
   const int hc = blockIdx.y;
   const int64_t b = s / p.Hkv, kvh = s % p.Hkv;
-  const int nh = tmin(8, p.g - hc * 8);
-  const bool app = pp.append && hc == 0;
+  const bool qrole = hc < p.nch;                 // query CTA (else the step's append CTA)
+  const int nh = qrole ? tmin(8, p.g - hc * 8) : 0;
+  const bool app = pp.append && (pp.append_cta ? !qrole : hc == 0);
   const int nbk = (1 << g.kb) - 1, nbv = (1 << g.vb) - 1;
 
   stage_async(rt, p.RT, D * D * 4, tid, kPrepThreads);
@@ -962,12 +967,14 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   }
   pdl_launch_dependents();
   pdl_wait();
-  for (int i = tid; i < 8 * D; i += kPrepThreads) {
-    const int hl = i / D, c = i % D;
-    xs[i] = hl < nh ? load_elem(p.q, p.q_dtype, b * p.q_stride[0] +
-                                (kvh * p.g + hc * 8 + hl) * p.q_stride[1] + c * p.q_stride[3])
-                    : 0.f;
-    if (hl >= nh) ys[i] = 0.f;                   // padded heads: zero fragments, not computed
+  if (qrole) {
+    for (int i = tid; i < 8 * D; i += kPrepThreads) {
+      const int hl = i / D, c = i % D;
+      xs[i] = hl < nh ? load_elem(p.q, p.q_dtype, b * p.q_stride[0] +
+                                  (kvh * p.g + hc * 8 + hl) * p.q_stride[1] + c * p.q_stride[3])
+                      : 0.f;
+      if (hl >= nh) ys[i] = 0.f;                 // padded heads: zero fragments, not computed
+    }
   }
   if (app) {
     if (warp == 0) {
@@ -1043,12 +1050,14 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
     }
   }
   __syncthreads();
-  uint32_t* qo = p.qf + (s * p.nch + hc) * 8 * (D / 2);
-  for (int i = tid; i < 8 * (D / 2); i += kPrepThreads) {
-    const int hl = i / (D / 2), c2 = i % (D / 2);
-    qo[i] = pack_half2(ys[hl * D + 2 * c2] * p.scale_q, ys[hl * D + 2 * c2 + 1] * p.scale_q);
+  if (qrole) {
+    uint32_t* qo = p.qf + (s * p.nch + hc) * 8 * (D / 2);
+    for (int i = tid; i < 8 * (D / 2); i += kPrepThreads) {
+      const int hl = i / (D / 2), c2 = i % (D / 2);
+      qo[i] = pack_half2(ys[hl * D + 2 * c2] * p.scale_q, ys[hl * D + 2 * c2 + 1] * p.scale_q);
+    }
   }
-  if (qjl) {
+  if (qjl && qrole) {
     uint32_t* so = p.sqf + (s * p.nch + hc) * 8 * (D / 2);
     for (int i = tid; i < 8 * (D / 2); i += kPrepThreads) {
       const int hl = i / (D / 2), c2 = i % (D / 2);
@@ -1543,7 +1552,11 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
       return TQ_ERR_INVALID;
     }
     if (set_smem_attr((const void*)pfn, psmem) != TQ_OK) return TQ_ERR_CUDA;
-    if (launch_result(launch_pdl(pfn, dim3((unsigned)pl.S, pl.nch), dim3(kPrepThreads), psmem, st, pp),
+    // the step's append gets its own CTA per stream where the grid stays
+    // within one wave (prep CTAs take most of an SM's shared memory)
+    pp.append_cta = step && pl.S * (pl.nch + 1) <= (int64_t)device_sm_count();
+    const unsigned prep_y = (unsigned)(pl.nch + (pp.append_cta ? 1 : 0));
+    if (launch_result(launch_pdl(pfn, dim3((unsigned)pl.S, prep_y), dim3(kPrepThreads), psmem, st, pp),
                       step ? "tq_decode_step/prep" : "tq_decode_attn/qprep") != TQ_OK)
       return TQ_ERR_CUDA;
   }
