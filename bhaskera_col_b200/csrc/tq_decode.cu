@@ -921,7 +921,7 @@ struct PrepSmem {
   }
 };
 
-template <int D>
+template <int D, bool SEP>
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int G = kPrepThreads / D;            // vector groups
@@ -947,9 +947,10 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(PrepParams pp) {
   const int64_t s = blockIdx.x;
   const int hc = blockIdx.y;
   const int64_t b = s / p.Hkv, kvh = s % p.Hkv;
-  const bool qrole = hc < p.nch;                 // query CTA (else the step's append CTA)
+  // SEP: the step's append has its own CTA (blockIdx.y == nch)
+  const bool qrole = !SEP || hc < p.nch;         // query CTA (else the step's append CTA)
   const int nh = qrole ? tmin(8, p.g - hc * 8) : 0;
-  const bool app = pp.append && (pp.append_cta ? !qrole : hc == 0);
+  const bool app = pp.append && (SEP ? !qrole : hc == 0);
   const int nbk = (1 << g.kb) - 1, nbv = (1 << g.vb) - 1;
 
   stage_async(rt, p.RT, D * D * 4, tid, kPrepThreads);
@@ -1122,15 +1123,19 @@ struct MergeParams {
   void* peer_out[TQ_MAX_PEERS];
   uint32_t* peer_flag[TQ_MAX_PEERS];   // [arrivals, this rank's finished CTAs]
   uint32_t* status;
+  int hpc;                // heads per CTA: CTA z of (stream, chunk) takes heads [z hpc, (z + 1) hpc)
 };
 
 constexpr int kMergeThreads = 256;
 constexpr int kSlotChunk = 8;
 
-// grid = (S, nch), 256 threads.  Shared memory: R [D][D], the rotated
-// combination orot [8][D], a chunk of partials [8][kSlotChunk][D], and for
-// the window q [8][D] and scores/probabilities [8][W].
-template <int D>
+// grid = (S, nch, ceil(heads / hpc)), 256 threads: with few streams the
+// heads of a chunk are spread over CTAs, so each stages and combines only
+// its own heads' partials (a long-context batch of 8 streams has ~50 slots
+// per stream).  Shared memory: R [D][D], the rotated combination orot
+// [8][D], a chunk of partials [slots][heads][D] (8 * kSlotChunk * D floats),
+// and for the window q [8][D] and scores/probabilities [8][W].
+template <int D, bool SPLIT>
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int64_t W = p.W;
@@ -1147,6 +1152,14 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int NWARP = kMergeThreads / 32;
   const int nh = tmin(8, p.g - hc * 8);
+  // SPLIT: this CTA's heads are [ha, hb) of the chunk and it stages only
+  // their rows; otherwise it takes the whole chunk and stages all 8 head rows
+  // of a slot (one contiguous run per chunk of slots)
+  constexpr bool whole = !SPLIT;
+  const int ha = SPLIT ? (int)blockIdx.z * p.hpc : 0;
+  const int hb = SPLIT ? tmin(nh, ha + p.hpc) : nh;
+  const int hn = tmax(0, hb - ha);
+  const int kcap = whole ? kSlotChunk : (8 * kSlotChunk) / tmax(hn, 1);   // slots per chunk
   stage_async(rs, p.R, D * D * 4, tid, kMergeThreads);
   pdl_launch_dependents();
   pdl_wait();
@@ -1165,16 +1178,25 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
       hrow0 = ((int64_t)hc * L.nid + first + s) * 8;
     }
   }
+  // slots k0 .. k0 + kn - 1 of heads [ha, hb) into po[k - k0][h - ha][D]
+  auto stage_chunk = [&](int k0, int kn) {
+    if constexpr (whole) {                         // one run: rows are (slot, head)
+      stage_async(po, p.part_o + (hrow0 + 8 * k0) * D, kn * 8 * D * 4, tid, kMergeThreads);
+    } else {
+      for (int k = 0; k < kn; ++k)
+        stage_async(po + k * hn * D, p.part_o + (hrow0 + 8 * (k0 + k) + ha) * D, hn * D * 4, tid,
+                    kMergeThreads);
+    }
+  };
   // the first chunk of partials starts copying now, behind the window and
   // per-head passes
-  if (nslot > 0)
-    stage_async(po, p.part_o + hrow0 * D, tmin(kSlotChunk, nslot) * 8 * D * 4, tid, kMergeThreads);
+  if (nslot > 0 && hn > 0) stage_chunk(0, tmin(kcap, nslot));
 
   // --- window scores (unrotated), all heads --------------------------------
   if (W > 0) {
     for (int i = tid; i < 8 * D; i += kMergeThreads) {
       const int hl = i / D, c = i % D;
-      qv[i] = hl < nh ? load_elem(p.q, p.q_dtype, b * p.q_stride[0] +
+      qv[i] = (hl >= ha && hl < hb) ? load_elem(p.q, p.q_dtype, b * p.q_stride[0] +
                                   (kvh * p.g + hc * 8 + hl) * p.q_stride[1] + c * p.q_stride[3])
                       : 0.f;
     }
@@ -1204,7 +1226,8 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
     // slots lane and lane + 32 (kMaxSlots = 64): m and l loaded together
     static_assert(kMaxSlots <= 64, "two slots per lane");
     float mk[2] = {kNegInf, kNegInf}, lk[2] = {0.f, 0.f};
-    if (h < nh) {
+    const bool mine = h >= ha && h < hb;
+    if (mine) {
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int k = lane + 32 * u;
@@ -1224,13 +1247,13 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
     for (int u = 0; u < 2; ++u) {
       const int k = lane + 32 * u;
       if (k < nslot) {
-        const float wt = (h < nh && mk[u] != kNegInf) ? exp2f(mk[u] - Ms) : 0.f;
+        const float wt = (mine && mk[u] != kNegInf) ? exp2f(mk[u] - Ms) : 0.f;
         s_wt[h][k] = wt;
         L = fmaf(wt, lk[u], L);
       }
     }
     for (int64_t t = lane; t < W; t += 32) {
-      const float e = h < nh ? exp2f(sc[h * W + t] - Ms) : 0.f;
+      const float e = mine ? exp2f(sc[h * W + t] - Ms) : 0.f;
       sc[h * W + t] = e;
       L += e;
     }
@@ -1241,20 +1264,30 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   // --- rotated partial combination, slots staged in chunks ------------------
   constexpr int OUT = 4;                          // outputs per thread (8 * 128 / 256)
   float acc[OUT] = {0.f, 0.f, 0.f, 0.f};
-  for (int k0 = 0; k0 < nslot; k0 += kSlotChunk) {
-    const int kn = tmin(kSlotChunk, nslot - k0);
-    // slots k0 .. k0 + kn - 1 of all 8 heads are one run: po[k][h][D]
+  for (int k0 = 0; hn > 0 && k0 < nslot; k0 += kcap) {
+    const int kn = tmin(kcap, nslot - k0);
     // (the first chunk was issued after the dependency wait)
-    if (k0 > 0)
-      stage_async(po, p.part_o + (hrow0 + 8 * k0) * D, kn * 8 * D * 4, tid, kMergeThreads);
+    if (k0 > 0) stage_chunk(k0, kn);
     cp_async_wait_all();
     __syncthreads();
+    if constexpr (whole) {
 #pragma unroll
-    for (int r = 0; r < OUT; ++r) {
-      const int i = tid + r * kMergeThreads;
-      if (i < 8 * D) {
-        const int h = i / D, d = i % D;
-        for (int k = 0; k < kn; ++k) acc[r] = fmaf(s_wt[h][k0 + k], po[(k * 8 + h) * D + d], acc[r]);
+      for (int r = 0; r < OUT; ++r) {
+        const int i = tid + r * kMergeThreads;
+        if (i < 8 * D) {
+          const int h = i / D, d = i % D;
+          for (int k = 0; k < kn; ++k) acc[r] = fmaf(s_wt[h][k0 + k], po[(k * 8 + h) * D + d], acc[r]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < OUT; ++r) {
+        const int i = tid + r * kMergeThreads;
+        if (i < hn * D) {
+          const int hl = i / D, d = i % D;
+          for (int k = 0; k < kn; ++k)
+            acc[r] = fmaf(s_wt[ha + hl][k0 + k], po[(k * hn + hl) * D + d], acc[r]);
+        }
       }
     }
     __syncthreads();
@@ -1262,7 +1295,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
 #pragma unroll
   for (int r = 0; r < OUT; ++r) {
     const int i = tid + r * kMergeThreads;
-    if (i < 8 * D) orot[i] = acc[r];
+    if (whole ? i < 8 * D : i < hn * D) orot[(whole ? 0 : ha * D) + i] = acc[r];
   }
   cp_async_wait_all();
   __syncthreads();
@@ -1275,19 +1308,20 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
   constexpr int groups = kMergeThreads / D;       // 2 for D = 128
   constexpr int hpg = 8 / groups;                 // heads per group
   static_assert(D * groups == kMergeThreads && groups * hpg * D <= 8 * kSlotChunk * D, "merge");
-  const bool split = groups > 1 && nh <= hpg;     // block-uniform
+  const bool split = groups > 1 && hn <= hpg;     // block-uniform
   const int j = tid % D, grp = tid / D;
-  const int h0 = split ? 0 : grp * hpg;
+  // rows h0 + h beyond 7 (a CTA's last heads) read row 7 and are never stored
+  const int h0 = split ? ha : ha + grp * hpg;
   const int d0 = split ? grp * (D / groups) : 0, d1 = split ? d0 + D / groups : D;
   float o[hpg];
 #pragma unroll
   for (int h = 0; h < hpg; ++h) o[h] = 0.f;
-  if (h0 < nh) {
+  if (h0 < hb) {
 #pragma unroll 4
     for (int d = d0; d < d1; ++d) {
       const float r = rs[d * D + j];
 #pragma unroll
-      for (int h = 0; h < hpg; ++h) o[h] = fmaf(orot[(h0 + h) * D + d], r, o[h]);
+      for (int h = 0; h < hpg; ++h) o[h] = fmaf(orot[tmin(h0 + h, 7) * D + d], r, o[h]);
     }
   }
   if (split) {
@@ -1299,17 +1333,17 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
 #pragma unroll
         for (int h = 0; h < hpg; ++h) o[h] += po[(q * hpg + h) * D + j];
   }
-  if (split ? grp == 0 : h0 < nh) {
+  if (split ? grp == 0 : h0 < hb) {
     for (int64_t t = 0; t < W; ++t) {
       const float vx = load_elem(p.wv, p.w_dtype, b * p.wv_stride[0] + kvh * p.wv_stride[1] +
                                                       t * p.wv_stride[2] + j * p.wv_stride[3]);
 #pragma unroll
-      for (int h = 0; h < hpg; ++h) o[h] = fmaf(sc[(h0 + h) * W + t], vx, o[h]);
+      for (int h = 0; h < hpg; ++h) o[h] = fmaf(sc[tmin(h0 + h, 7) * W + t], vx, o[h]);
     }
 #pragma unroll
     for (int h = 0; h < hpg; ++h) {
       const int hh = h0 + h;
-      if (hh >= nh) break;
+      if (hh >= hb) break;
       const float L = s_L[hh];
       const int64_t hq = kvh * p.g + hc * 8 + hh;
       const int64_t off = b * p.out_stride[0] + hq * p.out_stride[1] + j * p.out_stride[3];
@@ -1341,7 +1375,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeParams p) {
       uint32_t* arrived = p.peer_flag[p.rank];
       uint32_t* done = arrived + 1;
       uint32_t* calls = arrived + 2;
-      const uint32_t nctas = gridDim.x * gridDim.y;
+      const uint32_t nctas = gridDim.x * gridDim.y * gridDim.z;
       uint32_t prev;
       asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(done)
                    : "memory");
@@ -1476,11 +1510,14 @@ size_t decode_workspace_bytes(const tq_geom* g, const tq_cache* c, const tq_deco
 
 using PrepFn = void (*)(PrepParams);
 
-static bool prep_for(int D, PrepFn* fn, size_t* smem, bool qjl) {
+static bool prep_for(int D, PrepFn* fn, size_t* smem, bool qjl, bool sep) {
   switch (D) {
-    case 32: *fn = prep_kernel<32>; *smem = PrepSmem<32>::bytes(qjl); return true;
-    case 64: *fn = prep_kernel<64>; *smem = PrepSmem<64>::bytes(qjl); return true;
-    case 128: *fn = prep_kernel<128>; *smem = PrepSmem<128>::bytes(qjl); return true;
+    case 32: *fn = sep ? prep_kernel<32, true> : prep_kernel<32, false>;
+      *smem = PrepSmem<32>::bytes(qjl); return true;
+    case 64: *fn = sep ? prep_kernel<64, true> : prep_kernel<64, false>;
+      *smem = PrepSmem<64>::bytes(qjl); return true;
+    case 128: *fn = sep ? prep_kernel<128, true> : prep_kernel<128, false>;
+      *smem = PrepSmem<128>::bytes(qjl); return true;
     default: return false;
   }
 }
@@ -1547,14 +1584,14 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
     }
     PrepFn pfn;
     size_t psmem;
-    if (!prep_for(pl.D, &pfn, &psmem, G->qjl != 0)) {
+    // the step's append gets its own CTA per stream where the grid stays
+    // within one wave (prep CTAs take most of an SM's shared memory)
+    pp.append_cta = step && pl.S * (pl.nch + 1) <= (int64_t)device_sm_count();
+    if (!prep_for(pl.D, &pfn, &psmem, G->qjl != 0, pp.append_cta != 0)) {
       set_error("tq_decode_attn: head_dim %d has no query-preparation kernel", pl.D);
       return TQ_ERR_INVALID;
     }
     if (set_smem_attr((const void*)pfn, psmem) != TQ_OK) return TQ_ERR_CUDA;
-    // the step's append gets its own CTA per stream where the grid stays
-    // within one wave (prep CTAs take most of an SM's shared memory)
-    pp.append_cta = step && pl.S * (pl.nch + 1) <= (int64_t)device_sm_count();
     const unsigned prep_y = (unsigned)(pl.nch + (pp.append_cta ? 1 : 0));
     if (launch_result(launch_pdl(pfn, dim3((unsigned)pl.S, prep_y), dim3(kPrepThreads), psmem, st, pp),
                       step ? "tq_decode_step/prep" : "tq_decode_attn/qprep") != TQ_OK)
@@ -1607,10 +1644,20 @@ int launch_decode(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   if (pl.S > 0 && (phases & TQ_PHASE_MERGE)) {
     const size_t msmem =
         (size_t)(pl.D * pl.D + 16 * pl.D + 8 * kSlotChunk * pl.D + 8 * (mp.W > 0 ? mp.W : 1)) * 4;
-    void (*mfn)(MergeParams) = pl.D == 32 ? merge_kernel<32> : pl.D == 64 ? merge_kernel<64>
-                                                                          : merge_kernel<128>;
+    // few streams: spread a chunk's heads over CTAs, up to one CTA per SM
+    const int hmax = tmin(8, pl.g);
+    const int64_t per = (int64_t)pl.S * pl.nch;
+    const int nz = (int)tmax<int64_t>(1, tmin<int64_t>(hmax, device_sm_count() / tmax<int64_t>(per, 1)));
+    const bool split = nz > 1;
+    mp.hpc = split ? (hmax + nz - 1) / nz : 8;
+    const unsigned mz = (unsigned)((hmax + mp.hpc - 1) / mp.hpc);
+    void (*mfn)(MergeParams) =
+        split ? (pl.D == 32 ? merge_kernel<32, true> : pl.D == 64 ? merge_kernel<64, true>
+                                                                  : merge_kernel<128, true>)
+              : (pl.D == 32 ? merge_kernel<32, false> : pl.D == 64 ? merge_kernel<64, false>
+                                                                   : merge_kernel<128, false>);
     if (set_smem_attr((const void*)mfn, msmem) != TQ_OK) return TQ_ERR_CUDA;
-    if (launch_result(launch_pdl(mfn, dim3((unsigned)pl.S, pl.nch), dim3(kMergeThreads), msmem, st, mp),
+    if (launch_result(launch_pdl(mfn, dim3((unsigned)pl.S, pl.nch, mz), dim3(kMergeThreads), msmem, st, mp),
                       "tq_decode_attn/merge") != TQ_OK)
       return TQ_ERR_CUDA;
   }
