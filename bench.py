@@ -874,6 +874,8 @@ def run_profile(args):
     --profile step   : one layer's fused decode step (tq_decode_step), 4 calls
     --profile append_qjl : K4+QJL/V2 prefill append, B4 x Hkv8 x 8192 tokens, 4 calls
     --profile prefill    : prefill attention, B2 x Hq32/Hkv8 x 2048 tokens, 3 calls
+    --profile step_long  : one Qwen2.5-14B long-context layer's decode step (B1, Hq40/Hkv8,
+                           32768 tokens, K3/V3), 4 calls
     """
     import torch
     from bhaskera_col_b200.inference import TurboQuantKVCache, ops
@@ -932,6 +934,23 @@ def run_profile(args):
             ops.append(st.tables, st._pages, x, x, 0)
         torch.cuda.synchronize()
         return
+    if args.profile == "step_long":
+        Tl, Bl, Hql = 32768, 1, 40
+        cache = TurboQuantKVCache(num_layers=1, batch_size=Bl, num_heads=HKV, head_dim=D,
+                                  key_bits=3, value_bits=3, residual_window=0,
+                                  protected_layers=0, device=dev, max_seq_len=Tl + 64)
+        for c0 in range(0, Tl, 8192):
+            k = torch.randn((Bl, HKV, 8192, D), device=dev, generator=gen).to(torch.bfloat16)
+            cache.append(k, k, 0)
+        q = torch.randn((Bl, Hql, 1, D), device=dev, generator=gen).to(torch.bfloat16)
+        k1 = torch.randn((Bl, HKV, 1, D), device=dev, generator=gen).to(torch.bfloat16)
+        st = cache._stores[0]
+        for _ in range(4):
+            ops.decode_step(st.tables, st._pages, k1, k1, Tl, q, workspace=st.workspace)
+        torch.cuda.synchronize()
+        if st.workspace.status() != 0:
+            raise RuntimeError("device status error")
+        return
     cache = TurboQuantKVCache(num_layers=1, batch_size=B_PER_GPU, num_heads=HKV, head_dim=D,
                               key_bits=KEY_BITS, value_bits=VALUE_BITS, residual_window=0,
                               protected_layers=0, device=dev, max_seq_len=T_CTX + 64, qjl=QJL)
@@ -963,7 +982,8 @@ def main():
                     help="leave out the 256-sequence head-sharded serving workload")
     ap.add_argument("--skip-long", action="store_true",
                     help="leave out the long-context cases (1 GPU)")
-    ap.add_argument("--profile", choices=["decode", "append", "append_qjl", "step", "prefill"],
+    ap.add_argument("--profile", choices=["decode", "append", "append_qjl", "step", "prefill",
+                                          "step_long"],
                     default=None,
                     help="run a small single-layer case for ncu and exit")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mixtral",
