@@ -480,7 +480,10 @@ def _e2e(rig, args, rank, world, local_rank):
     copy_stream = torch.cuda.Stream(dev)
     chunks = [(0, 1), (1, min(4, L)), (min(4, L), L)]
     ev_in = [torch.cuda.Event() for _ in chunks]
-    ev_out = [torch.cuda.Event() for _ in range(2)]
+    # the gathered outputs come back in runs of layers as they finish, on the
+    # copy stream, so the read-back overlaps the later layers' compute
+    out_runs = [(a, min(a + 4, L)) for a in range(0, L, 4)]
+    ev_out = [torch.cuda.Event() for _ in out_runs]
     cache, fused, shard = rig.cache, rig.fused, rig.shard
 
     def e2e_step():
@@ -501,15 +504,13 @@ def _e2e(rig, args, rank, world, local_rank):
                                    out=rig.o_loc[layer] if rig.world > 1 else rig.o_all[layer])
                 if rig.world > 1:
                     shard.gather(out, buf=rig.o_all[layer], layer=layer)
-            if layer == L - 2:
-                ev_out[0].record(main)
-        ev_out[1].record(main)
-        if reader:
-            with torch.cuda.stream(copy_stream):
-                copy_stream.wait_event(ev_out[0])
-                o_h[:L - 1].copy_(rig.o_all[:L - 1], non_blocking=True)
-                copy_stream.wait_event(ev_out[1])
-                o_h[L - 1:].copy_(rig.o_all[L - 1:], non_blocking=True)
+            for (a, b), ev in zip(out_runs, ev_out):
+                if layer == b - 1:
+                    ev.record(main)
+                    if reader:
+                        with torch.cuda.stream(copy_stream):
+                            copy_stream.wait_event(ev)
+                            o_h[a:b].copy_(rig.o_all[a:b], non_blocking=True)
         copy_stream.synchronize()
         main.synchronize()
 
