@@ -26,12 +26,16 @@ __global__ void quantize_rotated_kernel(const float* __restrict__ y, int64_t n,
 }
 
 // ---------------------------------------------------------------------------
-// Fused append (CUDA cores, fp32).  One CTA processes tiles of kVT vectors of
-// one tensor (blockIdx.y: 0 = K, 1 = V); R^T (and S^T for K with QJL) stay
-// resident in shared memory across tiles.
+// Fused append (CUDA cores, fp32).  One CTA processes tiles of kAppendVT
+// vectors of one tensor (blockIdx.y: 0 = K, 1 = V); R^T (and S^T for K with
+// QJL) stay resident in shared memory across tiles.  The tables take most of
+// an SM's shared memory, so one CTA of 16 warps per SM shares them (4 warps
+// and 16-vector tiles ran at 73 GB/s); the rotations read four coordinates
+// of a vector per broadcast load.
 // ---------------------------------------------------------------------------
-constexpr int kVT = 16;
-constexpr int kAppendThreads = 128;
+constexpr int kVT = 16;                  // dequantisation tile (tokens)
+constexpr int kAppendVT = 64;            // append tile (vectors)
+constexpr int kAppendThreads = 512;
 
 struct AppendParams {
   PageGeom g;
@@ -39,7 +43,7 @@ struct AppendParams {
   const float* bnd[2];
   const float* RT;      // R^T row-major
   const float* ST;      // S^T row-major (QJL)
-  int vt;               // vectors per tile (<= kVT)
+  int vt;               // vectors per tile (<= kAppendVT)
   uint8_t* pages;
   PageMap pm;
   uint32_t* status;     // TQ_DEV_BAD_BLOCK on a block-table entry outside the pool
@@ -55,7 +59,7 @@ __global__ void __launch_bounds__(kAppendThreads)
 append_kernel(AppendParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int GR = kAppendThreads / D;  // vector groups
-  constexpr int NV = (kVT + GR - 1) / GR; // vectors per thread
+  constexpr int NV = (kAppendVT + GR - 1) / GR; // vectors per thread
   const int which = blockIdx.y;           // 0: K, 1: V
   const PageGeom& g = p.g;
   const int bits = which == 0 ? g.kb : g.vb;
@@ -64,15 +68,15 @@ append_kernel(AppendParams p) {
 
   float* RT = reinterpret_cast<float*>(smem);                 // [D][D]
   float* ST = RT + D * D;                                     // [D][D] (qjl)
-  float* u = ST + (qjl ? D * D : 0);                          // [kVT][D]
-  float* yv = u + kVT * D;                                    // [kVT][D]
-  float* cb = yv + kVT * D;                                   // [256]
+  float* u = ST + (qjl ? D * D : 0);                          // [kAppendVT][D]
+  float* yv = u + kAppendVT * D;                              // [kAppendVT][D]
+  float* cb = yv + kAppendVT * D;                             // [256]
   float* bb = cb + 256;                                       // [256]
-  float* nrm = bb + 256;                                      // [kVT]
-  float* gam = nrm + kVT;                                     // [kVT]
-  uint8_t* code = reinterpret_cast<uint8_t*>(gam + kVT);      // [kVT][D]
-  uint8_t* qb = code + kVT * D;                               // [kVT][D]
-  int16_t* ord = reinterpret_cast<int16_t*>(qb + kVT * D);    // [D] pos -> coord
+  float* nrm = bb + 256;                                      // [kAppendVT]
+  float* gam = nrm + kAppendVT;                               // [kAppendVT]
+  uint8_t* code = reinterpret_cast<uint8_t*>(gam + kAppendVT);      // [kAppendVT][D]
+  uint8_t* qb = code + kAppendVT * D;                         // [kAppendVT][D]
+  int16_t* ord = reinterpret_cast<int16_t*>(qb + kAppendVT * D);    // [D] pos -> coord
   int16_t* qinv = ord + D;                                    // [D] bit -> coord
 
   const int tid = threadIdx.x;
@@ -114,7 +118,7 @@ append_kernel(AppendParams p) {
       const int j = tid % D, grp = tid / D;
       const int mine = (grp < GR && nv > grp) ? (nv - grp + GR - 1) / GR : 0;
       float acc[NV];
-      rot_multi<D, NV>(u + grp * D, GR * D, mine, RT, j, acc);
+      rot_multi4<D, NV>(u + grp * D, GR * D, mine, RT, j, acc);
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         if (k < mine) {
@@ -134,7 +138,7 @@ append_kernel(AppendParams p) {
         const int j = tid % D, grp = tid / D;
         const int mine = (grp < GR && nv > grp) ? (nv - grp + GR - 1) / GR : 0;
         float acc[NV];
-        rot_multi<D, NV>(u + grp * D, GR * D, mine, ST, j, acc);
+        rot_multi4<D, NV>(u + grp * D, GR * D, mine, ST, j, acc);
 #pragma unroll
         for (int k = 0; k < NV; ++k)
           if (k < mine) qb[(grp + k * GR) * D + j] = acc[k] >= 0.f ? 1 : 0;
@@ -193,8 +197,8 @@ append_kernel(AppendParams p) {
 }
 
 size_t append_smem_bytes(int D, bool qjl) {
-  size_t f = (size_t)D * D * (qjl ? 2 : 1) + 2 * kVT * D + 512 + 2 * kVT;
-  return f * 4 + 2 * kVT * D + 2 * D * sizeof(int16_t) + 16;
+  size_t f = (size_t)D * D * (qjl ? 2 : 1) + 2 * kAppendVT * D + 512 + 2 * kAppendVT;
+  return f * 4 + 2 * kAppendVT * D + 2 * D * sizeof(int16_t) + 16;
 }
 
 // ---------------------------------------------------------------------------
@@ -300,7 +304,7 @@ int launch_append(const tq_geom* G, const tq_tables* t, const tq_cache* c,
   // small appends (decode steps): few vectors per CTA so the grid fills the
   // GPU; large appends: full tiles, persistent CTAs
   const int64_t want = (nvec + (int64_t)sms * occ - 1) / ((int64_t)sms * occ);
-  p.vt = (int)tmax<int64_t>(1, tmin<int64_t>(kVT, 2 * want));
+  p.vt = (int)tmax<int64_t>(1, tmin<int64_t>(kAppendVT, 2 * want));
   const int64_t tiles = (nvec + p.vt - 1) / p.vt;
   dim3 grid((unsigned)tmin<int64_t>(tiles, (int64_t)sms * occ), 2);
   fn<<<grid, kAppendThreads, smem, st>>>(p);

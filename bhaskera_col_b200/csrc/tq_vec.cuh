@@ -52,6 +52,32 @@ __device__ __forceinline__ void rot_multi(const float* x, int ldx, int nv, const
   }
 }
 
+// rot_multi with four coordinates of each vector per broadcast load (x rows
+// 16-byte aligned, ldx a multiple of 4): the same per-vector summation order
+// (i ascending, one fmaf per term), so the results are bit-identical.
+template <int D, int NV>
+__device__ __forceinline__ void rot_multi4(const float* x, int ldx, int nv, const float* T, int j,
+                                           float (&acc)[NV]) {
+  static_assert(D % 4 == 0, "head_dim");
+#pragma unroll
+  for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+#pragma unroll 2
+  for (int i = 0; i < D; i += 4) {
+    const float t0 = T[i * D + j], t1 = T[(i + 1) * D + j];
+    const float t2 = T[(i + 2) * D + j], t3 = T[(i + 3) * D + j];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      if (v < nv) {
+        const float4 xv = *reinterpret_cast<const float4*>(x + v * ldx + i);
+        acc[v] = fmaf(xv.x, t0, acc[v]);
+        acc[v] = fmaf(xv.y, t1, acc[v]);
+        acc[v] = fmaf(xv.z, t2, acc[v]);
+        acc[v] = fmaf(xv.w, t3, acc[v]);
+      }
+    }
+  }
+}
+
 // acc[v] = sum_i x[row[v] * D + i] T[i][j] for the first N vectors, i
 // ascending with one fmaf per term (rot_coord's order, so each result is
 // bit-identical to it).  N is a compile-time count and every load is
