@@ -596,7 +596,8 @@ def run_ours(args, rank, world, local_rank):
                          "unit": "GB/s", "frac": main["achieved_gbs"] / hbm_peak,
                          "traffic": _traffic_per_launch() if args.workload == "mixtral" else None,
                          "kernel": f"decode_kernel<{W.d},{W.kb},{W.vb},"
-                                   f"{'qjl' if W.qjl else 'mse'}>",
+                                   f"{'qjl' if W.qjl else 'mse'}"
+                                   f"{',self' if (W.d, W.kb) == (128, 4) and W.vb in (2, 4) else ''}>",
                          "algorithmic_bytes_per_launch": alg,
                          "avg_launch_ms": dec_avg, "peak_kind": peak_kind},
             "cpu_baseline": cpu_line,
