@@ -434,6 +434,11 @@ def measure_decode(W: Workload, args, rank, world, local_rank, *, e2e=True, chec
     torch.cuda.synchronize()
     torch.cuda._sleep(int(2e8))          # let the host queue the whole pass first
     for k in range(args.steps):
+        # ~5 ms of device sleep per step keeps the host's launches ahead of the
+        # GPU (with an all-gather per layer the host needs about as long per
+        # layer as the GPU); otherwise an event can fire before the host has
+        # queued the decode launch it brackets
+        torch.cuda._sleep(int(1e7))
         rig.step(phased_events=evs[k])
     torch.cuda.synchronize()
     dec_ms = [e0.elapsed_time(e1) for row in evs for (e0, e1) in row]
