@@ -16,14 +16,18 @@
 // Kernels per call:
 //   prep_kernel    q_rot, S q_rot -> fp16 fragments (scale * log2e folded in);
 //                  in a decode step also the append of the new token
-//   decode_kernel  persistent; each CTA owns a contiguous range of the
-//                  flattened (stream, page) space.  A producer warp streams
-//                  64-token pages into shared memory with bulk async copies
-//                  (no multicast) through full/empty mbarriers; four consumer
-//                  warps take 16 tokens of each page, dequantise codes
-//                  straight into mma.sync fragments through lane-replicated
-//                  pair lookup tables, and run an online softmax.  One partial
-//                  (m, l, O_rot) per (stream, head, CTA) touched.
+//   decode_kernel  persistent, one CTA per SM; each of its page groups (a
+//                  work unit) owns a contiguous range of the flattened
+//                  (stream, page) space.  A producer warp streams 64-token
+//                  pages into shared memory with bulk async copies (no
+//                  multicast) through full/empty mbarriers; the group's four
+//                  consumer warps take pages in pairs, 32 tokens per warp,
+//                  dequantise codes straight into mma.sync fragments through
+//                  lane-replicated pair lookup tables, and run an online
+//                  softmax.  The self-fed variant (uniform batch on contiguous
+//                  pages) has no producer warp: consumer threads issue the
+//                  copies themselves.  One partial (m, l, O_rot) per
+//                  (stream, head, work unit) touched.
 //   merge_kernel   combines the partials of each (stream, head), attends the
 //                  full-precision window, un-rotates, writes the output.
 #include "tq_common.cuh"
