@@ -1,4 +1,4 @@
-"""KV-head parallel decode, host logic, on CPU with gloo ranks (world size 2).
+"""KV-head parallel decode, host logic, on CPU with gloo ranks (world size 2 and 4).
 
 The per-rank attention is the oracle's (float64 SDPA over the rank's own
 heads), standing in for the CUDA decode, so these tests check what the
@@ -115,15 +115,17 @@ def test_single_rank_gather_is_identity():
     assert s.gather(x) is x
 
 
-def test_two_rank_decode_equals_single_process(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_multi_rank_decode_equals_single_process(tmp_path, world):
+    """world 4 leaves one KV head per rank, the 8-GPU split of 8 KV heads."""
     port = _free_port()
-    mp.start_processes(_worker_decode, args=(2, port, str(tmp_path)), nprocs=2, join=True,
-                       start_method="spawn")
+    mp.start_processes(_worker_decode, args=(world, port, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
     hk, hv, q, k1, v1 = _data()
     full = _OracleCache(hk, hv)
     want = torch.stack([full.decode(torch.from_numpy(q[l]), torch.from_numpy(k1[l]),
                                     torch.from_numpy(v1[l]), l) for l in range(LAYERS)])
-    for r in range(2):
+    for r in range(world):
         got = torch.load(os.path.join(tmp_path, f"out{r}.pt"))
         assert got.shape == (LAYERS, B, HQ, 1, D)
         assert torch.equal(got, want), r
